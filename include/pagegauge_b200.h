@@ -1,0 +1,205 @@
+/*
+ * PageGauge-B200: C ABI of the INT8 page-affine paged decode path.
+ *
+ * Every entry point takes raw device pointers, element strides and sizes, and
+ * a cudaStream_t (passed as void*); it validates what it can, launches on the
+ * given stream, never allocates device memory, and returns PG_OK or an error
+ * code.  pg_last_error() returns the message of the last failure on the
+ * calling thread; the messages of the checks that mirror the reference's
+ * host validation are kept verbatim so callers can match on them.
+ *
+ * Fixed geometry: head_dim 128, 16-token pages, NHD page layout
+ * [pages, 16, Hkv, 128]; GQA group Hq/Hkv in 1..8.
+ *
+ * Reference interfaces replaced (paths inside ahmed123hds/PageGauge):
+ *   pg_rope_append_fp16          <- rope_append_fp16[_dynamic]
+ *                                   tests/page_gauge_append_extension.cu:644-745
+ *   pg_rope_append_page_gauge    <- rope_append_page_gauge[_dynamic]
+ *                                   tests/page_gauge_append_extension.cu:747-948
+ *   pg_exact_tail_merge_center   <- exact_tail_merge_center
+ *                                   tests/page_gauge_append_extension.cu:950-1028
+ *   pg_decode_plan               <- BatchDecodeWithPagedKVCacheWrapper.plan as
+ *                                   called by plan()
+ *                                   scripts/benchmark_flashinfer_page_affine_int8.py:363-389
+ *   pg_decode_run                <- wrapper.run(q, (k_codes, v_codes), k_scale,
+ *                                   v_scale, sm_scale, out=, lse=)
+ *                                   scripts/benchmark_flashinfer_page_affine_int8.py:581-590
+ *                                   (INT8 segment), the FP16 tail run :591-597,
+ *                                   and the single-launch run_decode ABI
+ *                                   scripts/page_gauge_heterogeneous_fa2.py:330-379
+ *   pg_merge_state_in_place      <- flashinfer.merge_state_in_place
+ *                                   scripts/benchmark_page_gauge_transformer.py:2300-2305
+ *   pg_quantize_pages            <- quantize_completed_kv_pages
+ *                                   scripts/benchmark_page_gauge_overheads.py:208-239
+ *                                   and the codes/scales of quantize_page_gauge
+ *                                   scripts/benchmark_flashinfer_page_affine_int8.py:256-278
+ */
+#ifndef PAGEGAUGE_B200_H_
+#define PAGEGAUGE_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  PG_OK = 0,
+  PG_ERR_INVALID = 1,   /* argument validation failed (message set) */
+  PG_ERR_CUDA = 2,      /* a CUDA runtime/driver call failed */
+  PG_ERR_CAPACITY = 3   /* a caller-provided buffer is too small */
+};
+
+/* Device-side guard codes reported by pg_read_device_error. */
+enum {
+  PG_DEV_OK = 0,
+  PG_DEV_WAIT_TIMEOUT = 1, /* a bounded mbarrier wait gave up */
+  PG_DEV_BAD_POSITION = 2, /* device position outside cache / RoPE table */
+  PG_DEV_BAD_PAGE_ID = 3   /* page table entry outside the cache */
+};
+
+/* Message of the last error on this thread ("" if none). */
+const char* pg_last_error(void);
+
+/* ABI version (major*100 + minor). */
+int32_t pg_abi_version(void);
+
+/* Read and clear the device guard word of the current device. */
+int32_t pg_read_device_error(int32_t* code_out);
+
+/* ---------------------------------------------------------------------- */
+/* Fused RoPE + FP16 append (the comparator path).                         */
+/* query [B,Hq,128], key/value [B,Hkv,128] fp16 with contiguous heads;      */
+/* cosine/sine: one [128] row (device_position == NULL, position used) or   */
+/* a [rope_rows,128] table indexed by *device_position.                     */
+/* key_pages/value_pages fp16 [num_pages,16,Hkv,128], request-major.        */
+int32_t pg_rope_append_fp16(const void* query, const void* key,
+                            const void* value, const void* cosine,
+                            const void* sine, void* rotated_query,
+                            void* key_pages, void* value_pages,
+                            int64_t query_batch_stride,
+                            int64_t key_batch_stride,
+                            int64_t value_batch_stride, int32_t batch,
+                            int32_t query_heads, int32_t kv_heads,
+                            int64_t num_pages, int64_t position,
+                            const int32_t* device_position,
+                            int64_t rope_row_stride, int64_t rope_rows,
+                            void* stream);
+
+/* Fused RoPE + centred append into the exact FP16 ring + INT8 finalisation
+ * of the page closed by this token (codes [code_pages,16,Hkv,128] int8,
+ * scales [code_pages,Hkv] fp16).  centers: [B,Hkv,128] (center_batch_stride
+ * = Hkv*128) or one [Hkv,128] shared centre for batch one (stride 0).     */
+int32_t pg_rope_append_page_gauge(
+    const void* query, const void* key, const void* value,
+    const void* cosine, const void* sine, const void* key_center,
+    const void* value_center, void* rotated_query, void* exact_key_pages,
+    void* exact_value_pages, void* key_codes, void* value_codes,
+    void* key_scales, void* value_scales, int64_t query_batch_stride,
+    int64_t key_batch_stride, int64_t value_batch_stride,
+    int64_t center_batch_stride, int32_t batch, int32_t query_heads,
+    int32_t kv_heads, int64_t exact_pages, int64_t code_pages,
+    int64_t exact_sink_pages, int64_t position,
+    const int32_t* device_position, int64_t rope_row_stride,
+    int64_t rope_rows, void* stream);
+
+/* Exact FP16 tail attention merged into (old_output, old_lse) in place,
+ * plus the value centre.  exact_page_indices [B*n] int32,
+ * exact_last_page_len [B] int32 (device), old_lse base 2 [B,Hq].          */
+int32_t pg_exact_tail_merge_center(
+    const void* query, const void* exact_key_pages,
+    const void* exact_value_pages, int64_t exact_pages_total,
+    const int32_t* exact_page_indices, int64_t num_indices,
+    const int32_t* exact_last_page_len, void* old_output, float* old_lse,
+    const void* value_center, int64_t center_batch_stride, int32_t batch,
+    int32_t query_heads, int32_t kv_heads, double sm_scale, void* stream);
+
+/* ---------------------------------------------------------------------- */
+/* Split-KV paged decode.  Segment 0: INT8 codes + per-(page, head) FP16     */
+/* scales.  Segment 1: FP16 pages (exact tail ring or a plain FP16 cache).  */
+typedef struct pg_decode_item {
+  int32_t request;
+  int32_t head_seg;  /* kv_head | (segment << 16) */
+  int32_t idx_begin; /* absolute offset of the first page id */
+  int32_t count;     /* pages; bit 31: holds the request's last page */
+} pg_decode_item;
+
+typedef struct pg_segment {
+  const void* k_cache; /* NULL: segment absent */
+  const void* v_cache;
+  int64_t num_pages;             /* pages allocated in k_cache/v_cache */
+  const int32_t* indices;        /* device page ids */
+  const int32_t* last_page_len;  /* device [B] */
+  const void* k_scale;           /* fp16 [num_pages, Hkv], segment 0 */
+  const void* v_scale;
+} pg_segment;
+
+typedef struct pg_plan_info {
+  int64_t num_items;
+  int32_t max_items_per_head;
+  int32_t single_item_per_head; /* 1: run may use the final epilogue */
+  int32_t split_pages[2];       /* pages per work item chosen per segment */
+  int32_t warps_per_cta;
+} pg_plan_info;
+
+/* Host-only planner.  indptr_s (host, [B+1]) gives each request's page-id
+ * range in segment s (NULL: absent).  split_pages_s = pages per work item
+ * (0: automatic, sized for one wave on num_sms SMs).  Writes at most
+ * items_capacity items and item_off[B*Hkv+1]; returns PG_CAPACITY if the
+ * list does not fit.                                                       */
+int32_t pg_decode_plan(int32_t batch, int32_t kv_heads,
+                       const int32_t* indptr0, const int32_t* indptr1,
+                       int32_t split_pages0, int32_t split_pages1,
+                       int32_t num_sms, int32_t warps_per_cta,
+                       pg_decode_item* items, int64_t items_capacity,
+                       int32_t* item_off, pg_plan_info* info);
+
+typedef struct pg_decode_args {
+  const void* q; /* fp16 [B, Hq, 128], last dim contiguous */
+  int64_t q_stride_b, q_stride_h;
+  int32_t batch, kv_heads, group;
+  float sm_scale;
+  pg_segment seg[2];
+  const pg_decode_item* items; /* device, from pg_decode_plan */
+  const int32_t* item_off;     /* device [B*Hkv+1] */
+  int32_t num_items;
+  int32_t warps_per_cta;
+  float* part_o;   /* device workspace [num_items*group*128] */
+  float* part_lse; /* device workspace [num_items*group] */
+  int32_t final_mode; /* 1: one item per (request, head): no merge launch */
+  void* out;          /* fp16 [B, Hq, 128] */
+  int64_t out_stride_b, out_stride_h;
+  float* lse_out; /* base-2 [B, Hq] or NULL */
+  const void* extra_o; /* optional state merged in (may alias out) */
+  int64_t extra_stride_b, extra_stride_h;
+  const float* extra_lse;
+  const void* value_center; /* fp16 [B,Hkv,128] or NULL */
+  int64_t vc_stride_b;
+  int32_t stage_mask; /* 0 or 3: split + merge; 1: split kernel only;
+                         2: merge kernel only (stages on separate calls) */
+} pg_decode_args;
+
+int32_t pg_decode_run(const pg_decode_args* args, void* stream);
+
+/* (v_a, s_a) <- merge((v_a, s_a), (v_b, s_b)); rows of 128 fp16, lse base 2. */
+int32_t pg_merge_state_in_place(void* v_a, float* s_a, const void* v_b,
+                                const float* s_b, int64_t rows,
+                                int64_t va_row_stride, int64_t vb_row_stride,
+                                void* stream);
+
+/* Bulk completed-page quantisation: fp32 centring (no FP16 rounding),
+ * scale = f16(max(absmax/127, 2^-20)), rounding 0 = half away from zero
+ * (prefill quantiser), 1 = half to even (torch.round).                   */
+int32_t pg_quantize_pages(const void* key, const void* value,
+                          const void* key_center, const void* value_center,
+                          int64_t pages_per_center, void* key_codes,
+                          void* value_codes, void* key_scales,
+                          void* value_scales, int64_t num_pages,
+                          int32_t kv_heads, int32_t rounding, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PAGEGAUGE_B200_H_ */

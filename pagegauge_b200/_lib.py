@@ -1,0 +1,117 @@
+"""ctypes binding of libpagegauge_b200.so (the C ABI in include/pagegauge_b200.h).
+
+The shared library is built in-tree (``python -m pagegauge_b200.build``).
+There is no fallback: if the library is missing, every operator raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+LIB_NAME = "libpagegauge_b200.so"
+LIB_PATH = Path(__file__).resolve().parent / LIB_NAME
+
+c_i32 = ctypes.c_int32
+c_i64 = ctypes.c_int64
+c_vp = ctypes.c_void_p
+c_f32p = ctypes.POINTER(ctypes.c_float)
+c_i32p = ctypes.POINTER(ctypes.c_int32)
+
+
+class PgDecodeItem(ctypes.Structure):
+    _fields_ = [("request", c_i32), ("head_seg", c_i32), ("idx_begin", c_i32), ("count", c_i32)]
+
+
+class PgSegment(ctypes.Structure):
+    _fields_ = [
+        ("k_cache", c_vp), ("v_cache", c_vp), ("num_pages", c_i64),
+        ("indices", c_vp), ("last_page_len", c_vp), ("k_scale", c_vp), ("v_scale", c_vp),
+    ]
+
+
+class PgPlanInfo(ctypes.Structure):
+    _fields_ = [
+        ("num_items", c_i64), ("max_items_per_head", c_i32), ("single_item_per_head", c_i32),
+        ("split_pages", c_i32 * 2), ("warps_per_cta", c_i32),
+    ]
+
+
+class PgDecodeArgs(ctypes.Structure):
+    _fields_ = [
+        ("q", c_vp), ("q_stride_b", c_i64), ("q_stride_h", c_i64),
+        ("batch", c_i32), ("kv_heads", c_i32), ("group", c_i32), ("sm_scale", ctypes.c_float),
+        ("seg", PgSegment * 2),
+        ("items", c_vp), ("item_off", c_vp), ("num_items", c_i32), ("warps_per_cta", c_i32),
+        ("part_o", c_vp), ("part_lse", c_vp), ("final_mode", c_i32),
+        ("out", c_vp), ("out_stride_b", c_i64), ("out_stride_h", c_i64), ("lse_out", c_vp),
+        ("extra_o", c_vp), ("extra_stride_b", c_i64), ("extra_stride_h", c_i64), ("extra_lse", c_vp),
+        ("value_center", c_vp), ("vc_stride_b", c_i64), ("stage_mask", c_i32),
+    ]
+
+
+# name -> (restype, argtypes); every entry point returns int32 status.
+_SIGNATURES = {
+    "pg_last_error": (ctypes.c_char_p, []),
+    "pg_abi_version": (c_i32, []),
+    "pg_read_device_error": (c_i32, [c_i32p]),
+    "pg_rope_append_fp16": (c_i32, [c_vp] * 8 + [c_i64] * 3 + [c_i32] * 3 + [c_i64, c_i64, c_vp, c_i64, c_i64, c_vp]),
+    "pg_rope_append_page_gauge": (
+        c_i32,
+        [c_vp] * 14 + [c_i64] * 4 + [c_i32] * 3 + [c_i64] * 4 + [c_vp, c_i64, c_i64, c_vp],
+    ),
+    "pg_exact_tail_merge_center": (
+        c_i32,
+        [c_vp, c_vp, c_vp, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, c_i64, c_i32, c_i32, c_i32,
+         ctypes.c_double, c_vp],
+    ),
+    "pg_decode_plan": (
+        c_i32,
+        [c_i32, c_i32, c_vp, c_vp, c_i32, c_i32, c_i32, c_i32, c_vp, c_i64, c_vp,
+         ctypes.POINTER(PgPlanInfo)],
+    ),
+    "pg_decode_run": (c_i32, [ctypes.POINTER(PgDecodeArgs), c_vp]),
+    "pg_merge_state_in_place": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp]),
+    "pg_quantize_pages": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, c_i64, c_i32, c_i32, c_vp]),
+}
+
+EXPORTED = tuple(_SIGNATURES)
+
+_lib = None
+
+
+def library_path() -> Path:
+    override = os.environ.get("PAGEGAUGE_B200_LIB")
+    return Path(override) if override else LIB_PATH
+
+
+def load() -> ctypes.CDLL:
+    """Load the CUDA library once; raise if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    path = library_path()
+    if not path.is_file():
+        raise RuntimeError(
+            f"PageGauge CUDA library not found at {path}; build it with "
+            "`python -m pagegauge_b200.build` (no CPU fallback exists)"
+        )
+    lib = ctypes.CDLL(str(path))
+    for name, (restype, argtypes) in _SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = restype
+        fn.argtypes = argtypes
+    _lib = lib
+    return lib
+
+
+def check(rc: int) -> None:
+    """Translate a non-zero status into RuntimeError with the library message."""
+    if rc != 0:
+        msg = load().pg_last_error().decode("utf-8", "replace")
+        raise RuntimeError(msg or f"pagegauge_b200 call failed with status {rc}")
+
+
+def call(name: str, *args) -> None:
+    check(getattr(load(), name)(*args))

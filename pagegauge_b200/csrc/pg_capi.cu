@@ -1,0 +1,643 @@
+// extern "C" entry points of libpagegauge_b200.so: argument validation,
+// tensor-map encoding, work planning and kernel launches.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/pagegauge_b200.h"
+#include "pg_append.cuh"
+#include "pg_decode.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int32_t fail(int32_t code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int32_t cuda_check(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return PG_OK;
+  return fail(PG_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define PG_REQUIRE(cond, ...)                         \
+  do {                                                \
+    if (!(cond)) return fail(PG_ERR_INVALID, __VA_ARGS__); \
+  } while (0)
+
+// --------------------------------------------------------- device guard
+__device__ int g_device_error;
+
+int* device_error_ptr() {
+  static std::mutex mu;
+  static int* ptrs[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (ptrs[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return nullptr;
+    ptrs[dev] = static_cast<int*>(p);
+  }
+  return ptrs[dev];
+}
+
+// ---------------------------------------------------------- tensor maps
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
+                                   void*, const cuuint64_t*, const cuuint64_t*,
+                                   const cuuint32_t*, const cuuint32_t*,
+                                   CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion,
+                                   CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault,
+                                &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+  });
+  return fn;
+}
+
+// Page cache [num_pages, 16, Hkv, 128] viewed as rows of 128 bytes:
+//   INT8: dims {128 B, Hkv, pages*16}, box {128, 1, 16}
+//   FP16: dims {64 halves, 2*Hkv, pages*16}, box {64, 1, 16}
+// Both use the 128-byte swizzle so a 16-token tile lands conflict-free.
+int32_t make_page_map(CUtensorMap* map, const void* base, int64_t num_pages,
+                      int32_t hkv, bool fp16) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr)
+    return fail(PG_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  PG_REQUIRE(reinterpret_cast<uintptr_t>(base) % 16 == 0,
+             "page cache base must be 16-byte aligned");
+  PG_REQUIRE(num_pages > 0 && num_pages * pg::kPage < (int64_t(1) << 31),
+             "page cache row count out of range");
+  cuuint64_t dims[3];
+  cuuint64_t strides[2];
+  cuuint32_t box[3];
+  const cuuint32_t estr[3] = {1, 1, 1};
+  if (!fp16) {
+    dims[0] = 128;
+    dims[1] = static_cast<cuuint64_t>(hkv);
+    dims[2] = static_cast<cuuint64_t>(num_pages) * pg::kPage;
+    strides[0] = 128;
+    strides[1] = static_cast<cuuint64_t>(hkv) * 128;
+    box[0] = 128;
+  } else {
+    dims[0] = 64;
+    dims[1] = static_cast<cuuint64_t>(hkv) * 2;
+    dims[2] = static_cast<cuuint64_t>(num_pages) * pg::kPage;
+    strides[0] = 128;
+    strides[1] = static_cast<cuuint64_t>(hkv) * 256;
+    box[0] = 64;
+  }
+  box[1] = 1;
+  box[2] = pg::kPage;
+  CUresult r = fn(map, fp16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8,
+                  3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(PG_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  return PG_OK;
+}
+
+bool aligned(const void* p, size_t a) {
+  return reinterpret_cast<uintptr_t>(p) % a == 0;
+}
+
+int32_t ensure_decode_smem() {
+  static std::mutex mu;
+  static bool done[64] = {false};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return fail(PG_ERR_CUDA, "cudaGetDevice failed");
+  std::lock_guard<std::mutex> lock(mu);
+  if (!done[dev]) {
+    int32_t rc = cuda_check(
+        cudaFuncSetAttribute(pg::pg_decode_split_kernel,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             pg::decode_smem_bytes(pg::kMaxWarps)),
+        "cudaFuncSetAttribute(decode smem)");
+    if (rc != PG_OK) return rc;
+    done[dev] = true;
+  }
+  return PG_OK;
+}
+
+int32_t launch_decode(const pg::DecodeParams& p, const CUtensorMap& k8,
+                      const CUtensorMap& v8, const CUtensorMap& k16,
+                      const CUtensorMap& v16, int num_ctas, int warps,
+                      cudaStream_t stream) {
+  int32_t rc = ensure_decode_smem();
+  if (rc != PG_OK) return rc;
+  pg::pg_decode_split_kernel<<<num_ctas, warps * 32, pg::decode_smem_bytes(warps),
+                               stream>>>(k8, v8, k16, v16, p);
+  return cuda_check(cudaGetLastError(), "decode kernel launch");
+}
+
+// Resident CTAs of the decode kernel per SM at `warps` warps per CTA
+// (shared-memory bound: 228 KB per SM, 1 KB reserved per CTA; at most
+// 2048 threads and 64 K registers at 128 registers per thread).
+int pg_ctas_per_sm(int warps) {
+  const int by_smem = (228 * 1024) / (pg::decode_smem_bytes(warps) + 1024);
+  const int by_threads = 2048 / (warps * 32);
+  const int by_regs = 65536 / (warps * 32 * 128);
+  return std::max(1, std::min(by_smem, std::min(by_threads, by_regs)));
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* pg_last_error(void) { return g_last_error.c_str(); }
+
+int32_t pg_abi_version(void) { return 100; }
+
+int32_t pg_read_device_error(int32_t* code_out) {
+  int* p = device_error_ptr();
+  if (p == nullptr) return fail(PG_ERR_CUDA, "device error word unavailable");
+  int v = 0;
+  int32_t rc = cuda_check(cudaMemcpy(&v, p, sizeof(int), cudaMemcpyDeviceToHost),
+                          "read device error");
+  if (rc != PG_OK) return rc;
+  int zero = 0;
+  rc = cuda_check(cudaMemcpy(p, &zero, sizeof(int), cudaMemcpyHostToDevice),
+                  "clear device error");
+  if (code_out) *code_out = v;
+  return rc;
+}
+
+// ------------------------------------------------------------------ append
+int32_t pg_rope_append_fp16(const void* query, const void* key,
+                            const void* value, const void* cosine,
+                            const void* sine, void* rotated_query,
+                            void* key_pages, void* value_pages,
+                            int64_t query_batch_stride,
+                            int64_t key_batch_stride,
+                            int64_t value_batch_stride, int32_t batch,
+                            int32_t query_heads, int32_t kv_heads,
+                            int64_t num_pages, int64_t position,
+                            const int32_t* device_position,
+                            int64_t rope_row_stride, int64_t rope_rows,
+                            void* stream) {
+  PG_REQUIRE(batch > 0, "Q/K/V batch sizes must match and be positive");
+  PG_REQUIRE(query_heads > 0 && kv_heads > 0, "head counts must be positive");
+  if (device_position == nullptr) {
+    PG_REQUIRE(position >= 0, "position must be non-negative");
+    PG_REQUIRE(position / pg::kPage < num_pages,
+               "position exceeds the allocated FP16 cache");
+  } else {
+    PG_REQUIRE(rope_rows > 0, "dynamic RoPE tables must be matching [positions,128] tensors");
+  }
+  PG_REQUIRE(num_pages % batch == 0, "FP16 cache pages must divide evenly across requests");
+  const int64_t ppr = num_pages / batch;
+  if (device_position == nullptr)
+    PG_REQUIRE(position / pg::kPage < ppr,
+               "position exceeds the per-request FP16 cache capacity");
+  PG_REQUIRE(aligned(query, 4) && aligned(key, 4) && aligned(value, 4) &&
+                 aligned(cosine, 4) && aligned(sine, 4) && aligned(key_pages, 4) &&
+                 aligned(value_pages, 4) && aligned(rotated_query, 4),
+             "tensors must be 4-byte aligned");
+  PG_REQUIRE(query_batch_stride % 2 == 0 && key_batch_stride % 2 == 0 &&
+                 value_batch_stride % 2 == 0 && rope_row_stride % 2 == 0,
+             "batch strides must be even");
+  pg::AppendParams p{};
+  p.q = static_cast<const __half*>(query);
+  p.k = static_cast<const __half*>(key);
+  p.v = static_cast<const __half*>(value);
+  p.q_stride_b = query_batch_stride;
+  p.k_stride_b = key_batch_stride;
+  p.v_stride_b = value_batch_stride;
+  p.cos = static_cast<const __half*>(cosine);
+  p.sin = static_cast<const __half*>(sine);
+  p.device_position = device_position;
+  p.host_position = position;
+  p.rope_row_stride = rope_row_stride;
+  p.rope_rows = rope_rows;
+  p.rotated_q = static_cast<__half*>(rotated_query);
+  p.key_pages = static_cast<__half*>(key_pages);
+  p.value_pages = static_cast<__half*>(value_pages);
+  p.batch = batch;
+  p.hq = query_heads;
+  p.hkv = kv_heads;
+  p.exact_pages_per_request = ppr;
+  p.error_flag = device_error_ptr();
+  pg::pg_rope_append_fp16_kernel<<<batch * kv_heads, 64, 0,
+                                   static_cast<cudaStream_t>(stream)>>>(p);
+  return cuda_check(cudaGetLastError(), "rope_append_fp16 launch");
+}
+
+int32_t pg_rope_append_page_gauge(
+    const void* query, const void* key, const void* value,
+    const void* cosine, const void* sine, const void* key_center,
+    const void* value_center, void* rotated_query, void* exact_key_pages,
+    void* exact_value_pages, void* key_codes, void* value_codes,
+    void* key_scales, void* value_scales, int64_t query_batch_stride,
+    int64_t key_batch_stride, int64_t value_batch_stride,
+    int64_t center_batch_stride, int32_t batch, int32_t query_heads,
+    int32_t kv_heads, int64_t exact_pages, int64_t code_pages,
+    int64_t exact_sink_pages, int64_t position,
+    const int32_t* device_position, int64_t rope_row_stride,
+    int64_t rope_rows, void* stream) {
+  PG_REQUIRE(batch > 0, "Q/K/V batch sizes must match and be positive");
+  PG_REQUIRE(query_heads > 0 && kv_heads > 0, "head counts must be positive");
+  if (device_position == nullptr) {
+    PG_REQUIRE(position >= 0, "position must be non-negative");
+  } else {
+    PG_REQUIRE(rope_rows > 0, "dynamic RoPE tables must be matching [positions,128] tensors");
+  }
+  PG_REQUIRE(exact_pages > 0 && exact_pages % batch == 0 && code_pages % batch == 0,
+             "PageGauge pages must be positive and divide evenly across requests");
+  const int64_t exact_ppr = exact_pages / batch;
+  PG_REQUIRE(exact_sink_pages >= 0, "exact prefix page count must be nonnegative");
+  PG_REQUIRE(exact_ppr > exact_sink_pages,
+             "exact cache must retain at least one tail-ring page");
+  const int64_t code_ppr = code_pages / batch;
+  PG_REQUIRE(exact_sink_pages < code_ppr,
+             "exact prefix exceeds the logical cache capacity");
+  if (device_position == nullptr)
+    PG_REQUIRE(position / pg::kPage < code_ppr,
+               "position exceeds the per-request PageGauge cache capacity");
+  PG_REQUIRE(aligned(query, 4) && aligned(key, 4) && aligned(value, 4) &&
+                 aligned(cosine, 4) && aligned(sine, 4) && aligned(key_center, 4) &&
+                 aligned(value_center, 4) && aligned(exact_key_pages, 4) &&
+                 aligned(exact_value_pages, 4) && aligned(key_codes, 2) &&
+                 aligned(value_codes, 2) && aligned(rotated_query, 4),
+             "tensors must be 4-byte aligned");
+  PG_REQUIRE(query_batch_stride % 2 == 0 && key_batch_stride % 2 == 0 &&
+                 value_batch_stride % 2 == 0 && rope_row_stride % 2 == 0 &&
+                 center_batch_stride % 2 == 0,
+             "batch strides must be even");
+  pg::AppendParams p{};
+  p.q = static_cast<const __half*>(query);
+  p.k = static_cast<const __half*>(key);
+  p.v = static_cast<const __half*>(value);
+  p.q_stride_b = query_batch_stride;
+  p.k_stride_b = key_batch_stride;
+  p.v_stride_b = value_batch_stride;
+  p.cos = static_cast<const __half*>(cosine);
+  p.sin = static_cast<const __half*>(sine);
+  p.device_position = device_position;
+  p.host_position = position;
+  p.rope_row_stride = rope_row_stride;
+  p.rope_rows = rope_rows;
+  p.rotated_q = static_cast<__half*>(rotated_query);
+  p.key_pages = static_cast<__half*>(exact_key_pages);
+  p.value_pages = static_cast<__half*>(exact_value_pages);
+  p.key_center = static_cast<const __half*>(key_center);
+  p.value_center = static_cast<const __half*>(value_center);
+  p.center_stride_b = center_batch_stride;
+  p.key_codes = static_cast<int8_t*>(key_codes);
+  p.value_codes = static_cast<int8_t*>(value_codes);
+  p.key_scales = static_cast<__half*>(key_scales);
+  p.value_scales = static_cast<__half*>(value_scales);
+  p.batch = batch;
+  p.hq = query_heads;
+  p.hkv = kv_heads;
+  p.exact_pages_per_request = exact_ppr;
+  p.exact_sink_pages = exact_sink_pages;
+  p.code_pages_per_request = code_ppr;
+  p.error_flag = device_error_ptr();
+  pg::pg_rope_append_page_gauge_kernel<<<batch * kv_heads, 64, 0,
+                                         static_cast<cudaStream_t>(stream)>>>(p);
+  return cuda_check(cudaGetLastError(), "rope_append_page_gauge launch");
+}
+
+// -------------------------------------------------------------- tail merge
+int32_t pg_exact_tail_merge_center(
+    const void* query, const void* exact_key_pages,
+    const void* exact_value_pages, int64_t exact_pages_total,
+    const int32_t* exact_page_indices, int64_t num_indices,
+    const int32_t* exact_last_page_len, void* old_output, float* old_lse,
+    const void* value_center, int64_t center_batch_stride, int32_t batch,
+    int32_t query_heads, int32_t kv_heads, double sm_scale, void* stream) {
+  PG_REQUIRE(batch > 0, "batch size must be positive");
+  PG_REQUIRE(query_heads > 0 && kv_heads > 0 && query_heads % kv_heads == 0,
+             "query heads must be a positive multiple of KV heads");
+  PG_REQUIRE(query_heads / kv_heads <= 8,
+             "the fused exact-tail kernel supports GQA group sizes up to 8");
+  PG_REQUIRE(num_indices % batch == 0, "exact page indices must divide evenly across requests");
+  const int64_t n = num_indices / batch;
+  PG_REQUIRE(n > 0 && n <= 16, "the fused exact tail supports 1..16 pages per request");
+  PG_REQUIRE(exact_pages_total >= batch * n, "exact page index count exceeds the ring allocation");
+  PG_REQUIRE(sm_scale > 0.0 && std::isfinite(sm_scale), "sm_scale must be positive and finite");
+  PG_REQUIRE(aligned(exact_key_pages, 16) && aligned(exact_value_pages, 16),
+             "exact caches must be 16-byte aligned");
+  pg::DecodeParams p{};
+  p.q = static_cast<const __half*>(query);
+  p.q_stride_b = static_cast<int64_t>(query_heads) * pg::kHeadDim;
+  p.q_stride_h = pg::kHeadDim;
+  p.seg[1].indices = exact_page_indices;
+  p.seg[1].last_len = exact_last_page_len;
+  p.seg[1].num_pages = static_cast<int32_t>(exact_pages_total);
+  p.items = nullptr;
+  p.num_items = batch * kv_heads;
+  p.hkv = kv_heads;
+  p.group = query_heads / kv_heads;
+  p.sm_scale_log2 = static_cast<float>(sm_scale) * 1.4426950408889634f;
+  p.final_mode = 1;
+  p.out = static_cast<__half*>(old_output);
+  p.out_stride_b = static_cast<int64_t>(query_heads) * pg::kHeadDim;
+  p.out_stride_h = pg::kHeadDim;
+  p.lse_out = old_lse;
+  p.extra_o = static_cast<const __half*>(old_output);
+  p.extra_stride_b = p.out_stride_b;
+  p.extra_stride_h = p.out_stride_h;
+  p.extra_lse = old_lse;
+  p.value_center = static_cast<const __half*>(value_center);
+  p.vc_stride_b = center_batch_stride;
+  p.implicit_pages = static_cast<int32_t>(n);
+  p.error_flag = device_error_ptr();
+  CUtensorMap k16, v16, none;
+  std::memset(&none, 0, sizeof(none));
+  int32_t rc = make_page_map(&k16, exact_key_pages, exact_pages_total, kv_heads, true);
+  if (rc != PG_OK) return rc;
+  rc = make_page_map(&v16, exact_value_pages, exact_pages_total, kv_heads, true);
+  if (rc != PG_OK) return rc;
+  const int warps = n >= 8 ? 8 : static_cast<int>(n);
+  return launch_decode(p, none, none, k16, v16, batch * kv_heads, warps,
+                       static_cast<cudaStream_t>(stream));
+}
+
+// ------------------------------------------------------------------ decode
+int32_t pg_decode_plan(int32_t batch, int32_t kv_heads, const int32_t* indptr0,
+                       const int32_t* indptr1, int32_t split_pages0,
+                       int32_t split_pages1, int32_t num_sms,
+                       int32_t warps_per_cta, pg_decode_item* items,
+                       int64_t items_capacity, int32_t* item_off,
+                       pg_plan_info* info) {
+  PG_REQUIRE(batch > 0 && kv_heads > 0, "batch and kv heads must be positive");
+  PG_REQUIRE(indptr0 != nullptr || indptr1 != nullptr, "at least one segment is required");
+  PG_REQUIRE(split_pages0 >= 0 && split_pages1 >= 0, "fixed split size must be non-negative");
+  PG_REQUIRE(kv_heads < 65536, "too many kv heads");
+  const int W = warps_per_cta <= 0 ? 4 : std::min(warps_per_cta, pg::kMaxWarps);
+  const int32_t* ind[2] = {indptr0, indptr1};
+  int64_t pages[2] = {0, 0};
+  for (int s = 0; s < 2; ++s) {
+    if (ind[s] == nullptr) continue;
+    PG_REQUIRE(ind[s][0] >= 0, "indptr must start at a non-negative offset");
+    for (int r = 0; r < batch; ++r) {
+      const int64_t n = static_cast<int64_t>(ind[s][r + 1]) - ind[s][r];
+      PG_REQUIRE(n >= 0, "indptr must be non-decreasing");
+      pages[s] += n;
+    }
+  }
+  int split[2] = {split_pages0, split_pages1};
+  if (split[0] == 0 || split[1] == 0) {
+    // Automatic: minimise the estimated makespan
+    //   ceil(items / resident_slots) * (pages per item + startup overhead)
+    // where an FP16 page counts twice an INT8 page and an FP16 item gets
+    // half the pages.  One full wave (items <= slots) is what this usually
+    // picks; a partial second wave doubles the step time.
+    const int ctas_per_sm = pg_ctas_per_sm(W);
+    const int64_t slots = static_cast<int64_t>(std::max(num_sms, 1)) * ctas_per_sm;
+    int64_t max_n = 1;
+    for (int s = 0; s < 2; ++s) {
+      if (ind[s] == nullptr) continue;
+      for (int r = 0; r < batch; ++r)
+        max_n = std::max<int64_t>(max_n, static_cast<int64_t>(ind[s][r + 1]) - ind[s][r]);
+    }
+    constexpr double kOverheadPages = 8.0;  // ~2 us of CTA start-up at 15 GB/s
+    double best_cost = 1e300;
+    int best = 1;
+    for (int64_t c = 1; c <= max_n; c = c < 64 ? c + 1 : c + c / 32) {
+      const int64_t c0 = split[0] ? split[0] : c;
+      const int64_t c1 = split[1] ? split[1] : std::max<int64_t>(1, c / 2);
+      int64_t items = 0;
+      double longest = 0.0;
+      for (int r = 0; r < batch; ++r) {
+        for (int s = 0; s < 2; ++s) {
+          if (ind[s] == nullptr) continue;
+          const int64_t n = static_cast<int64_t>(ind[s][r + 1]) - ind[s][r];
+          const int64_t cs = s == 0 ? c0 : c1;
+          items += (n + cs - 1) / cs;
+          longest = std::max(longest, static_cast<double>(std::min(n, cs)) * (s == 0 ? 1.0 : 2.0));
+        }
+      }
+      items *= kv_heads;
+      const double waves = static_cast<double>((items + slots - 1) / slots);
+      const double cost = waves * (longest + kOverheadPages);
+      if (cost < best_cost - 1e-9) {
+        best_cost = cost;
+        best = static_cast<int>(c);
+      }
+    }
+    if (split[0] == 0) split[0] = best;
+    if (split[1] == 0) split[1] = std::max(1, best / 2);
+  }
+  int64_t count = 0;
+  int32_t max_per_head = 0;
+  bool single = true;
+  for (int r = 0; r < batch; ++r) {
+    for (int h = 0; h < kv_heads; ++h) {
+      if (item_off) item_off[r * kv_heads + h] = static_cast<int32_t>(count);
+      int32_t here = 0;
+      for (int s = 0; s < 2; ++s) {
+        if (ind[s] == nullptr) continue;
+        const int32_t b = ind[s][r], e = ind[s][r + 1];
+        for (int32_t c = b; c < e; c += split[s]) {
+          const int32_t n = std::min(split[s], e - c);
+          if (count < items_capacity && items != nullptr) {
+            pg_decode_item& it = items[count];
+            it.request = r;
+            it.head_seg = h | (s << 16);
+            it.idx_begin = c;
+            it.count = n | ((c + n == e) ? static_cast<int32_t>(0x80000000u) : 0);
+          }
+          ++count;
+          ++here;
+        }
+      }
+      max_per_head = std::max(max_per_head, here);
+      if (here != 1) single = false;
+    }
+  }
+  if (item_off) item_off[batch * kv_heads] = static_cast<int32_t>(count);
+  if (info) {
+    info->num_items = count;
+    info->max_items_per_head = max_per_head;
+    info->single_item_per_head = single ? 1 : 0;
+    info->split_pages[0] = split[0];
+    info->split_pages[1] = split[1];
+    info->warps_per_cta = W;
+  }
+  if (count > items_capacity)
+    return fail(PG_ERR_CAPACITY, "work list needs %lld items, capacity %lld",
+                static_cast<long long>(count), static_cast<long long>(items_capacity));
+  PG_REQUIRE(count < (int64_t(1) << 31), "too many work items");
+  return PG_OK;
+}
+
+int32_t pg_decode_run(const pg_decode_args* a, void* stream) {
+  PG_REQUIRE(a != nullptr, "null arguments");
+  PG_REQUIRE(a->batch > 0 && a->kv_heads > 0, "batch and kv heads must be positive");
+  PG_REQUIRE(a->group >= 1 && a->group <= 8, "GQA group size must be in 1..8");
+  PG_REQUIRE(a->sm_scale > 0.f && std::isfinite(a->sm_scale), "sm_scale must be positive and finite");
+  PG_REQUIRE(a->q != nullptr && aligned(a->q, 4) && a->q_stride_b % 2 == 0 && a->q_stride_h % 2 == 0,
+             "query must be 4-byte aligned with even strides");
+  PG_REQUIRE(a->out != nullptr, "output is required");
+  PG_REQUIRE(a->num_items >= 0, "negative item count");
+  const int W = a->warps_per_cta <= 0 ? 4 : std::min(a->warps_per_cta, pg::kMaxWarps);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  pg::DecodeParams p{};
+  p.q = static_cast<const __half*>(a->q);
+  p.q_stride_b = a->q_stride_b;
+  p.q_stride_h = a->q_stride_h;
+  CUtensorMap maps[4];
+  std::memset(maps, 0, sizeof(maps));
+  for (int s = 0; s < 2; ++s) {
+    const pg_segment& sg = a->seg[s];
+    if (sg.k_cache == nullptr) continue;
+    PG_REQUIRE(sg.v_cache != nullptr && sg.indices != nullptr && sg.last_page_len != nullptr,
+               "segment %d is incomplete", s);
+    PG_REQUIRE(sg.num_pages > 0 && sg.num_pages < (int64_t(1) << 27),
+               "segment %d page count out of range", s);
+    if (s == 0)
+      PG_REQUIRE(sg.k_scale != nullptr && sg.v_scale != nullptr,
+                 "INT8 segment needs k/v page scales");
+    int32_t rc = make_page_map(&maps[2 * s], sg.k_cache, sg.num_pages, a->kv_heads, s == 1);
+    if (rc != PG_OK) return rc;
+    rc = make_page_map(&maps[2 * s + 1], sg.v_cache, sg.num_pages, a->kv_heads, s == 1);
+    if (rc != PG_OK) return rc;
+    p.seg[s].indices = sg.indices;
+    p.seg[s].last_len = sg.last_page_len;
+    p.seg[s].k_scale = static_cast<const __half*>(sg.k_scale);
+    p.seg[s].v_scale = static_cast<const __half*>(sg.v_scale);
+    p.seg[s].num_pages = static_cast<int32_t>(sg.num_pages);
+  }
+  p.items = reinterpret_cast<const pg::DecodeItem*>(a->items);
+  p.num_items = a->num_items;
+  p.hkv = a->kv_heads;
+  p.group = a->group;
+  p.sm_scale_log2 = a->sm_scale * 1.4426950408889634f;
+  p.part_o = a->part_o;
+  p.part_lse = a->part_lse;
+  p.final_mode = a->final_mode;
+  p.out = static_cast<__half*>(a->out);
+  p.out_stride_b = a->out_stride_b;
+  p.out_stride_h = a->out_stride_h;
+  p.lse_out = a->lse_out;
+  p.extra_o = static_cast<const __half*>(a->extra_o);
+  p.extra_stride_b = a->extra_stride_b;
+  p.extra_stride_h = a->extra_stride_h;
+  p.extra_lse = a->extra_lse;
+  p.value_center = static_cast<const __half*>(a->value_center);
+  p.vc_stride_b = a->vc_stride_b;
+  p.implicit_pages = 0;
+  p.error_flag = device_error_ptr();
+  if (a->extra_o != nullptr) PG_REQUIRE(a->extra_lse != nullptr, "extra state needs its lse");
+
+  const int mask = (a->stage_mask & 3) == 0 ? 3 : (a->stage_mask & 3);
+  if (a->num_items > 0 && (mask & 1)) {
+    PG_REQUIRE(a->items != nullptr, "work items are required");
+    if (!a->final_mode)
+      PG_REQUIRE(a->part_o != nullptr && a->part_lse != nullptr,
+                 "split decode needs a partial-state workspace");
+    int32_t rc = launch_decode(p, maps[0], maps[1], maps[2], maps[3], a->num_items, W, st);
+    if (rc != PG_OK) return rc;
+  }
+  if (a->final_mode && a->num_items > 0) return PG_OK;
+  if (!(mask & 2)) return PG_OK;
+
+  PG_REQUIRE(a->item_off != nullptr, "item offsets are required for the merge");
+  pg::MergeParams m{};
+  m.part_o = a->part_o;
+  m.part_lse = a->part_lse;
+  m.item_off = a->item_off;
+  m.batch = a->batch;
+  m.hkv = a->kv_heads;
+  m.group = a->group;
+  m.out = p.out;
+  m.out_stride_b = a->out_stride_b;
+  m.out_stride_h = a->out_stride_h;
+  m.lse_out = a->lse_out;
+  m.extra_o = p.extra_o;
+  m.extra_stride_b = a->extra_stride_b;
+  m.extra_stride_h = a->extra_stride_h;
+  m.extra_lse = a->extra_lse;
+  m.value_center = p.value_center;
+  m.vc_stride_b = a->vc_stride_b;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(a->batch * a->kv_heads * a->group);
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_check(cudaLaunchKernelEx(&cfg, pg::pg_merge_partials_kernel, m),
+                    "merge kernel launch");
+}
+
+int32_t pg_merge_state_in_place(void* v_a, float* s_a, const void* v_b,
+                                const float* s_b, int64_t rows,
+                                int64_t va_row_stride, int64_t vb_row_stride,
+                                void* stream) {
+  PG_REQUIRE(rows >= 0, "rows must be non-negative");
+  if (rows == 0) return PG_OK;
+  PG_REQUIRE(rows < (int64_t(1) << 31), "too many rows");
+  pg::pg_merge_state_kernel<<<static_cast<unsigned>(rows), 128, 0,
+                              static_cast<cudaStream_t>(stream)>>>(
+      static_cast<__half*>(v_a), s_a, static_cast<const __half*>(v_b), s_b, rows,
+      va_row_stride, vb_row_stride);
+  return cuda_check(cudaGetLastError(), "merge_state launch");
+}
+
+int32_t pg_quantize_pages(const void* key, const void* value,
+                          const void* key_center, const void* value_center,
+                          int64_t pages_per_center, void* key_codes,
+                          void* value_codes, void* key_scales,
+                          void* value_scales, int64_t num_pages,
+                          int32_t kv_heads, int32_t rounding, void* stream) {
+  PG_REQUIRE(num_pages >= 0 && kv_heads > 0, "page and head counts must be positive");
+  PG_REQUIRE(rounding == 0 || rounding == 1, "rounding must be 0 (half away) or 1 (half even)");
+  PG_REQUIRE(pages_per_center >= 0, "pages_per_center must be non-negative");
+  if (num_pages == 0) return PG_OK;
+  PG_REQUIRE(num_pages * kv_heads < (int64_t(1) << 31), "too many pages");
+  PG_REQUIRE(aligned(key, 4) && aligned(value, 4) && aligned(key_center, 4) &&
+                 aligned(value_center, 4) && aligned(key_codes, 2) && aligned(value_codes, 2),
+             "tensors must be aligned");
+  pg::QuantizeParams p{};
+  p.key = static_cast<const __half*>(key);
+  p.value = static_cast<const __half*>(value);
+  p.key_center = static_cast<const __half*>(key_center);
+  p.value_center = static_cast<const __half*>(value_center);
+  p.pages_per_center = pages_per_center;
+  p.key_codes = static_cast<int8_t*>(key_codes);
+  p.value_codes = static_cast<int8_t*>(value_codes);
+  p.key_scales = static_cast<__half*>(key_scales);
+  p.value_scales = static_cast<__half*>(value_scales);
+  p.num_pages = num_pages;
+  p.hkv = kv_heads;
+  p.half_even = rounding;
+  pg::pg_quantize_pages_kernel<<<static_cast<unsigned>(num_pages * kv_heads), 64, 0,
+                                 static_cast<cudaStream_t>(stream)>>>(p);
+  return cuda_check(cudaGetLastError(), "quantize launch");
+}
+
+}  // extern "C"

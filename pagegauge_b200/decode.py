@@ -1,0 +1,105 @@
+"""Fused PageGauge decode attention: old INT8 pages + exact FP16 pages,
+LSE merge and value-centre restore in one split-KV launch plus one merge
+launch (or a single launch when every (request, KV head) fits one CTA).
+
+This is the B200 form of the reference's segmented eager attention
+(scripts/benchmark_page_gauge_transformer.py:2261-2308: old_wrapper.run +
+exact_wrapper.run + merge_state_in_place + add_(output_center)) and of its
+single-launch heterogeneous ABI (scripts/page_gauge_heterogeneous_fa2.py).
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import torch
+
+from .wrapper import (HEAD_DIM, PAGE, PagedDecodePlan, _segment, _Workspace, check_cache,
+                      host_indptr, launch_decode, num_sms, plan_items)
+
+
+class PageGaugeDecode:
+    """Plan once per page-table change, run per layer/step (graph-safe)."""
+
+    def __init__(self, workspace: torch.Tensor, warps_per_cta: int = 4):
+        self._ws = _Workspace(workspace)
+        self._warps = warps_per_cta
+        self._plan: PagedDecodePlan | None = None
+        self.sm_scale = 1.0 / math.sqrt(HEAD_DIM)
+
+    def plan(self, old_indptr, old_indices, exact_indptr, exact_indices, exact_last_page_len,
+             num_qo_heads: int = 32, num_kv_heads: int = 8, old_split_pages: int = 0,
+             exact_split_pages: int = 0, old_last_page_len: torch.Tensor | None = None,
+             sm_scale: float | None = None) -> None:
+        """``*_indptr`` CSR over the per-request page ids (host or device);
+        ``*_indices`` device int32.  Old pages are full unless
+        ``old_last_page_len`` says otherwise."""
+        if num_qo_heads % num_kv_heads or not 1 <= num_qo_heads // num_kv_heads <= 8:
+            raise ValueError("num_qo_heads must be a multiple (1..8) of num_kv_heads")
+        o_ind = None if old_indptr is None else host_indptr(old_indptr)
+        e_ind = None if exact_indptr is None else host_indptr(exact_indptr)
+        batch = (o_ind if o_ind is not None else e_ind).size - 1
+        dev = self._ws.buffer.device
+        items, off, info = plan_items(batch, num_kv_heads, o_ind, e_ind, int(old_split_pages),
+                                      int(exact_split_pages), num_sms(dev), self._warps)
+        self._plan = PagedDecodePlan(self._ws, items, off, info, batch, num_kv_heads,
+                                     num_qo_heads // num_kv_heads)
+        self._old_indices = old_indices
+        self._exact_indices = exact_indices
+        self._exact_last = exact_last_page_len
+        if old_last_page_len is None and o_ind is not None:
+            old_last_page_len = torch.full((batch,), PAGE, dtype=torch.int32, device=dev)
+        self._old_last = old_last_page_len
+        self._num_qo_heads, self._num_kv_heads = num_qo_heads, num_kv_heads
+        if sm_scale is not None:
+            self.sm_scale = float(sm_scale)
+
+    @property
+    def work_plan(self) -> PagedDecodePlan:
+        if self._plan is None:
+            raise RuntimeError("plan() has not been called")
+        return self._plan
+
+    def run(self, q: torch.Tensor, key_codes, value_codes, key_scales, value_scales,
+            exact_key, exact_value, value_center: torch.Tensor | None,
+            out: torch.Tensor | None = None, lse: torch.Tensor | None = None,
+            sm_scale: float | None = None) -> torch.Tensor:
+        plan = self.work_plan
+        segs = [None, None]
+        if self._old_indices is not None:
+            check_cache(key_codes, "key_codes", torch.int8, self._num_kv_heads)
+            check_cache(value_codes, "value_codes", torch.int8, self._num_kv_heads)
+            segs[0] = _segment(key_codes, value_codes, self._old_indices, self._old_last,
+                               key_scales, value_scales)
+        if self._exact_indices is not None:
+            check_cache(exact_key, "exact_key", torch.float16, self._num_kv_heads)
+            check_cache(exact_value, "exact_value", torch.float16, self._num_kv_heads)
+            segs[1] = _segment(exact_key, exact_value, self._exact_indices, self._exact_last)
+        if out is None:
+            out = torch.empty_like(q)
+        if value_center is not None and (value_center.dtype != torch.float16
+                                         or not value_center.is_contiguous()):
+            raise ValueError("value_center must be contiguous float16")
+        launch_decode(plan, q, segs, self.sm_scale if sm_scale is None else sm_scale, out, lse,
+                      value_center=value_center)
+        return out
+
+
+def split_tables(pages_per_row, exact_tail_pages: int, exact_sink_pages: int = 0):
+    """Host CSR tables of the old INT8 segment and the exact segment for
+    request-major contiguous storage (segment_page_table semantics,
+    scripts/benchmark_flashinfer_page_affine_int8.py:392-420)."""
+    old_counts = [max(c - exact_tail_pages - exact_sink_pages, 0) for c in pages_per_row]
+    exact_counts = [c - o for c, o in zip(pages_per_row, old_counts)]
+    old_idx, exact_idx = [], []
+    start = 0
+    for count, old in zip(pages_per_row, old_counts):
+        mid = start + exact_sink_pages
+        old_idx.extend(range(mid, mid + old))
+        exact_idx.extend(range(start, mid))
+        exact_idx.extend(range(mid + old, start + count))
+        start += count
+    def csr(counts):
+        return np.concatenate([[0], np.cumsum(counts)]).astype(np.int32)
+    return csr(old_counts), np.asarray(old_idx, np.int32), csr(exact_counts), np.asarray(exact_idx, np.int32)

@@ -1,0 +1,130 @@
+"""Split-KV scheduler: pick pages per work item (``num_splits`` =
+ceil(pages / split)) per (batch, context) bucket from measured timings.
+
+The reference froze one ``fixed_split_size`` per method from a pilot sweep
+over {auto, 64, 128, 256, 512} pages, keeping the cache-neutral p50 argmin
+(scripts/run_page_gauge_validation.py:277-316, B1/49K at :374-416).  Here
+the sweep covers num_splits 1..64 per KV head (and the heuristic), each
+candidate timed on the GPU with a >= 256 MiB scrub before every sample, and
+the argmin is stored per bucket in ``split_table.json`` next to this file.
+
+    python -m pagegauge_b200.scheduler --sweep [--batch 1 --context 49152]
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import statistics
+from pathlib import Path
+
+TABLE_PATH = Path(__file__).resolve().parent / "split_table.json"
+PAGE = 16
+
+
+def bucket(batch: int, context: int) -> str:
+    """Batch exact, context rounded up to a power of two (>= 1024)."""
+    c = 1 << max(10, math.ceil(math.log2(max(context, 1))))
+    return f"b{batch}_c{c}"
+
+
+def load_table(path: Path = TABLE_PATH) -> dict:
+    if path.is_file():
+        return json.loads(path.read_text())
+    return {"entries": {}}
+
+
+def lookup(batch: int, context: int, path: Path = TABLE_PATH) -> int:
+    """Pages per work item for this shape; 0 (the one-wave heuristic) when
+    the bucket was never measured."""
+    entry = load_table(path)["entries"].get(bucket(batch, context))
+    return int(entry["split_pages"]) if entry else 0
+
+
+def candidates(old_pages_per_request: int) -> list[int]:
+    """Split sizes giving num_splits in {1,2,4,...,64} per (request, head),
+    plus 0 for the heuristic."""
+    out = {0}
+    for splits in (1, 2, 4, 8, 16, 32, 48, 64):
+        out.add(max(1, math.ceil(old_pages_per_request / splits)))
+    return sorted(out)
+
+
+def record(batch: int, context: int, results: dict[int, float], path: Path = TABLE_PATH,
+           meta: dict | None = None) -> int:
+    """Store the argmin of {split_pages: p50 microseconds}."""
+    best = min(results, key=results.get)
+    table = load_table(path)
+    table["entries"][bucket(batch, context)] = {
+        "split_pages": int(best), "p50_us": results[best],
+        "candidates_us": {str(k): v for k, v in sorted(results.items())}, **(meta or {})}
+    path.write_text(json.dumps(table, indent=1, sort_keys=True) + "\n")
+    return best
+
+
+def sweep(batch: int, context: int, repeats: int = 60, seeds=(20261001, 20261002, 20261003),
+          write: bool = True) -> dict[int, float]:
+    """Time every candidate split on the current GPU (cache-neutral p50 over
+    seeds) and record the winner."""
+    import torch
+
+    from .cache import build_gauge_cache, synthetic_dense_cache
+    from .decode import PageGaugeDecode
+
+    lengths = [context] * batch
+    scrub = torch.zeros(256 << 18, dtype=torch.int32, device="cuda")  # 256 MiB
+    ws = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    results: dict[int, list[float]] = {}
+    for seed in seeds:
+        q, dk, dv = synthetic_dense_cache(lengths, seed=seed, device="cuda")
+        cache, tables = build_gauge_cache(dk, dv, lengths)
+        del dk, dv
+        old_pages = tables.old_tokens[0] // PAGE
+        for split in candidates(old_pages):
+            dec = PageGaugeDecode(ws)
+            dec.plan(tables.old_indptr, tables.old_indices, tables.exact_indptr, tables.exact_indices,
+                     tables.exact_last_page_len, 32, 8, old_split_pages=split)
+            out = torch.empty_like(q)
+
+            def run():
+                dec.run(q, cache.key_codes, cache.value_codes, cache.key_scales, cache.value_scales,
+                        cache.exact_key, cache.exact_value, cache.value_center, out=out)
+
+            for _ in range(5):
+                run()
+            times = []
+            for _ in range(repeats):
+                scrub.add_(1)
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s.record()
+                run()
+                e.record()
+                e.synchronize()
+                times.append(s.elapsed_time(e) * 1e3)
+            results.setdefault(split, []).append(statistics.median(times))
+        del cache
+    p50 = {k: statistics.median(v) for k, v in results.items()}
+    if write:
+        record(batch, context, p50, meta={"gpu": torch.cuda.get_device_name(), "repeats": repeats,
+                                           "seeds": list(seeds), "mode": "cache_neutral"})
+    return p50
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser(description=__doc__)
+    parser.add_argument("--sweep", action="store_true")
+    parser.add_argument("--batch", type=int, nargs="*", default=[1])
+    parser.add_argument("--context", type=int, nargs="*", default=[49152])
+    parser.add_argument("--repeats", type=int, default=60)
+    args = parser.parse_args()
+    if not args.sweep:
+        print(json.dumps(load_table(), indent=1))
+        return
+    for b in args.batch:
+        for c in args.context:
+            print(b, c, json.dumps(sweep(b, c, args.repeats)), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,58 @@
+"""Shared builders for the GPU parity tests: synthetic inputs on a CPU
+generator (so the oracle and the GPU see the same bytes), caches built by
+the product on the GPU, expected values from the CPU oracle."""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from oracle import pagegauge_oracle as O
+from pagegauge_b200.cache import build_gauge_cache, synthetic_dense_cache
+
+ATOL = 2e-3        # max-abs 2e-3 in FP16 ...
+MIN_COSINE = 0.9999  # ... and cosine >= 0.9999
+
+
+def make_case(lengths, hkv=8, group=4, tail_pages=16, sink_pages=0, seed=20261001):
+    q, dk, dv = synthetic_dense_cache(lengths, hkv=hkv, seed=seed, group=group)
+    cache, tables = build_gauge_cache(dk.cuda(), dv.cuda(), lengths, tail_pages, sink_pages)
+    return q.cuda(), dk, dv, cache, tables
+
+
+def cpu(t):
+    return t.detach().cpu().numpy()
+
+
+def check_quantizer_bit_exact(dk, dv, cache, lengths):
+    """The GPU-built codes/scales equal the oracle's bulk quantiser given the
+    same centres (fp32 centring, half-away rounding)."""
+    pages = [-(-n // 16) for n in lengths]
+    start = 0
+    for r, n in enumerate(pages):
+        for dense, codes, scales, center in ((dk, cache.key_codes, cache.key_scales, cache.key_center),
+                                             (dv, cache.value_codes, cache.value_scales, cache.value_center)):
+            c, s = O.quantize_pages_bulk(cpu(dense[start:start + n]), cpu(center[r]), "half_away")
+            assert np.array_equal(cpu(codes[start:start + n]), c)
+            assert np.array_equal(cpu(scales[start:start + n]).view(np.uint16), s.view(np.uint16))
+        start += n
+
+
+def oracle_decode(q, cache, tables, lengths, request, with_center=True, sm_scale=128 ** -0.5):
+    o_ptr = cpu(tables.old_indptr)
+    e_ptr = cpu(tables.exact_indptr)
+    old_ids = cpu(tables.old_indices)[o_ptr[request]:o_ptr[request + 1]]
+    ex_ids = cpu(tables.exact_indices)[e_ptr[request]:e_ptr[request + 1]]
+    return O.page_gauge_decode(
+        cpu(q[request]), cpu(cache.key_codes), cpu(cache.value_codes), cpu(cache.key_scales),
+        cpu(cache.value_scales), old_ids, tables.old_tokens[request], cpu(cache.exact_key),
+        cpu(cache.exact_value), ex_ids, tables.exact_tokens[request],
+        cpu(cache.value_center[request]) if with_center else None, sm_scale)
+
+
+def assert_close_decode(out, expected, atol=ATOL):
+    got = out.float().cpu().numpy()
+    err = O.max_abs(got, expected)
+    cos = O.cosine(got, expected)
+    assert err <= atol and cos >= MIN_COSINE, f"max-abs {err:.3e}, cosine {cos:.6f}"
+    return err, cos

@@ -1,0 +1,93 @@
+"""The C-ABI library loads without a GPU, exports every symbol the header
+declares, and its host-only planner produces the expected work lists."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from pagegauge_b200 import _lib
+from pagegauge_b200.wrapper import plan_items
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from pagegauge_b200 import build
+
+    build.build()
+    return _lib.load()
+
+
+def declared_symbols() -> set[str]:
+    names = set()
+    for header in (ROOT / "include").glob("*.h"):
+        text = header.read_text()
+        names |= set(re.findall(r"^\s*(?:const\s+)?[\w\s\*]+?\b(pg_\w+)\s*\(", text, flags=re.M))
+    return names
+
+
+def test_every_declared_symbol_is_exported(lib):
+    names = declared_symbols()
+    assert {"pg_decode_run", "pg_rope_append_page_gauge", "pg_exact_tail_merge_center"} <= names
+    for name in names:
+        assert hasattr(lib, name), name
+    assert set(_lib.EXPORTED) <= names
+
+
+def test_struct_sizes_match_header_layout(lib):
+    assert ctypes.sizeof(_lib.PgDecodeItem) == 16
+    assert ctypes.sizeof(_lib.PgSegment) == 56
+    assert lib.pg_abi_version() == 100
+
+
+def test_planner_chunks_and_offsets(lib):
+    indptr0 = np.array([0, 10, 10, 25], np.int32)   # request 1 has no old pages
+    indptr1 = np.array([0, 2, 4, 5], np.int32)
+    items, off, info = plan_items(3, 2, indptr0, indptr1, 4, 1, 148)
+    # per head: r0: ceil(10/4)=3 old + 2 exact; r1: 0 + 2; r2: ceil(15/4)=4 + 1
+    assert off.tolist() == [0, 5, 10, 12, 14, 19, 24]
+    assert info.num_items == 24 and not info.single_item_per_head
+    it = items.reshape(-1, 4)
+    first = it[off[0]:off[1]]
+    assert first[:, 0].tolist() == [0] * 5
+    assert (first[:, 1] >> 16).tolist() == [0, 0, 0, 1, 1]
+    assert first[:, 2].tolist() == [0, 4, 8, 0, 1]
+    counts = first[:, 3] & 0x7FFFFFFF
+    last_flag = (first[:, 3] >> 31) & 1
+    assert counts.tolist() == [4, 4, 2, 1, 1]
+    assert last_flag.tolist() == [0, 0, 1, 0, 1]
+    # head 1 of request 0 is a copy with head index 1
+    assert (it[off[1]:off[2], 1] & 0xFFFF).tolist() == [1] * 5
+
+
+def test_planner_single_item_and_auto_split(lib):
+    indptr = np.array([0, 3056], np.int32)
+    items, off, info = plan_items(1, 8, indptr, None, 1 << 20, 0, 148)
+    assert info.single_item_per_head and info.num_items == 8
+    items, off, info = plan_items(1, 8, indptr, None, 0, 0, 148)
+    # one full wave of 3 CTAs per SM (444 slots) with the smallest items
+    assert info.split_pages[0] == 56
+    assert info.num_items == 8 * -(-3056 // 56) <= 444
+    # with the 16-page FP16 tail as one more item per head, 56 would need a
+    # partial second wave (448 > 444): the planner moves to 57
+    items, off, info = plan_items(1, 8, indptr, np.array([0, 16], np.int32), 0, 0, 148)
+    assert info.split_pages[0] == 57 and info.num_items == 440
+
+
+def test_planner_rejects_bad_input(lib):
+    with pytest.raises(RuntimeError, match="non-decreasing"):
+        plan_items(2, 8, np.array([0, 5, 3], np.int32), None, 4, 0, 148)
+    with pytest.raises(RuntimeError, match="at least one segment"):
+        plan_items(1, 8, None, None, 4, 0, 148)
+
+
+def test_error_message_roundtrip_without_gpu(lib):
+    rc = lib.pg_merge_state_in_place(None, None, None, None, -1, 128, 128, None)
+    assert rc == 1
+    assert b"non-negative" in lib.pg_last_error()

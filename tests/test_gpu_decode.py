@@ -1,0 +1,255 @@
+"""GPU parity of the split-KV page-affine decode path against the CPU oracle.
+
+Tolerance: FP16 outputs within max-abs 2e-3 and
+cosine >= 0.9999 of the float64 oracle; LSE within 2e-4 (the reference's
+tail-merge test, tests/test_page_gauge_append_extension.py:671-676)."""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import pagegauge_oracle as O
+from pagegauge_b200 import wrapper as W
+from pagegauge_b200.decode import PageGaugeDecode
+from pagegauge_b200.runtime import load_append_extension, read_device_error
+
+from gpu_helpers import (assert_close_decode, check_quantizer_bit_exact, cpu, make_case,
+                          oracle_decode)
+
+pytestmark = pytest.mark.gpu
+
+LSE_ATOL = 2e-4
+
+
+def workspace(mb=64):
+    return torch.empty(mb << 20, dtype=torch.uint8, device="cuda")
+
+
+def run_fused(q, cache, tables, split_old=0, split_exact=0, warps=4, with_center=True):
+    dec = PageGaugeDecode(workspace(), warps_per_cta=warps)
+    dec.plan(tables.old_indptr, tables.old_indices, tables.exact_indptr, tables.exact_indices,
+             tables.exact_last_page_len, q.shape[1], cache.key_codes.shape[2],
+             old_split_pages=split_old, exact_split_pages=split_exact)
+    lse = torch.empty(q.shape[0], q.shape[1], device="cuda", dtype=torch.float32)
+    out = dec.run(q, cache.key_codes, cache.value_codes, cache.key_scales, cache.value_scales,
+                  cache.exact_key, cache.exact_value, cache.value_center if with_center else None,
+                  lse=lse)
+    torch.cuda.synchronize()
+    assert read_device_error() == 0
+    return out, lse, dec
+
+
+@pytest.mark.parametrize("split", [0, 1, 7, 64, 1 << 20])
+def test_b1_4k_configs0_all_splits(cuda_lib, split):
+    """B=1, 4096 tokens = 240 INT8 pages + 16 FP16 tail pages."""
+    lengths = [4096]
+    q, dk, dv, cache, tables = make_case(lengths)
+    if split == 0:
+        check_quantizer_bit_exact(dk, dv, cache, lengths)
+    out, lse, _ = run_fused(q, cache, tables, split_old=split, split_exact=split)
+    exp, exp_lse = oracle_decode(q, cache, tables, lengths, 0)
+    assert_close_decode(out[0], exp)
+    np.testing.assert_allclose(cpu(lse[0]), exp_lse, atol=LSE_ATOL, rtol=0)
+
+
+@pytest.mark.parametrize("lengths", [[1000, 333, 2050], [17, 256, 257, 4095], [5000], [1]])
+def test_ragged_partial_pages(cuda_lib, lengths):
+    """Ragged requests with partial last pages, tail-only requests (<=256
+    tokens: no INT8 pages) and a single-token request."""
+    q, dk, dv, cache, tables = make_case(lengths, seed=7)
+    out, lse, _ = run_fused(q, cache, tables, split_old=5, split_exact=3)
+    for r in range(len(lengths)):
+        exp, exp_lse = oracle_decode(q, cache, tables, lengths, r)
+        assert_close_decode(out[r], exp)
+        np.testing.assert_allclose(cpu(lse[r]), exp_lse, atol=LSE_ATOL, rtol=0)
+
+
+@pytest.mark.parametrize("hkv,group", [(8, 1), (4, 2), (2, 4), (1, 8), (8, 8)])
+def test_gqa_group_sizes(cuda_lib, hkv, group):
+    lengths = [700, 1600]
+    q, dk, dv, cache, tables = make_case(lengths, hkv=hkv, group=group, seed=11)
+    out, lse, _ = run_fused(q, cache, tables, split_old=9, split_exact=4)
+    for r in range(len(lengths)):
+        exp, exp_lse = oracle_decode(q, cache, tables, lengths, r)
+        assert_close_decode(out[r], exp)
+
+
+@pytest.mark.parametrize("warps", [1, 2, 4, 8])
+def test_warps_per_cta(cuda_lib, warps):
+    lengths = [3000]
+    q, dk, dv, cache, tables = make_case(lengths, seed=3)
+    out, _, _ = run_fused(q, cache, tables, split_old=37, split_exact=16, warps=warps)
+    exp, _ = oracle_decode(q, cache, tables, lengths, 0)
+    assert_close_decode(out[0], exp)
+
+
+def test_single_item_final_epilogue_matches_split_path(cuda_lib):
+    lengths = [2048, 1024]
+    q, dk, dv, cache, tables = make_case(lengths, seed=5)
+    single, lse1, dec = run_fused(q, cache, tables, split_old=1 << 20, split_exact=1 << 20)
+    assert not dec.work_plan.single  # old + exact segments: two items per head
+    split, lse2, _ = run_fused(q, cache, tables, split_old=3, split_exact=2)
+    assert (single.float() - split.float()).abs().max().item() < 2e-3
+    # old segment only, one item per head -> single-launch final epilogue
+    dec = PageGaugeDecode(workspace())
+    dec.plan(tables.old_indptr, tables.old_indices, None, None, None, 32, 8, old_split_pages=1 << 20)
+    assert dec.work_plan.single
+    out = dec.run(q, cache.key_codes, cache.value_codes, cache.key_scales, cache.value_scales,
+                  None, None, None)
+    torch.cuda.synchronize()
+    for r, n in enumerate(lengths):
+        o_ptr = cpu(tables.old_indptr)
+        ids = cpu(tables.old_indices)[o_ptr[r]:o_ptr[r + 1]]
+        ko = O.dequant_tokens(cpu(cache.key_codes), cpu(cache.key_scales), ids, tables.old_tokens[r])
+        vo = O.dequant_tokens(cpu(cache.value_codes), cpu(cache.value_scales), ids, tables.old_tokens[r])
+        exp, _ = O.attention_state(cpu(q[r]), ko, vo, 128 ** -0.5)
+        assert_close_decode(out[r], exp)
+
+
+def test_reference_segmented_sequence_equals_fused(cuda_lib):
+    """The reference's eager attention (old wrapper run + exact wrapper run
+    + merge_state_in_place + centre add,
+    scripts/benchmark_page_gauge_transformer.py:2261-2308) through the
+    drop-in wrappers equals the fused launch and the oracle."""
+    lengths = [3000, 1500]
+    q, dk, dv, cache, tables = make_case(lengths, seed=13)
+    old = W.make_page_gauge_wrapper(None, workspace())
+    W.plan(old, tables.old_indptr, tables.old_indices, torch.full((2,), 16, dtype=torch.int32, device="cuda"),
+           torch.int8, 0)
+    exact = W.BatchDecodeWithPagedKVCacheWrapper(workspace(), "NHD", use_tensor_cores=True, backend="fa2")
+    W.plan(exact, tables.exact_indptr, tables.exact_indices, tables.exact_last_page_len, torch.float16, 0)
+    out = torch.empty_like(q)
+    old_lse = torch.empty(2, 32, device="cuda", dtype=torch.float32)
+    ex_out = torch.empty_like(q)
+    ex_lse = torch.empty_like(old_lse)
+    old.run(q, (cache.key_codes, cache.value_codes), cache.key_scales, cache.value_scales,
+            1.0 / math.sqrt(128), out=out, lse=old_lse, return_lse=True)
+    exact.run(q, (cache.exact_key, cache.exact_value), out=ex_out, lse=ex_lse, return_lse=True)
+    W.merge_state_in_place(out, old_lse, ex_out, ex_lse)
+    out.add_(cache.value_center.repeat_interleave(4, dim=1))
+    fused, fused_lse, _ = run_fused(q, cache, tables)
+    torch.cuda.synchronize()
+    assert (out.float() - fused.float()).abs().max().item() < 2e-3
+    for r in range(2):
+        exp, exp_lse = oracle_decode(q, cache, tables, lengths, r)
+        assert_close_decode(out[r], exp)
+        np.testing.assert_allclose(cpu(old_lse[r]), exp_lse, atol=LSE_ATOL, rtol=0)
+
+
+def test_merge_state_in_place_matches_oracle(cuda_lib):
+    g = torch.Generator().manual_seed(2)
+    va = torch.randn(3, 32, 128, generator=g).half()
+    vb = torch.randn(3, 32, 128, generator=g).half()
+    sa = torch.randn(3, 32, generator=g) * 4
+    sb = torch.randn(3, 32, generator=g) * 4
+    sb[0, 0] = -math.inf
+    exp, exp_lse = O.merge_state_in_place(va.reshape(-1, 128).numpy(), sa.reshape(-1).numpy(),
+                                          vb.reshape(-1, 128).numpy(), sb.reshape(-1).numpy())
+    va_d, sa_d = va.cuda(), sa.cuda()
+    W.merge_state_in_place(va_d, sa_d, vb.cuda(), sb.cuda())
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(cpu(va_d).reshape(-1, 128).astype(np.float64), exp, atol=2e-3)
+    np.testing.assert_allclose(cpu(sa_d).reshape(-1), exp_lse, atol=LSE_ATOL)
+
+
+@pytest.mark.parametrize("tail_tokens", [1, 15, 16, 17, 241, 255, 256])
+def test_exact_tail_merge_center_vs_reference_formula(cuda_lib, tail_tokens):
+    """Golden fixture from the reference test's own einsum oracle
+    (tests/test_page_gauge_append_extension.py:588-676): atol 3e-3/rtol 2e-3
+    on the output, 2e-4 on the LSE."""
+    from pathlib import Path
+    g = np.load(Path(__file__).resolve().parent / "golden" / "tail_merge.npz")
+    p = f"t{tail_tokens}_"
+    ext = load_append_extension()
+    old_out = torch.from_numpy(g[p + "old_out"]).cuda()
+    old_lse = torch.from_numpy(g[p + "old_lse"]).cuda()
+    ext.exact_tail_merge_center(torch.from_numpy(g["query"]).cuda(), torch.from_numpy(g["exact_k"]).cuda(),
+                                torch.from_numpy(g["exact_v"]).cuda(), torch.from_numpy(g[p + "indices"]).cuda(),
+                                torch.from_numpy(g[p + "last_len"]).cuda(), old_out, old_lse,
+                                torch.from_numpy(g["value_center"]).cuda(), 128 ** -0.5)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(old_out.float().cpu(), torch.from_numpy(g[p + "expected_out"]), atol=3e-3, rtol=2e-3)
+    torch.testing.assert_close(old_lse.cpu(), torch.from_numpy(g[p + "expected_lse"]), atol=2e-4, rtol=2e-5)
+
+
+def test_batched_exact_tail_merge_center(cuda_lib):
+    """tests/test_page_gauge_append_extension.py:832-930 scenario vs oracle."""
+    g = torch.Generator().manual_seed(173)
+    batch, ring, tails = 3, 4, [33, 37, 47]
+    q = torch.randn(batch, 32, 128, generator=g).half()
+    ek = (torch.randn(batch * ring, 16, 8, 128, generator=g) * 0.35).half()
+    ev = (torch.randn(batch * ring, 16, 8, 128, generator=g) * 0.35).half()
+    vc = (torch.randn(batch, 8, 128, generator=g) * 0.1).half()
+    idx = torch.stack([r * ring + torch.tensor([2, 3, 0], dtype=torch.int32) for r in range(batch)]).reshape(-1)
+    last = torch.tensor([(t - 1) % 16 + 1 for t in tails], dtype=torch.int32)
+    old_out = (torch.randn(batch, 32, 128, generator=g) * 0.2).half()
+    old_lse = torch.randn(batch, 32, generator=g) * 0.5 + 8.0
+    d_out, d_lse = old_out.cuda(), old_lse.cuda()
+    load_append_extension().exact_tail_merge_center(q.cuda(), ek.cuda(), ev.cuda(), idx.cuda(), last.cuda(),
+                                                    d_out, d_lse, vc.cuda(), 128 ** -0.5)
+    torch.cuda.synchronize()
+    for r in range(batch):
+        exp, exp_lse = O.exact_tail_merge_center(q[r].numpy(), ek.numpy(), ev.numpy(),
+                                                 idx.view(batch, 3)[r].numpy(), tails[r],
+                                                 old_out[r].numpy(), old_lse[r].numpy(), vc[r].numpy(),
+                                                 128 ** -0.5)
+        np.testing.assert_allclose(cpu(d_out[r]).astype(np.float64), exp, atol=3e-3, rtol=2e-3)
+        np.testing.assert_allclose(cpu(d_lse[r]), exp_lse, atol=2e-4, rtol=2e-5)
+
+
+def test_heterogeneous_run_decode_abi(cuda_lib):
+    """scripts/page_gauge_heterogeneous_fa2.py ABI: one table, old pages
+    first (INT8 ids) then exact ring ids; old_kv_len splits them."""
+    from pagegauge_b200 import heterogeneous as H
+    lengths = [2000, 1200]
+    q, dk, dv, cache, tables = make_case(lengths, seed=17)
+    o_ptr, e_ptr = cpu(tables.old_indptr), cpu(tables.exact_indptr)
+    o_idx, e_idx = cpu(tables.old_indices), cpu(tables.exact_indices)
+    unified, indptr = [], [0]
+    for r in range(2):
+        unified += list(o_idx[o_ptr[r]:o_ptr[r + 1]]) + list(e_idx[e_ptr[r]:e_ptr[r + 1]])
+        indptr.append(len(unified))
+    wrapper = H.make_heterogeneous_page_gauge_wrapper(None, workspace())
+    H.plan_decode(wrapper, torch.tensor(indptr, dtype=torch.int32, device="cuda"),
+                  torch.tensor(unified, dtype=torch.int32, device="cuda"), tables.exact_last_page_len,
+                  fixed_split_pages=11)
+    old_kv_len = torch.tensor(tables.old_tokens, dtype=torch.int32, device="cuda")
+    out = H.run_decode(wrapper, q.contiguous(), cache.key_codes, cache.value_codes, cache.key_scales,
+                       cache.value_scales, cache.exact_key, cache.exact_value, old_kv_len,
+                       cache.value_center)
+    torch.cuda.synchronize()
+    for r in range(2):
+        exp, _ = oracle_decode(q, cache, tables, lengths, r)
+        assert_close_decode(out[r], exp)
+    with pytest.raises(ValueError, match="page-aligned"):
+        H.run_decode(wrapper, q.contiguous(), cache.key_codes, cache.value_codes, cache.key_scales,
+                     cache.value_scales, cache.exact_key, cache.exact_value, old_kv_len + 3, cache.value_center)
+
+
+def test_cuda_graph_capture_and_replay(cuda_lib):
+    """plan() outside capture, run() captured once and replayed."""
+    lengths = [4096]
+    q, dk, dv, cache, tables = make_case(lengths, seed=19)
+    dec = PageGaugeDecode(workspace())
+    dec.plan(tables.old_indptr, tables.old_indices, tables.exact_indptr, tables.exact_indices,
+             tables.exact_last_page_len, 32, 8)
+    out = torch.empty_like(q)
+    args = (q, cache.key_codes, cache.value_codes, cache.key_scales, cache.value_scales,
+            cache.exact_key, cache.exact_value, cache.value_center)
+    dec.run(*args, out=out)
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            dec.run(*args, out=out)
+    out.zero_()
+    graph.replay()
+    torch.cuda.synchronize()
+    exp, _ = oracle_decode(q, cache, tables, lengths, 0)
+    assert_close_decode(out[0], exp)
+    del graph
