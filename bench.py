@@ -38,13 +38,15 @@ SEED = 20261001
 def parse_args():
     p = argparse.ArgumentParser(description=__doc__)
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=200)
-    p.add_argument("--warmup", type=int, default=20)
+    p.add_argument("--steps", type=int, default=20000)
+    p.add_argument("--warmup", type=int, default=50)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--workload", choices=("b1_49k", "b8_ragged", "b1_4k"), default="b1_49k")
     p.add_argument("--split", type=int, default=-1,
                    help="pages per work item (-1: measured scheduler table, 0: heuristic)")
     p.add_argument("--layers", type=int, default=4)
+    p.add_argument("--merge", choices=("kernel", "fused"), default="kernel",
+                   help="cross-CTA merge: separate merge kernel or last-CTA merge in the split kernel")
     p.add_argument("--no-cpu-baseline", action="store_true")
     return p.parse_args()
 
@@ -223,24 +225,38 @@ def main() -> None:
     def step(layer: int):
         c = caches[layer]
         dec.run(q, c.key_codes, c.value_codes, c.key_scales, c.value_scales, c.exact_key,
-                c.exact_value, c.value_center, out=out)
+                c.exact_value, c.value_center, out=out, fused_merge=args.merge == "fused")
 
-    # One CUDA graph per layer: the step's two launches replayed without
-    # host overhead (plan stays outside capture, as in the reference).
+    # Steps are captured into CUDA graphs (plan stays outside capture, as in
+    # the reference): one graph of CHUNK consecutive steps cycling the
+    # layers, replayed K // CHUNK times, plus single-step graphs for the
+    # remainder, so host launch overhead is amortised and exactly K steps
+    # are timed on the device.
     stream = torch.cuda.Stream()
-    graphs = []
+    chunk = 8 * layers
     with torch.cuda.stream(stream):
         for layer in range(layers):
             step(layer)
         torch.cuda.synchronize()
+        chunk_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(chunk_graph, stream=stream):
+            for i in range(chunk):
+                step(i % layers)
+        single = []
         for layer in range(layers):
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, stream=stream):
                 step(layer)
-            graphs.append(g)
+            single.append(g)
     torch.cuda.synchronize()
-    for i in range(max(args.warmup, 3)):
-        graphs[i % layers].replay()
+
+    def run_steps(k: int) -> None:
+        for _ in range(k // chunk):
+            chunk_graph.replay()
+        for i in range(k - k % chunk, k):
+            single[i % layers].replay()
+
+    run_steps(max(args.warmup, 3))
     torch.cuda.synchronize()
     if dist is not None:
         dist.barrier()
@@ -248,8 +264,7 @@ def main() -> None:
     with ClockSampler(local) as clocks:
         torch.cuda.synchronize()
         start.record()
-        for i in range(args.steps):
-            graphs[i % layers].replay()
+        run_steps(args.steps)
         end.record()
         torch.cuda.synchronize()
     if dist is not None:
@@ -267,7 +282,6 @@ def main() -> None:
     # graph per layer, timed with events on the replay stream.
     plan = dec.work_plan
     lib_launches = 1 if (plan.single and plan.num_items) else 2
-    kernel_graphs = []
     from pagegauge_b200 import wrapper as W
 
     def decode_only(layer: int):
@@ -288,27 +302,25 @@ def main() -> None:
         a.final_mode = 1 if plan.single else 0
         a.out = out.data_ptr()
         a.out_stride_b, a.out_stride_h = out.stride(0), out.stride(1)
-        a.stage_mask = 1  # split kernel only
+        a.stage_mask = 1  # split kernel only (partials; no fused merge)
         _lib.check(_lib.load().pg_decode_run(ctypes.byref(a), torch.cuda.current_stream().cuda_stream))
 
     with torch.cuda.stream(stream):
-        for layer in range(layers):
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=stream):
-                decode_only(layer)
-            kernel_graphs.append(g)
+        kernel_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(kernel_graph, stream=stream):
+            for i in range(chunk):
+                decode_only(i % layers)
     torch.cuda.synchronize()
-    for i in range(6):
-        kernel_graphs[i % layers].replay()
+    kernel_graph.replay()
     ks, ke = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
+    kreps = max(4, args.steps // chunk)
     ks.record()
-    kreps = max(args.steps, 40)
-    for i in range(kreps):
-        kernel_graphs[i % layers].replay()
+    for _ in range(kreps):
+        kernel_graph.replay()
     ke.record()
     torch.cuda.synchronize()
-    kernel_ms = ks.elapsed_time(ke) / kreps
+    kernel_ms = ks.elapsed_time(ke) / (kreps * chunk)
 
     peaks_path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "MEASURED_PEAKS.json")
     if os.path.exists(peaks_path):
@@ -401,7 +413,7 @@ def main() -> None:
         }
         print(json.dumps(line), flush=True)
     if dist is not None:
-        del graphs, kernel_graphs
+        del chunk_graph, single, kernel_graph
         dist.barrier()
         dist.destroy_process_group()
 

@@ -178,6 +178,11 @@ typedef struct pg_decode_args {
   int64_t vc_stride_b;
   int32_t stage_mask; /* 0 or 3: split + merge; 1: split kernel only;
                          2: merge kernel only (stages on separate calls) */
+  int32_t* merge_sem; /* device [B*Hkv] int32, zero when idle (the planner's
+                         workspace provides it); non-NULL: the split kernel
+                         merges each head in its last CTA (one launch, no
+                         merge kernel).  Launches sharing it must not run
+                         concurrently. */
 } pg_decode_args;
 
 int32_t pg_decode_run(const pg_decode_args* args, void* stream);

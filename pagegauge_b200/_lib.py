@@ -48,6 +48,7 @@ class PgDecodeArgs(ctypes.Structure):
         ("out", c_vp), ("out_stride_b", c_i64), ("out_stride_h", c_i64), ("lse_out", c_vp),
         ("extra_o", c_vp), ("extra_stride_b", c_i64), ("extra_stride_h", c_i64), ("extra_lse", c_vp),
         ("value_center", c_vp), ("vc_stride_b", c_i64), ("stage_mask", c_i32),
+        ("merge_sem", c_vp),
     ]
 
 

@@ -12,7 +12,7 @@
 #include <string>
 #include <vector>
 
-#include "../../include/pagegauge_b200.h"
+#include "pagegauge_b200.h"
 #include "pg_append.cuh"
 #include "pg_decode.cuh"
 
@@ -153,18 +153,31 @@ int32_t launch_decode(const pg::DecodeParams& p, const CUtensorMap& k8,
                       cudaStream_t stream) {
   int32_t rc = ensure_decode_smem();
   if (rc != PG_OK) return rc;
-  pg::pg_decode_split_kernel<<<num_ctas, warps * 32, pg::decode_smem_bytes(warps),
-                               stream>>>(k8, v8, k16, v16, p);
-  return cuda_check(cudaGetLastError(), "decode kernel launch");
+  // Programmatic dependent launch: the kernel's prologue (work item, page
+  // ids, first INT8 tiles) may overlap the tail of the previous kernel in
+  // the stream; it waits for that kernel before reading q or the exact
+  // pages and before writing anything.
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(num_ctas);
+  cfg.blockDim = dim3(warps * 32);
+  cfg.dynamicSmemBytes = pg::decode_smem_bytes(warps);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_check(cudaLaunchKernelEx(&cfg, pg::pg_decode_split_kernel, k8, v8, k16, v16, p),
+                    "decode kernel launch");
 }
 
 // Resident CTAs of the decode kernel per SM at `warps` warps per CTA
 // (shared-memory bound: 228 KB per SM, 1 KB reserved per CTA; at most
-// 2048 threads and 64 K registers at 128 registers per thread).
+// 2048 threads and 64 K registers at up to 168 registers per thread).
 int pg_ctas_per_sm(int warps) {
   const int by_smem = (228 * 1024) / (pg::decode_smem_bytes(warps) + 1024);
   const int by_threads = 2048 / (warps * 32);
-  const int by_regs = 65536 / (warps * 32 * 128);
+  const int by_regs = 65536 / (warps * 32 * 168);
   return std::max(1, std::min(by_smem, std::min(by_threads, by_regs)));
 }
 
@@ -370,6 +383,8 @@ int32_t pg_exact_tail_merge_center(
   p.value_center = static_cast<const __half*>(value_center);
   p.vc_stride_b = center_batch_stride;
   p.implicit_pages = static_cast<int32_t>(n);
+  p.sem = nullptr;
+  p.item_off = nullptr;
   p.error_flag = device_error_ptr();
   CUtensorMap k16, v16, none;
   std::memset(&none, 0, sizeof(none));
@@ -423,7 +438,7 @@ int32_t pg_decode_plan(int32_t batch, int32_t kv_heads, const int32_t* indptr0,
     constexpr double kOverheadPages = 8.0;  // ~2 us of CTA start-up at 15 GB/s
     double best_cost = 1e300;
     int best = 1;
-    for (int64_t c = 1; c <= max_n; c = c < 64 ? c + 1 : c + c / 32) {
+    for (int64_t c = 1; c <= std::min<int64_t>(max_n, 32 * W); c = c < 64 ? c + 1 : c + c / 32) {
       const int64_t c0 = split[0] ? split[0] : c;
       const int64_t c1 = split[1] ? split[1] : std::max<int64_t>(1, c / 2);
       int64_t items = 0;
@@ -448,6 +463,10 @@ int32_t pg_decode_plan(int32_t batch, int32_t kv_heads, const int32_t* indptr0,
     if (split[0] == 0) split[0] = best;
     if (split[1] == 0) split[1] = std::max(1, best / 2);
   }
+  // At most 32 pages per warp: the kernel keeps a warp's page ids and scales
+  // in one register window.
+  split[0] = std::min(split[0], 32 * W);
+  split[1] = std::min(split[1], 32 * W);
   int64_t count = 0;
   int32_t max_per_head = 0;
   bool single = true;
@@ -548,6 +567,10 @@ int32_t pg_decode_run(const pg_decode_args* a, void* stream) {
   p.vc_stride_b = a->vc_stride_b;
   p.implicit_pages = 0;
   p.error_flag = device_error_ptr();
+  const bool fused = a->merge_sem != nullptr && !a->final_mode;
+  p.sem = fused ? a->merge_sem : nullptr;
+  p.item_off = a->item_off;
+  if (fused) PG_REQUIRE(a->item_off != nullptr, "the fused merge needs item offsets");
   if (a->extra_o != nullptr) PG_REQUIRE(a->extra_lse != nullptr, "extra state needs its lse");
 
   const int mask = (a->stage_mask & 3) == 0 ? 3 : (a->stage_mask & 3);
@@ -560,6 +583,7 @@ int32_t pg_decode_run(const pg_decode_args* a, void* stream) {
     if (rc != PG_OK) return rc;
   }
   if (a->final_mode && a->num_items > 0) return PG_OK;
+  if (fused && a->num_items > 0 && (mask & 1)) return PG_OK;
   if (!(mask & 2)) return PG_OK;
 
   PG_REQUIRE(a->item_off != nullptr, "item offsets are required for the merge");
@@ -582,7 +606,7 @@ int32_t pg_decode_run(const pg_decode_args* a, void* stream) {
   m.vc_stride_b = a->vc_stride_b;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(a->batch * a->kv_heads * a->group);
-  cfg.blockDim = dim3(128);
+  cfg.blockDim = dim3(pg::kMergeWarps * 32);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];

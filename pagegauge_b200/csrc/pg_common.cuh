@@ -57,23 +57,26 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar,
 }
 
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  // The suspend-time hint lets the hardware park the warp until the phase
+  // completes (or ~20 us pass) instead of spinning through issue slots.
   uint32_t done;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(done)
-      : "r"(smem_addr(bar)), "r"(parity)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(20000u)
       : "memory");
   return done != 0;
 }
 
-// Bounded wait.  try_wait already suspends the thread for a hardware-defined
-// window, so 1<<22 polls is far beyond any legitimate TMA latency (seconds).
-// Returns false when the bound is hit; the caller records an error.
+// Bounded wait: at most 2^18 suspended polls (seconds), far beyond any
+// legitimate TMA latency.  Returns false when the bound is hit; the caller
+// records an error and skips the work.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar,
                                                   uint32_t parity) {
-  for (uint32_t i = 0; i < (1u << 22); ++i) {
+  if (mbar_try_wait(bar, parity)) return true;
+  for (uint32_t i = 0; i < (1u << 18); ++i) {
     if (mbar_try_wait(bar, parity)) return true;
   }
   return false;
@@ -94,6 +97,18 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map,
       : "memory");
 }
 
+// Bulk tensor prefetch of a tile into L2 only (no shared memory, no
+// completion tracking): pages further ahead than the shared-memory ring can
+// hold are pulled into L2 so the ring's loads hit L2.
+__device__ __forceinline__ void tma_prefetch_l2_3d(const CUtensorMap* map, int c0,
+                                                   int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(
                    reinterpret_cast<uint64_t>(map))
@@ -104,7 +119,7 @@ __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
 // D = A(16x16 f16, row) * B(16x8 f16, col) + D, fp32 accumulate.
 __device__ __forceinline__ void mma_16816(float* d, const uint32_t* a,
                                           uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
       "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -126,10 +141,19 @@ __device__ __forceinline__ uint32_t hsub2_u32(uint32_t a, uint32_t b) {
 
 // Signed INT8 -> FP16 without a conversion instruction: a byte u placed in
 // the low mantissa bits of 0x64xx is the half 1024 + u.  With u = z ^ 0x80
-// (= z + 128 mod 256) the value is z + 1152, and one f16x2 subtraction of
-// 1152 (exact in FP16) recovers z exactly for every z in [-128, 127].
+// (= z + 128 mod 256) the value is z + 1152 exactly, for every z in
+// [-128, 127]; the constant bias is removed after the matrix product.
 constexpr uint32_t kMagic = 0x64646464u;
-constexpr uint32_t kBias2 = 0x64806480u;  // half2(1152, 1152)
+
+// Bytes 0 and 2 of w as the biased half2 (z0 + 1152, z2 + 1152): sign-flip,
+// mask and exponent in one bitwise select (a single LOP3).
+__device__ __forceinline__ uint32_t biased_half2_even(uint32_t w) {
+  return ((w ^ 0x64806480u) & 0x00ff00ffu) | (0x64806480u & 0xff00ff00u);
+}
+// Bytes 1 and 3 of w (shift + LOP3).
+__device__ __forceinline__ uint32_t biased_half2_odd(uint32_t w) {
+  return biased_half2_even(w >> 8);
+}
 
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
@@ -163,12 +187,23 @@ __device__ __forceinline__ float warp_sum_xor_g(float v) {
   return v;
 }
 
-__device__ __forceinline__ uint4 lds128(uint32_t addr) {
-  uint4 v;
-  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "r"(addr));
-  return v;
+// 16-byte shared-memory load through a plain pointer, so the compiler can
+// schedule it freely between the mma/permute instructions while still
+// ordering it after the mbarrier wait (which clobbers memory).
+__device__ __forceinline__ uint4 lds128(const uint8_t* base, uint32_t offset) {
+  return *reinterpret_cast<const uint4*>(base + offset);
+}
+
+// Four transposed 8x8 b16 matrices from shared memory; lane l supplies
+// the address of row l%8 of matrix l/8 and receives, for matrix j, the
+// elements (row 2(l%4), col l/4) and (row 2(l%4)+1, col l/4).
+__device__ __forceinline__ void ldsm_x4_trans(const uint8_t* addr, uint32_t& r0,
+                                              uint32_t& r1, uint32_t& r2,
+                                              uint32_t& r3) {
+  asm volatile(
+      "ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+      : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+      : "r"(smem_addr(addr)));
 }
 
 // Programmatic dependent launch controls (no-ops when launched normally).

@@ -68,12 +68,18 @@ struct DecodeParams {
   // items == null: implicit list, CTA b = (request b / Hkv, head b % Hkv)
   // over `implicit_pages` FP16 pages starting at request * implicit_pages.
   int32_t implicit_pages;
+  // Fused cross-CTA merge (partial mode): per-(request, head) arrival
+  // counters (zero between launches) and the item ranges of each head.  The
+  // last CTA of a head merges its partial states into out / lse_out.
+  int32_t* sem;
+  const int32_t* item_off;
   int* error_flag;
 };
 
 constexpr int kStagesI8 = 4;              // INT8 stages per warp
 constexpr int kRingBytes = kStagesI8 * 4096;
 constexpr int kMaxWarps = 8;
+constexpr int kCoStride = 132;  // padded row of the CTA combine buffer
 
 __host__ __device__ constexpr int decode_smem_bytes(int warps) {
   return warps * kRingBytes + warps * kStagesI8 * 8 + 1024;
@@ -82,20 +88,38 @@ __host__ __device__ constexpr int decode_smem_bytes(int warps) {
 // Output dimension held by accumulator row (m-tile i, row g / g+8).
 template <int SEG>
 __device__ __forceinline__ int out_dim(int i, int g, int odd) {
-  if (SEG == 0) return 16 * g + 2 * i + odd;
+  if (SEG == 0) return 16 * i + 2 * g + odd;
   return 64 * (i >> 2) + 8 * g + 2 * (i & 3) + odd;
 }
 
 struct WarpState {
-  float m0, m1, l0, l1;
-  float o[32];
-  float sref;
+  float m0, m1, l0, l1;  // running max / sum for query rows 2t, 2t+1
+  float o[32];           // O^T accumulator: 8 m-tiles x (rows g, g+8) x 2 q
+  float o1[4];           // "ones" row: sum of the FP16 P'' fed to the PV mma
+  float sref;            // reference V scale (INT8 segment)
 };
+
+// Q for the INT8 segment as two int8 parts per row, q ~ sq * (hi + lo/254)
+// with sq = max|q_row| / 127 (|error| <= sq/508).  Q is the A operand of
+// mma.m16n8k32.s8: rows 0-7 hold the hi parts of the GQA query rows, rows
+// 8-15 the lo parts, so one mma yields both partial dot products of a
+// query row in the same thread.  a[ks] = {hi dims 32t+8ks+0..3, lo same,
+// hi dims 32t+8ks+4..7, lo same} of query row g (the B operand, K, uses
+// the identical dimension order).
+struct QInt8 {
+  uint32_t a[4][4];
+  float c;  // sq(row g) / 254 * sm_scale * log2(e)
+};
+
+// A page's scores may exceed the running reference max by this many log2
+// units before the output is rescaled (P <= 2^8 stays exact-range in FP16).
+constexpr float kRescaleSlack = 8.f;
 
 // Page-id / scale window: lane L of set A holds warp-page base+L, set B
 // holds base+32+L.  Shuffles fetch the value of any page in [base, base+64).
 struct PageWindow {
   int base;
+  bool two;  // more than 32 pages: set B is live
   int id_a, id_b;
   float sk_a, sk_b, sv_a, sv_b;
 };
@@ -127,74 +151,128 @@ __device__ __forceinline__ void load_window_set(const DecodeParams& p,
 __device__ __forceinline__ int win_id(const PageWindow& w, int u) {
   const int k = u - w.base;
   const int a = __shfl_sync(0xffffffffu, w.id_a, k & 31);
+  if (!w.two) return a;
   const int b = __shfl_sync(0xffffffffu, w.id_b, k & 31);
   return k < 32 ? a : b;
 }
-__device__ __forceinline__ float win_f(float fa, float fb, int k) {
+__device__ __forceinline__ float win_f(const PageWindow& w, float fa, float fb, int k) {
   const float a = __shfl_sync(0xffffffffu, fa, k & 31);
+  if (!w.two) return a;
   const float b = __shfl_sync(0xffffffffu, fb, k & 31);
   return k < 32 ? a : b;
 }
 
-// Q^T fragments (mma B operand) with the same dimension permutation the K
-// fragments use, so the contraction over head_dim is unchanged.
-template <int SEG>
-__device__ __forceinline__ void load_q_frag(const DecodeParams& p, int r,
-                                            int h, int g, int t,
-                                            uint32_t* qf) {
+// FP16 Q^T fragments (mma B operand) for the FP16 segment, with the same
+// dimension permutation the K fragments use.
+__device__ __forceinline__ void load_q_fp16(const DecodeParams& p, int r, int h,
+                                            int g, int t, uint32_t* qf) {
   if (g >= p.group) {
 #pragma unroll
     for (int i = 0; i < 16; ++i) qf[i] = 0u;
     return;
   }
-  const __half* qrow =
+  const uint32_t* q32 = reinterpret_cast<const uint32_t*>(
       p.q + static_cast<int64_t>(r) * p.q_stride_b +
-      static_cast<int64_t>(h * p.group + g) * p.q_stride_h;
-  const uint32_t* q32 = reinterpret_cast<const uint32_t*>(qrow);
-  if (SEG == 0) {
-    // thread t covers dims [32t, 32t+32); k-step ks uses dims 32t+4ks..+3
+      static_cast<int64_t>(h * p.group + g) * p.q_stride_h);
+  const int R = t >> 1;
+  const int cb = 4 * (t & 1);
 #pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {
-      qf[2 * ks] = __ldg(q32 + (32 * t + 4 * ks) / 2);
-      qf[2 * ks + 1] = __ldg(q32 + (32 * t + 4 * ks + 2) / 2);
-    }
-  } else {
-    const int R = t >> 1;
-    const int cb = 4 * (t & 1);
-#pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {
-      const int j = ks >> 1, e = ks & 1;
-      const int c = cb + ((j + 2 * R) & 3);
-      const int d = 64 * R + 8 * c + 4 * e;
-      qf[2 * ks] = __ldg(q32 + d / 2);
-      qf[2 * ks + 1] = __ldg(q32 + (d + 2) / 2);
-    }
+  for (int ks = 0; ks < 8; ++ks) {
+    const int j = ks >> 1, e = ks & 1;
+    const int c = cb + ((j + 2 * R) & 3);
+    const int d = 64 * R + 8 * c + 4 * e;
+    qf[2 * ks] = __ldg(q32 + d / 2);
+    qf[2 * ks + 1] = __ldg(q32 + (d + 2) / 2);
   }
 }
 
-// Online-softmax update for one 16-token page given raw fp32 scores.
-// Returns the packed P^T fragments (pb0, pb1) for the PV mma.
-__device__ __forceinline__ void softmax_page(WarpState& st, float* s, float r,
-                                             int g, int t, int group,
-                                             uint32_t& pb0, uint32_t& pb1) {
-  float mx0 = warp_max_xor_g(fmaxf(s[0], s[2]));
-  float mx1 = warp_max_xor_g(fmaxf(s[1], s[3]));
-  const float mn0 = fmaxf(st.m0, mx0);
-  const float mn1 = fmaxf(st.m1, mx1);
-  const float ref0 = mn0 == kNegInf ? 0.f : mn0;
-  const float ref1 = mn1 == kNegInf ? 0.f : mn1;
-  const float a0 = fast_exp2(st.m0 - ref0);
-  const float a1 = fast_exp2(st.m1 - ref1);
-  const float p0 = fast_exp2(s[0] - ref0);
-  const float p1 = fast_exp2(s[1] - ref1);
-  const float p2 = fast_exp2(s[2] - ref0);
-  const float p3 = fast_exp2(s[3] - ref1);
-  st.l0 = st.l0 * a0 + (p0 + p2);
-  st.l1 = st.l1 * a1 + (p1 + p3);
-  st.m0 = mn0;
-  st.m1 = mn1;
-  // Rescale the running output only when some row's maximum moved.
-  if (__any_sync(0xffffffffu, (a0 != 1.f) || (a1 != 1.f))) {
+__device__ __forceinline__ uint32_t pack_s8x4(int a, int b, int c, int d) {
+  return (static_cast<uint32_t>(a) & 0xffu) | ((static_cast<uint32_t>(b) & 0xffu) << 8) |
+         ((static_cast<uint32_t>(c) & 0xffu) << 16) | (static_cast<uint32_t>(d) << 24);
+}
+
+__device__ __forceinline__ int clamp127(int v) { return v < -127 ? -127 : (v > 127 ? 127 : v); }
+
+// Two-part int8 Q for the INT8 segment (thread t owns dims [32t, 32t+32)).
+__device__ __forceinline__ void load_q_int8(const DecodeParams& p, int r, int h,
+                                            int g, int t, QInt8& qi) {
+  float qv[32];
+  if (g < p.group) {
+    const __half2* q2 = reinterpret_cast<const __half2*>(
+        p.q + static_cast<int64_t>(r) * p.q_stride_b +
+        static_cast<int64_t>(h * p.group + g) * p.q_stride_h + 32 * t);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float2 f = __half22float2(q2[i]);
+      qv[2 * i] = f.x;
+      qv[2 * i + 1] = f.y;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) qv[i] = 0.f;
+  }
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(qv[i]));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+  const float sq = amax > 0.f ? amax / 127.f : 1.f;
+  const float inv = 1.f / sq;
+  const float inv_lo = 254.f / sq;
+#pragma unroll
+  for (int ks = 0; ks < 4; ++ks) {
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      int hv[4], lv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float x = qv[8 * ks + 4 * half + i];
+        const int hi = clamp127(__float2int_rn(x * inv));
+        const float rem = fmaf(-static_cast<float>(hi), sq, x);
+        hv[i] = hi;
+        lv[i] = clamp127(__float2int_rn(rem * inv_lo));
+      }
+      qi.a[ks][2 * half] = pack_s8x4(hv[0], hv[1], hv[2], hv[3]);
+      qi.a[ks][2 * half + 1] = pack_s8x4(lv[0], lv[1], lv[2], lv[3]);
+    }
+  }
+  qi.c = sq * (p.sm_scale_log2 / 254.f);
+}
+
+__device__ __forceinline__ void mma_s8_16832(int* d, const uint32_t* a,
+                                             uint32_t b0, uint32_t b1) {
+  asm(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Online-softmax update for NP 16-token pages given scaled scores (log2
+// units, s[4*i .. 4*i+3] for page i).  The running reference max is only
+// raised when some score exceeds it by more than kRescaleSlack, so most
+// pages need no cross-lane max and no output rescale.  Returns the packed
+// P^T fragments of every page (V scale ratio r[i] folded in).
+template <int NP>
+__device__ __forceinline__ void softmax_pages(WarpState& st, const float* s,
+                                              const float* r, int g, int t,
+                                              int group, uint32_t* pb0,
+                                              uint32_t* pb1) {
+  float lm0 = fmaxf(s[0], s[2]);
+  float lm1 = fmaxf(s[1], s[3]);
+#pragma unroll
+  for (int i = 1; i < NP; ++i) {
+    lm0 = fmaxf(lm0, fmaxf(s[4 * i + 0], s[4 * i + 2]));
+    lm1 = fmaxf(lm1, fmaxf(s[4 * i + 1], s[4 * i + 3]));
+  }
+  const bool need = (lm0 > st.m0 + kRescaleSlack) || (lm1 > st.m1 + kRescaleSlack);
+  if (__any_sync(0xffffffffu, need)) {
+    const float mn0 = fmaxf(st.m0, warp_max_xor_g(lm0));
+    const float mn1 = fmaxf(st.m1, warp_max_xor_g(lm1));
+    const float a0 = mn0 == kNegInf ? 1.f : fast_exp2(st.m0 - mn0);  // -inf -> 0
+    const float a1 = mn1 == kNegInf ? 1.f : fast_exp2(st.m1 - mn1);
+    st.l0 *= a0;
+    st.l1 *= a1;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       st.o[4 * i + 0] *= a0;
@@ -202,113 +280,187 @@ __device__ __forceinline__ void softmax_page(WarpState& st, float* s, float r,
       st.o[4 * i + 2] *= a0;
       st.o[4 * i + 3] *= a1;
     }
+    st.o1[0] *= a0;
+    st.o1[1] *= a1;
+    st.o1[2] *= a0;
+    st.o1[3] *= a1;
+    st.m0 = mn0;
+    st.m1 = mn1;
   }
-  const uint32_t h01 = pack_half2(p0 * r, p1 * r);
-  const uint32_t h23 = pack_half2(p2 * r, p3 * r);
+  const float ref0 = st.m0 == kNegInf ? 0.f : st.m0;
+  const float ref1 = st.m1 == kNegInf ? 0.f : st.m1;
   const int src0 = 8 * t + (g >> 1);
   const int src1 = src0 + 4;
-  const uint32_t x01 = __shfl_sync(0xffffffffu, h01, src0);
-  const uint32_t y01 = __shfl_sync(0xffffffffu, h01, src1);
-  const uint32_t x23 = __shfl_sync(0xffffffffu, h23, src0);
-  const uint32_t y23 = __shfl_sync(0xffffffffu, h23, src1);
   const uint32_t sel = (g & 1) ? 0x7632u : 0x5410u;
-  pb0 = prmt(x01, y01, sel);
-  pb1 = prmt(x23, y23, sel);
-  if (g >= group) {
-    pb0 = 0u;
-    pb1 = 0u;
+#pragma unroll
+  for (int i = 0; i < NP; ++i) {
+    const float p0 = fast_exp2(s[4 * i + 0] - ref0);
+    const float p1 = fast_exp2(s[4 * i + 1] - ref1);
+    const float p2 = fast_exp2(s[4 * i + 2] - ref0);
+    const float p3 = fast_exp2(s[4 * i + 3] - ref1);
+    st.l0 += p0 + p2;
+    st.l1 += p1 + p3;
+    const uint32_t h01 = pack_half2(p0 * r[i], p1 * r[i]);
+    const uint32_t h23 = pack_half2(p2 * r[i], p3 * r[i]);
+    const uint32_t x01 = __shfl_sync(0xffffffffu, h01, src0);
+    const uint32_t y01 = __shfl_sync(0xffffffffu, h01, src1);
+    const uint32_t x23 = __shfl_sync(0xffffffffu, h23, src0);
+    const uint32_t y23 = __shfl_sync(0xffffffffu, h23, src1);
+    pb0[i] = g < group ? prmt(x01, y01, sel) : 0u;
+    pb1[i] = g < group ? prmt(x23, y23, sel) : 0u;
   }
 }
 
-// One INT8 page: K tile at st_addr, V tile at st_addr + 2048 (both 16 rows
-// of 128 bytes, 128B-swizzled by row).
-__device__ __forceinline__ void page_int8(WarpState& st, uint32_t st_addr,
-                                          const uint32_t* qf, float kscale,
-                                          float r, int valid, int g, int t,
-                                          int group) {
-  float s[4] = {0.f, 0.f, 0.f, 0.f};
-  {
-    const uint32_t rg = st_addr + g * 128;
-    const uint32_t rh = st_addr + (g + 8) * 128;
-    const uint32_t c0 = static_cast<uint32_t>((2 * t) ^ g) << 4;
-    const uint32_t c1 = static_cast<uint32_t>((2 * t + 1) ^ g) << 4;
-    const uint4 kg0 = lds128(rg + c0);
-    const uint4 kg1 = lds128(rg + c1);
-    const uint4 kh0 = lds128(rh + c0);
-    const uint4 kh1 = lds128(rh + c1);
-    const uint32_t wg[8] = {kg0.x, kg0.y, kg0.z, kg0.w,
-                            kg1.x, kg1.y, kg1.z, kg1.w};
-    const uint32_t wh[8] = {kh0.x, kh0.y, kh0.z, kh0.w,
-                            kh1.x, kh1.y, kh1.z, kh1.w};
-#pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {
-      const uint32_t xg = wg[ks] ^ 0x80808080u;
-      const uint32_t xh = wh[ks] ^ 0x80808080u;
-      uint32_t a[4];
-      a[0] = hsub2_u32(prmt(xg, kMagic, 0x4140u), kBias2);
-      a[1] = hsub2_u32(prmt(xh, kMagic, 0x4140u), kBias2);
-      a[2] = hsub2_u32(prmt(xg, kMagic, 0x4342u), kBias2);
-      a[3] = hsub2_u32(prmt(xh, kMagic, 0x4342u), kBias2);
-      mma_16816(s, a, qf[2 * ks], qf[2 * ks + 1]);
-    }
-  }
-#pragma unroll
-  for (int i = 0; i < 4; ++i) s[i] *= kscale;
+// INT8 QK scores of one page for query row g: K tile at stage (16 rows of
+// 128 bytes, 128B-swizzled by row) is the B operand straight from shared
+// memory (n-tile 0 = tokens 0-7, n-tile 1 = tokens 8-15); the accumulator
+// rows g / g+8 carry the hi / lo parts.  s[] = tokens 2t, 2t+1, 8+2t, 9+2t
+// in log2 units (masked tokens -inf).
+__device__ __forceinline__ void qk_int8(const uint8_t* stage, const QInt8& qi,
+                                        float sk, int valid, int g, int t,
+                                        float* s) {
+  const uint32_t rg = g * 128;
+  const uint32_t rh = (g + 8) * 128;
+  const uint32_t c0 = static_cast<uint32_t>((2 * t) ^ g) << 4;
+  const uint32_t c1 = static_cast<uint32_t>((2 * t + 1) ^ g) << 4;
+  const uint4 kg0 = lds128(stage, rg + c0);
+  const uint4 kg1 = lds128(stage, rg + c1);
+  const uint4 kh0 = lds128(stage, rh + c0);
+  const uint4 kh1 = lds128(stage, rh + c1);
+  int c_lo[4] = {0, 0, 0, 0}, c_hi[4] = {0, 0, 0, 0};  // n-tile 0 / 1
+  mma_s8_16832(c_lo, qi.a[0], kg0.x, kg0.y);
+  mma_s8_16832(c_hi, qi.a[0], kh0.x, kh0.y);
+  mma_s8_16832(c_lo, qi.a[1], kg0.z, kg0.w);
+  mma_s8_16832(c_hi, qi.a[1], kh0.z, kh0.w);
+  mma_s8_16832(c_lo, qi.a[2], kg1.x, kg1.y);
+  mma_s8_16832(c_hi, qi.a[2], kh1.x, kh1.y);
+  mma_s8_16832(c_lo, qi.a[3], kg1.z, kg1.w);
+  mma_s8_16832(c_hi, qi.a[3], kh1.z, kh1.w);
+  const float e = qi.c * sk;
+  s[0] = static_cast<float>(c_lo[0] * 254 + c_lo[2]) * e;
+  s[1] = static_cast<float>(c_lo[1] * 254 + c_lo[3]) * e;
+  s[2] = static_cast<float>(c_hi[0] * 254 + c_hi[2]) * e;
+  s[3] = static_cast<float>(c_hi[1] * 254 + c_hi[3]) * e;
   if (valid < kPage) {
-    if (g >= valid) s[0] = s[1] = kNegInf;
-    if (g + 8 >= valid) s[2] = s[3] = kNegInf;
+    if (2 * t >= valid) s[0] = kNegInf;
+    if (2 * t + 1 >= valid) s[1] = kNegInf;
+    if (2 * t + 8 >= valid) s[2] = kNegInf;
+    if (2 * t + 9 >= valid) s[3] = kNegInf;
   }
-  uint32_t pb0, pb1;
-  softmax_page(st, s, r, g, t, group, pb0, pb1);
-  {
-    const uint32_t vbase = st_addr + 2048;
-    const uint32_t ta = 2 * t, tb = 2 * t + 1;
-    const uint4 va = lds128(vbase + ta * 128 + ((g ^ ta) << 4));
-    const uint4 vb = lds128(vbase + tb * 128 + ((g ^ tb) << 4));
-    const uint4 vc = lds128(vbase + (ta + 8) * 128 + ((g ^ ta) << 4));
-    const uint4 vd = lds128(vbase + (tb + 8) * 128 + ((g ^ tb) << 4));
-    const uint32_t wa[4] = {va.x, va.y, va.z, va.w};
-    const uint32_t wb[4] = {vb.x, vb.y, vb.z, vb.w};
-    const uint32_t wc[4] = {vc.x, vc.y, vc.z, vc.w};
-    const uint32_t wd[4] = {vd.x, vd.y, vd.z, vd.w};
+}
+
+// Online softmax for query row g over NP pages (INT8 path).  The reference
+// max m0 / sum l0 of row g live in the four lanes of groupID g.  The
+// output accumulator holds rows 2t / 2t+1, whose rescale factors are
+// fetched from those rows' lanes on the (rare) rescale path.
+template <int NP>
+__device__ __forceinline__ void softmax_rowg(WarpState& st, const float* s,
+                                             const float* r, int t,
+                                             uint32_t* pb0, uint32_t* pb1) {
+  float lm = s[0];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const uint32_t x = wa[k] ^ 0x80808080u, y = wb[k] ^ 0x80808080u;
-      const uint32_t z = wc[k] ^ 0x80808080u, w = wd[k] ^ 0x80808080u;
-      const uint32_t lo_ab = prmt(x, y, 0x5140u), hi_ab = prmt(x, y, 0x7362u);
-      const uint32_t lo_cd = prmt(z, w, 0x5140u), hi_cd = prmt(z, w, 0x7362u);
-      uint32_t a[4];
-      a[0] = hsub2_u32(prmt(lo_ab, kMagic, 0x4140u), kBias2);
-      a[1] = hsub2_u32(prmt(lo_ab, kMagic, 0x4342u), kBias2);
-      a[2] = hsub2_u32(prmt(lo_cd, kMagic, 0x4140u), kBias2);
-      a[3] = hsub2_u32(prmt(lo_cd, kMagic, 0x4342u), kBias2);
-      mma_16816(st.o + 4 * (2 * k), a, pb0, pb1);
-      a[0] = hsub2_u32(prmt(hi_ab, kMagic, 0x4140u), kBias2);
-      a[1] = hsub2_u32(prmt(hi_ab, kMagic, 0x4342u), kBias2);
-      a[2] = hsub2_u32(prmt(hi_cd, kMagic, 0x4140u), kBias2);
-      a[3] = hsub2_u32(prmt(hi_cd, kMagic, 0x4342u), kBias2);
-      mma_16816(st.o + 4 * (2 * k + 1), a, pb0, pb1);
+  for (int i = 1; i < 4 * NP; ++i) lm = fmaxf(lm, s[i]);
+  if (__any_sync(0xffffffffu, lm > st.m0 + kRescaleSlack)) {
+    lm = fmaxf(lm, __shfl_xor_sync(0xffffffffu, lm, 1));
+    lm = fmaxf(lm, __shfl_xor_sync(0xffffffffu, lm, 2));
+    const float mn = fmaxf(st.m0, lm);
+    const float a = mn == kNegInf ? 1.f : fast_exp2(st.m0 - mn);  // -inf -> 0
+    st.l0 *= a;
+    st.m0 = mn;
+    const float a0 = __shfl_sync(0xffffffffu, a, 8 * t);
+    const float a1 = __shfl_sync(0xffffffffu, a, 8 * t + 4);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      st.o[4 * i + 0] *= a0;
+      st.o[4 * i + 1] *= a1;
+      st.o[4 * i + 2] *= a0;
+      st.o[4 * i + 3] *= a1;
     }
+    st.o1[0] *= a0;
+    st.o1[1] *= a1;
+    st.o1[2] *= a0;
+    st.o1[3] *= a1;
   }
+  const float ref = st.m0 == kNegInf ? 0.f : st.m0;
+#pragma unroll
+  for (int i = 0; i < NP; ++i) {
+    const float p0 = fast_exp2(s[4 * i + 0] - ref);
+    const float p1 = fast_exp2(s[4 * i + 1] - ref);
+    const float p2 = fast_exp2(s[4 * i + 2] - ref);
+    const float p3 = fast_exp2(s[4 * i + 3] - ref);
+    st.l0 += (p0 + p1) + (p2 + p3);
+    pb0[i] = pack_half2(p0 * r[i], p1 * r[i]);
+    pb1[i] = pack_half2(p2 * r[i], p3 * r[i]);
+  }
+}
+
+// INT8 PV of one page: V tile at stage + 2048.  ldmatrix.trans on the
+// 16-bit view of the tile hands each lane the byte pairs (dims 2d, 2d+1) of
+// tokens (2t, 2t+1) (and +8), so one bitwise select per register yields
+// the FP16 A operand of O^T += V^T P^T for m-tile i: row g = dim 16i+2g,
+// row g+8 = dim 16i+2g+1.  The PV mma runs on the biased codes z + 1152
+// (exact); the bias is removed once at the end through the "ones" row
+// that accumulates sum(P).  vaddr[k] = this lane's ldmatrix row offset for
+// the m-tile pair {2k, 2k+1}.
+__device__ __forceinline__ void pv_int8(WarpState& st, const uint8_t* stage,
+                                        const uint32_t* vaddr, uint32_t pb0,
+                                        uint32_t pb1, int g) {
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    uint32_t r0, r1, r2, r3;  // (tok 0-7, m-tile 2k) (tok 8-15, 2k) (0-7, 2k+1) (8-15, 2k+1)
+    ldsm_x4_trans(stage + 2048 + vaddr[k], r0, r1, r2, r3);
+    uint32_t a[4];
+    a[0] = biased_half2_even(r0);
+    a[1] = biased_half2_odd(r0);
+    a[2] = biased_half2_even(r1);
+    a[3] = biased_half2_odd(r1);
+    mma_16816(st.o + 4 * (2 * k), a, pb0, pb1);
+    a[0] = biased_half2_even(r2);
+    a[1] = biased_half2_odd(r2);
+    a[2] = biased_half2_even(r3);
+    a[3] = biased_half2_odd(r3);
+    mma_16816(st.o + 4 * (2 * k + 1), a, pb0, pb1);
+  }
+  const uint32_t one = g == 0 ? 0x3c003c00u : 0u;
+  const uint32_t ones[4] = {one, 0u, one, 0u};
+  mma_16816(st.o1, ones, pb0, pb1);
+}
+
+// NP INT8 pages at once: the pages' QK chains, softmax work and PV chains
+// are independent, which gives each warp the instruction-level parallelism
+// that a single page's dependency chain lacks.
+template <int NP>
+__device__ __forceinline__ void pages_int8(WarpState& st,
+                                           const uint8_t* const* stages,
+                                           const QInt8& qi, const float* sk,
+                                           const float* r, const int* valid,
+                                           int g, int t, const uint32_t* vaddr) {
+  float s[4 * NP];
+#pragma unroll
+  for (int i = 0; i < NP; ++i) qk_int8(stages[i], qi, sk[i], valid[i], g, t, s + 4 * i);
+  uint32_t pb0[NP], pb1[NP];
+  softmax_rowg<NP>(st, s, r, t, pb0, pb1);
+#pragma unroll
+  for (int i = 0; i < NP; ++i) pv_int8(st, stages[i], vaddr, pb0[i], pb1[i], g);
 }
 
 // One FP16 page: K dims 0-63 at st_addr, 64-127 at +2048; V likewise at
 // +4096 / +6144.  Each region is 16 rows of 128 bytes, 128B-swizzled.
-__device__ __forceinline__ void page_fp16(WarpState& st, uint32_t st_addr,
+__device__ __forceinline__ void page_fp16(WarpState& st, const uint8_t* stage,
                                           const uint32_t* qf, float sscale,
                                           int valid, int g, int t, int group) {
   float s[4] = {0.f, 0.f, 0.f, 0.f};
   {
     const int R = t >> 1;
     const int cb = 4 * (t & 1);
-    const uint32_t rg = st_addr + R * 2048 + g * 128;
+    const uint32_t rg = R * 2048 + g * 128;
     const uint32_t rh = rg + 8 * 128;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const uint32_t c = static_cast<uint32_t>(cb + ((j + 2 * R) & 3));
       const uint32_t off = (c ^ static_cast<uint32_t>(g)) << 4;
-      const uint4 kg = lds128(rg + off);
-      const uint4 kh = lds128(rh + off);
+      const uint4 kg = lds128(stage, rg + off);
+      const uint4 kh = lds128(stage, rh + off);
       uint32_t a[4];
       a[0] = kg.x;
       a[1] = kh.x;
@@ -329,16 +481,17 @@ __device__ __forceinline__ void page_fp16(WarpState& st, uint32_t st_addr,
     if (g + 8 >= valid) s[2] = s[3] = kNegInf;
   }
   uint32_t pb0, pb1;
-  softmax_page(st, s, 1.f, g, t, group, pb0, pb1);
+  const float one_r = 1.f;
+  softmax_pages<1>(st, s, &one_r, g, t, group, &pb0, &pb1);
   {
     const uint32_t ta = 2 * t, tb = 2 * t + 1;
 #pragma unroll
     for (int R = 0; R < 2; ++R) {
-      const uint32_t vbase = st_addr + 4096 + R * 2048;
-      const uint4 va = lds128(vbase + ta * 128 + ((g ^ ta) << 4));
-      const uint4 vb = lds128(vbase + tb * 128 + ((g ^ tb) << 4));
-      const uint4 vc = lds128(vbase + (ta + 8) * 128 + ((g ^ ta) << 4));
-      const uint4 vd = lds128(vbase + (tb + 8) * 128 + ((g ^ tb) << 4));
+      const uint32_t vbase = 4096 + R * 2048;
+      const uint4 va = lds128(stage, vbase + ta * 128 + ((g ^ ta) << 4));
+      const uint4 vb = lds128(stage, vbase + tb * 128 + ((g ^ tb) << 4));
+      const uint4 vc = lds128(stage, vbase + (ta + 8) * 128 + ((g ^ ta) << 4));
+      const uint4 vd = lds128(stage, vbase + (tb + 8) * 128 + ((g ^ tb) << 4));
       const uint32_t wa[4] = {va.x, va.y, va.z, va.w};
       const uint32_t wb[4] = {vb.x, vb.y, vb.z, vb.w};
       const uint32_t wc[4] = {vc.x, vc.y, vc.z, vc.w};
@@ -380,9 +533,26 @@ __device__ __forceinline__ void issue_page(const CUtensorMap* tk,
 }
 
 template <int SEG>
+__device__ __forceinline__ void prefetch_page(const CUtensorMap* tk,
+                                              const CUtensorMap* tv, int id, int h) {
+  if (SEG == 0) {
+    tma_prefetch_l2_3d(tk, 0, h, id * kPage);
+    tma_prefetch_l2_3d(tv, 0, h, id * kPage);
+  } else {
+    tma_prefetch_l2_3d(tk, 0, 2 * h, id * kPage);
+    tma_prefetch_l2_3d(tk, 0, 2 * h + 1, id * kPage);
+    tma_prefetch_l2_3d(tv, 0, 2 * h, id * kPage);
+    tma_prefetch_l2_3d(tv, 0, 2 * h + 1, id * kPage);
+  }
+}
+
+// Pages prefetched into L2 ahead of the shared-memory ring (per warp).
+constexpr int kL2Ahead = 0;
+
+template <int SEG, typename QFrag>
 __device__ __forceinline__ bool run_warp_pages(
     const DecodeParams& p, const CUtensorMap* tk, const CUtensorMap* tv,
-    WarpState& st, uint8_t* ring, uint64_t* bars, const uint32_t* qf, int r,
+    WarpState& st, uint8_t* ring, uint64_t* bars, QFrag& qf, int r,
     int h, int idx_begin, int n_pages, bool has_last, int warp, int W,
     int lane) {
   constexpr int S = SEG == 0 ? kStagesI8 : kStagesI8 / 2;
@@ -392,65 +562,120 @@ __device__ __forceinline__ bool run_warp_pages(
   const int n_w = n_pages > warp ? (n_pages - warp + W - 1) / W : 0;
   if (n_w == 0) return true;
 
-  int last_valid = kPage;
-  if (has_last) {
-    const int lv = __ldg(sd.last_len + r);
-    last_valid = lv < 1 ? 1 : (lv > kPage ? kPage : lv);
-  }
+  // Programmatic dependent launch: the FP16 exact pages may have been
+  // written by the kernel just before this one (the append), so their loads
+  // wait for it; completed INT8 pages never are, so their first tiles are
+  // requested before the wait and overlap the predecessor's tail.
+  if constexpr (SEG == 1) pdl_wait_primary();
 
   PageWindow win;
   win.base = 0;
+  win.two = n_w > 32;
   load_window_set<SEG>(p, sd, idx_begin, warp, W, n_w, h, 0, lane, win.id_a,
                        win.sk_a, win.sv_a);
-  load_window_set<SEG>(p, sd, idx_begin, warp, W, n_w, h, 32, lane, win.id_b,
-                       win.sk_b, win.sv_b);
+  win.id_b = 0;
+  win.sk_b = win.sv_b = 0.f;
+  if (win.two)
+    load_window_set<SEG>(p, sd, idx_begin, warp, W, n_w, h, 32, lane, win.id_b,
+                         win.sk_b, win.sv_b);
 
-  // Prologue: fill the ring.
+  // Prologue: fill the ring, then start the L2 prefetch window behind it.
   const int pro = n_w < S ? n_w : S;
   for (int u = 0; u < pro; ++u) {
     const int id = win_id(win, u);
     if (lane == 0) issue_page<SEG>(tk, tv, ring, bars, u, id, h);
   }
+  for (int u = S; u < S + kL2Ahead && u < n_w; ++u) {
+    const int id = win_id(win, u);
+    if (lane == 0) prefetch_page<SEG>(tk, tv, id, h);
+  }
 
-  if (SEG == 0) st.sref = win_f(win.sv_a, win.sv_b, 0);
+  // ldmatrix row addresses for the V tile (see pv_int8): lane l reads row
+  // l%8 of matrix l/8; matrices alternate token halves (0-7 / 8-15) and the
+  // m-tile pair {2k, 2k+1}; chunks are 128B-swizzled by token row.
+  uint32_t vaddr[4] = {0u, 0u, 0u, 0u};
+  if constexpr (SEG == 0) {
+    const int j = lane >> 3, row = lane & 7;
+    const int tok = 8 * (j & 1) + row;
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      vaddr[k] = tok * 128 + (((2 * k + (j >> 1)) ^ row) << 4);
+  }
+  if constexpr (SEG == 0) pdl_wait_primary();
+  int last_valid = kPage;
+  if (has_last) {
+    const int lv = __ldg(sd.last_len + r);
+    last_valid = lv < 1 ? 1 : (lv > kPage ? kPage : lv);
+  }
+  // Prepare Q while the first tiles are in flight.
+  if constexpr (SEG == 0)
+    load_q_int8(p, r, h, g, t, qf);
+  else
+    load_q_fp16(p, r, h, g, t, qf);
+  if (SEG == 0) st.sref = win_f(win, win.sv_a, win.sv_b, 0);
   bool ok = true;
   int u = 0;
-  for (; u < n_w; ++u) {
-    const int stage = u % S;
-    const uint32_t parity = static_cast<uint32_t>(u / S) & 1u;
-    const bool waited = mbar_wait_bounded(bars + stage, parity);
+  while (u < n_w) {
+    // INT8 pages are consumed in pairs (independent chains -> ILP); FP16
+    // tail pages (2 stages per warp) one at a time.
+    const int np = (SEG == 0 && u + 1 < n_w) ? 2 : 1;
+    bool waited = mbar_wait_bounded(bars + (u % S), static_cast<uint32_t>(u / S) & 1u);
+    if (np == 2)
+      waited = waited && mbar_wait_bounded(bars + ((u + 1) % S),
+                                           static_cast<uint32_t>((u + 1) / S) & 1u);
     if (!__all_sync(0xffffffffu, waited)) {
       ok = false;
       break;
     }
-    const int k = u - win.base;
-    const int local = warp + W * u;
-    const int valid = (has_last && local == n_pages - 1) ? last_valid : kPage;
-    const uint32_t st_addr = smem_addr(ring + stage * STAGE_BYTES);
-    if (SEG == 0) {
-      const float sk = win_f(win.sk_a, win.sk_b, k);
-      const float sv = win_f(win.sv_a, win.sv_b, k);
-      if (sv > st.sref) {
-        // Keep P * (s_V / s_ref) <= 1 in FP16 by raising the reference.
-        const float f = st.sref / sv;
+    if constexpr (SEG == 0) {
+      float sk[2], sv[2], rr[2];
+      int valid[2];
+      const uint8_t* stg[2];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int uj = j < np ? u + j : u;
+        sk[j] = win_f(win, win.sk_a, win.sk_b, uj - win.base);
+        sv[j] = win_f(win, win.sv_a, win.sv_b, uj - win.base);
+        valid[j] = (has_last && warp + W * uj == n_pages - 1) ? last_valid : kPage;
+        stg[j] = ring + (uj % S) * STAGE_BYTES;
+      }
+      const float svmax = fmaxf(sv[0], sv[1]);
+      if (svmax > st.sref) {
+        // Keep P * (s_V / s_ref) <= P in FP16 by raising the reference.
+        const float f = st.sref / svmax;
 #pragma unroll
         for (int i = 0; i < 32; ++i) st.o[i] *= f;
-        st.sref = sv;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) st.o1[i] *= f;
+        st.sref = svmax;
       }
-      const float rr = st.sref > 0.f ? sv / st.sref : 1.f;
-      page_int8(st, st_addr, qf, sk * p.sm_scale_log2, rr, valid, g, t,
-                p.group);
+      const float inv_ref = st.sref > 0.f ? __fdividef(1.f, st.sref) : 1.f;
+      rr[0] = st.sref > 0.f ? sv[0] * inv_ref : 1.f;
+      rr[1] = st.sref > 0.f ? sv[1] * inv_ref : 1.f;
+      if (np == 2)
+        pages_int8<2>(st, stg, qf, sk, rr, valid, g, t, vaddr);
+      else
+        pages_int8<1>(st, stg, qf, sk, rr, valid, g, t, vaddr);
     } else {
-      page_fp16(st, st_addr, qf, p.sm_scale_log2, valid, g, t, p.group);
+      const int valid = (has_last && warp + W * u == n_pages - 1) ? last_valid : kPage;
+      page_fp16(st, ring + (u % S) * STAGE_BYTES, qf, p.sm_scale_log2, valid, g, t, p.group);
     }
     __syncwarp();
-    const int nu = u + S;
-    if (nu < n_w) {
-      const int id = win_id(win, nu);
-      if (lane == 0) issue_page<SEG>(tk, tv, ring, bars, stage, id, h);
+    for (int j = 0; j < np; ++j) {
+      const int nu = u + j + S;
+      if (nu < n_w) {
+        const int id = win_id(win, nu);
+        if (lane == 0) issue_page<SEG>(tk, tv, ring, bars, (u + j) % S, id, h);
+      }
+      const int pu = nu + kL2Ahead;
+      if (pu < n_w) {
+        const int id = win_id(win, pu);
+        if (lane == 0) prefetch_page<SEG>(tk, tv, id, h);
+      }
     }
+    u += np;
     // Slide the id window once the consumer leaves its first half.
-    if (u + 1 - win.base == 32) {
+    if (win.two && u - win.base >= 32) {
       win.base += 32;
       win.id_a = win.id_b;
       win.sk_a = win.sk_b;
@@ -470,15 +695,96 @@ __device__ __forceinline__ bool run_warp_pages(
   return ok;
 }
 
-__global__ void __launch_bounds__(kMaxWarps * 32)
+// Merge the optional extra state (lse xl, value read from extra_o), add the
+// value centre and store output element (q, d) of head h of request r.
+__device__ __forceinline__ void store_final(const DecodeParams& p, int r, int h, int q,
+                                            int d, float v, float lv, float xl,
+                                            bool write_lse) {
+  const int group = p.group;
+  const int qh = h * group + q;
+  if (p.extra_o != nullptr) {
+    const float xo = __half2float(p.extra_o[static_cast<int64_t>(r) * p.extra_stride_b +
+                                            static_cast<int64_t>(qh) * p.extra_stride_h + d]);
+    const float mm = fmaxf(xl, lv);
+    if (mm == kNegInf) {
+      v = 0.f;
+      lv = kNegInf;
+    } else {
+      const float wx = fast_exp2(xl - mm), wy = fast_exp2(lv - mm);
+      const float den = wx + wy;
+      v = (wx * xo + wy * v) / den;
+      lv = mm + fast_log2(den);
+    }
+  }
+  if (p.value_center != nullptr)
+    v += __half2float(p.value_center[static_cast<int64_t>(r) * p.vc_stride_b + h * kHeadDim + d]);
+  p.out[static_cast<int64_t>(r) * p.out_stride_b + static_cast<int64_t>(qh) * p.out_stride_h + d] =
+      __float2half_rn(v);
+  if (write_lse && p.lse_out != nullptr)
+    p.lse_out[static_cast<int64_t>(r) * (p.hkv * group) + qh] = lv;
+}
+
+// Last CTA of head h: merge the head's partial states (written by every CTA
+// of the head, made visible by the arrival protocol) into the final output.
+// Thread -> (query row, 4 dims); partials are folded with an online max.
+__device__ __forceinline__ void merge_head(const DecodeParams& p, int r, int h,
+                                           const float* xls) {
+  const int group = p.group;
+  const int rh = r * p.hkv + h;
+  const int begin = p.item_off[rh], end = p.item_off[rh + 1];
+  for (int slot = threadIdx.x; slot < group * 32; slot += blockDim.x) {
+    const int q = slot >> 5, d4 = slot & 31;
+    float m = kNegInf, den = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    constexpr int U = 8;
+    for (int i0 = begin; i0 < end; i0 += U) {
+      float l[U];
+      float4 v[U];
+#pragma unroll
+      for (int k = 0; k < U; ++k) {
+        l[k] = kNegInf;
+        v[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (i0 + k < end) {
+          const int64_t b = static_cast<int64_t>(i0 + k) * group + q;
+          l[k] = __ldcg(p.part_lse + b);
+          v[k] = __ldcg(reinterpret_cast<const float4*>(p.part_o + b * kHeadDim) + d4);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < U; ++k) {
+        if (l[k] == kNegInf) continue;
+        if (l[k] > m) {
+          const float sc = fast_exp2(m - l[k]);
+          acc.x *= sc; acc.y *= sc; acc.z *= sc; acc.w *= sc;
+          den *= sc;
+          m = l[k];
+        }
+        const float w = fast_exp2(l[k] - m);
+        acc.x += w * v[k].x; acc.y += w * v[k].y; acc.z += w * v[k].z; acc.w += w * v[k].w;
+        den += w;
+      }
+    }
+    const float inv = den > 0.f ? 1.f / den : 0.f;
+    const float lv = den > 0.f ? m + fast_log2(den) : kNegInf;
+    const float xl = xls[q];
+    const int d = 4 * d4;
+    store_final(p, r, h, q, d + 0, acc.x * inv, lv, xl, d4 == 0);
+    store_final(p, r, h, q, d + 1, acc.y * inv, lv, xl, false);
+    store_final(p, r, h, q, d + 2, acc.z * inv, lv, xl, false);
+    store_final(p, r, h, q, d + 3, acc.w * inv, lv, xl, false);
+  }
+}
+
+__global__ void __launch_bounds__(kMaxWarps * 32, 1)
     pg_decode_split_kernel(const __grid_constant__ CUtensorMap tm_k8,
                            const __grid_constant__ CUtensorMap tm_v8,
                            const __grid_constant__ CUtensorMap tm_k16,
                            const __grid_constant__ CUtensorMap tm_v16,
                            const __grid_constant__ DecodeParams p) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 1024-byte alignment (128B-swizzled TMA destinations) by pointer
+  // arithmetic on the shared array, so loads stay in the shared space.
+  uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
   const int W = blockDim.x >> 5;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
@@ -517,24 +823,43 @@ __global__ void __launch_bounds__(kMaxWarps * 32)
   st.sref = 1.f;
 #pragma unroll
   for (int i = 0; i < 32; ++i) st.o[i] = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) st.o1[i] = 0.f;
 
-  uint32_t qf[16];
   bool ok;
   if (seg == 0) {
-    load_q_frag<0>(p, r, h, g, t, qf);
-    ok = run_warp_pages<0>(p, &tm_k8, &tm_v8, st, ring, bars, qf, r, h,
+    QInt8 qi;
+    ok = run_warp_pages<0>(p, &tm_k8, &tm_v8, st, ring, bars, qi, r, h,
                            item.idx_begin, n_pages, has_last, warp, W, lane);
+    // Remove the +1152 code bias of the PV operand: O -= 1152 * sum(P'').
+    const float sp0 = 1152.f * __shfl_sync(0xffffffffu, st.o1[0], t);
+    const float sp1 = 1152.f * __shfl_sync(0xffffffffu, st.o1[1], t);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      st.o[4 * i + 0] -= sp0;
+      st.o[4 * i + 1] -= sp1;
+      st.o[4 * i + 2] -= sp0;
+      st.o[4 * i + 3] -= sp1;
+    }
   } else {
-    load_q_frag<1>(p, r, h, g, t, qf);
+    uint32_t qf[16];
     ok = run_warp_pages<1>(p, &tm_k16, &tm_v16, st, ring, bars, qf, r, h,
                            item.idx_begin, n_pages, has_last, warp, W, lane);
   }
+  // Warps without pages skipped the wait above; everything below writes.
+  pdl_wait_primary();
   // Let a dependent (merge) grid start launching while we finish.
   pdl_launch_dependents();
 
-  // Per-warp totals: reduce l across the 8 token lanes.
-  st.l0 = warp_sum_xor_g(st.l0);
-  st.l1 = warp_sum_xor_g(st.l1);
+  // Per-warp totals.  FP16 path: rows 2t/2t+1, reduce l over the 8 token
+  // lanes.  INT8 path: row g, reduce l over the 4 lanes of the group.
+  if (seg == 0) {
+    st.l0 += __shfl_xor_sync(0xffffffffu, st.l0, 1);
+    st.l0 += __shfl_xor_sync(0xffffffffu, st.l0, 2);
+  } else {
+    st.l0 = warp_sum_xor_g(st.l0);
+    st.l1 = warp_sum_xor_g(st.l1);
+  }
   const float oscale = seg == 0 ? st.sref : 1.f;
 
   __syncthreads();  // every warp has drained its ring
@@ -543,38 +868,37 @@ __global__ void __launch_bounds__(kMaxWarps * 32)
   float* cl = cm + kMaxWarps * 8;                      // [W][8]
   float* co = cl + kMaxWarps * 8;                      // [W][8][128]
   const int q0 = 2 * t, q1 = 2 * t + 1;
-  if (g == 0) {
+  if (seg == 0) {
+    if (t == 0) {
+      cm[warp * 8 + g] = ok ? st.m0 : kNegInf;
+      cl[warp * 8 + g] = ok ? st.l0 : 0.f;
+    }
+  } else if (g == 0) {
     cm[warp * 8 + q0] = ok ? st.m0 : kNegInf;
     cm[warp * 8 + q1] = ok ? st.m1 : kNegInf;
     cl[warp * 8 + q0] = ok ? st.l0 : 0.f;
     cl[warp * 8 + q1] = ok ? st.l1 : 0.f;
   }
+  // Rows of the combine buffer are padded to 132 floats so the float2
+  // stores of the 32 lanes fall on distinct bank pairs.
   if (q0 < group) {
-    float* c0 = co + (warp * 8 + q0) * kHeadDim;
-    float* c1 = co + (warp * 8 + q1) * kHeadDim;
+    float* c0 = co + (warp * 8 + q0) * kCoStride;
+    float* c1 = co + (warp * 8 + q1) * kCoStride;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      int d0, d1;
-      if (seg == 0) {
-        d0 = out_dim<0>(i, g, 0);
-        d1 = out_dim<0>(i, g, 1);
-      } else {
-        d0 = out_dim<1>(i, g, 0);
-        d1 = out_dim<1>(i, g, 1);
-      }
-      c0[d0] = st.o[4 * i + 0] * oscale;
-      c0[d1] = st.o[4 * i + 2] * oscale;
-      if (q1 < group) {
-        c1[d0] = st.o[4 * i + 1] * oscale;
-        c1[d1] = st.o[4 * i + 3] * oscale;
-      }
+      const int d0 = seg == 0 ? out_dim<0>(i, g, 0) : out_dim<1>(i, g, 0);
+      *reinterpret_cast<float2*>(c0 + d0) =
+          make_float2(st.o[4 * i + 0] * oscale, st.o[4 * i + 2] * oscale);
+      if (q1 < group)
+        *reinterpret_cast<float2*>(c1 + d0) =
+            make_float2(st.o[4 * i + 1] * oscale, st.o[4 * i + 3] * oscale);
     }
   }
   __syncthreads();
 
   // The extra state may alias the outputs (in-place merge): read its lse
   // for every row before any thread writes lse_out.
-  float* xls = co + W * 8 * kHeadDim;  // [8], inside this CTA's rings
+  float* xls = co + W * 8 * kCoStride;  // [8], inside this CTA's rings
   if (p.final_mode && p.extra_o != nullptr && threadIdx.x < group)
     xls[threadIdx.x] = p.extra_lse[static_cast<int64_t>(r) * (p.hkv * group) + h * group + threadIdx.x];
   __syncthreads();
@@ -590,7 +914,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32)
         if (mw == kNegInf) continue;
         const float e = fast_exp2(mw - M);
         L += cl[w * 8 + q] * e;
-        O += co[(w * 8 + q) * kHeadDim + d] * e;
+        O += co[(w * 8 + q) * kCoStride + d] * e;
       }
     }
     const float on = L > 0.f ? O / L : 0.f;
@@ -600,36 +924,34 @@ __global__ void __launch_bounds__(kMaxWarps * 32)
       p.part_o[base * kHeadDim + d] = on;
       if (d == 0) p.part_lse[base] = lse;
     } else {
-      const int qh = h * group + q;
-      float v = on, lv = lse;
-      if (p.extra_o != nullptr) {
-        const float xl = xls[q];
-        const float xo = __half2float(
-            p.extra_o[static_cast<int64_t>(r) * p.extra_stride_b +
-                      static_cast<int64_t>(qh) * p.extra_stride_h + d]);
-        const float mm = fmaxf(xl, lv);
-        if (mm == kNegInf) {
-          v = 0.f;
-          lv = kNegInf;
-        } else {
-          const float wx = fast_exp2(xl - mm), wy = fast_exp2(lv - mm);
-          const float den = wx + wy;
-          v = (wx * xo + wy * v) / den;
-          lv = mm + fast_log2(den);
-        }
-      }
-      if (p.value_center != nullptr) {
-        v += __half2float(p.value_center[static_cast<int64_t>(r) * p.vc_stride_b +
-                                         h * kHeadDim + d]);
-      }
-      // All threads read the extra state before any thread writes: the
-      // output may alias it, and (q, d) is owned by exactly this thread.
-      p.out[static_cast<int64_t>(r) * p.out_stride_b +
-            static_cast<int64_t>(qh) * p.out_stride_h + d] = __float2half_rn(v);
-      if (d == 0 && p.lse_out != nullptr)
-        p.lse_out[static_cast<int64_t>(r) * (p.hkv * group) + qh] = lv;
+      store_final(p, r, h, q, d, on, lse, xls[q], d == 0);
     }
   }
+  if (p.final_mode || p.sem == nullptr) return;
+  // Fused merge: publish this CTA's partial, count arrivals per head; the
+  // last CTA of the head merges.  It also re-arms the counter for the next
+  // launch (CUDA-graph replays reuse it).
+  __threadfence();
+  __syncthreads();
+  int* s_last = reinterpret_cast<int*>(xls + 8);
+  if (threadIdx.x == 0) {
+    const int rh = r * p.hkv + h;
+    const int n = p.item_off[rh + 1] - p.item_off[rh];
+    const int prev = atomicAdd(p.sem + rh, 1);
+    const int last = prev == n - 1;
+    if (last) p.sem[rh] = 0;
+    *s_last = last;
+  }
+  __syncthreads();
+  if (!*s_last) return;
+  __threadfence();
+  // The extra state may alias out / lse_out: stage its lse first.
+  if (threadIdx.x < group)
+    xls[threadIdx.x] = p.extra_o != nullptr
+                           ? p.extra_lse[static_cast<int64_t>(r) * (p.hkv * group) + h * group + threadIdx.x]
+                           : kNegInf;
+  __syncthreads();
+  merge_head(p, r, h, xls);
 }
 
 // --------------------------------------------------------------- merging
@@ -648,15 +970,17 @@ struct MergeParams {
   int64_t vc_stride_b;
 };
 
-// One CTA of 128 threads per (request, query head).  Warp w folds the
-// partials w, w+4, ... with float4 lanes (4 dims per lane, independent
-// loads in flight), then the four warp states are combined in shared
-// memory and thread d writes output dim d.
-__global__ void __launch_bounds__(128)
+// One CTA of 256 threads per (request, query head).  Warp w folds the
+// partials w, w+8, ... with float4 lanes (4 dims per lane, up to 8 loads in
+// flight), then the eight warp states are combined in shared memory and
+// thread d < 128 writes output dim d.  The item range is plan data, read
+// before waiting on the split kernel.
+constexpr int kMergeWarps = 8;
+
+__global__ void __launch_bounds__(kMergeWarps * 32)
     pg_merge_partials_kernel(const __grid_constant__ MergeParams p) {
-  __shared__ float s_m[4], s_den[4];
-  __shared__ float4 s_acc[4][32];
-  pdl_wait_primary();
+  __shared__ float s_m[kMergeWarps], s_den[kMergeWarps];
+  __shared__ float4 s_acc[kMergeWarps][32];
   const int hq = p.hkv * p.group;
   const int r = blockIdx.x / hq;
   const int qh = blockIdx.x % hq;
@@ -664,37 +988,40 @@ __global__ void __launch_bounds__(128)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int begin = p.item_off[r * p.hkv + h];
   const int end = p.item_off[r * p.hkv + h + 1];
+  // The next decode launch may start its cache stream now; it waits for this
+  // grid before touching anything this grid reads or writes.
+  pdl_launch_dependents();
+  pdl_wait_primary();
   float m = kNegInf, den = 0.f;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  auto push = [&](float lse, float4 v) {
-    if (lse == kNegInf) return;
-    if (lse > m) {
-      const float sc = fast_exp2(m - lse);  // m = -inf -> 0
-      acc.x *= sc; acc.y *= sc; acc.z *= sc; acc.w *= sc;
-      den *= sc;
-      m = lse;
-    }
-    const float w = fast_exp2(lse - m);
-    acc.x += w * v.x; acc.y += w * v.y; acc.z += w * v.z; acc.w += w * v.w;
-    den += w;
-  };
-  constexpr int U = 4;
-  for (int i0 = begin + warp; i0 < end; i0 += 4 * U) {
+  constexpr int U = 8;
+  for (int i0 = begin + warp; i0 < end; i0 += kMergeWarps * U) {
     float l[U];
     float4 v[U];
 #pragma unroll
     for (int k = 0; k < U; ++k) {
-      const int i = i0 + 4 * k;
+      const int i = i0 + kMergeWarps * k;
       l[k] = kNegInf;
       v[k] = make_float4(0.f, 0.f, 0.f, 0.f);
       if (i < end) {
         const int64_t b = static_cast<int64_t>(i) * p.group + q;
-        l[k] = p.part_lse[b];
-        v[k] = reinterpret_cast<const float4*>(p.part_o + b * kHeadDim)[lane];
+        l[k] = __ldcg(p.part_lse + b);
+        v[k] = __ldcg(reinterpret_cast<const float4*>(p.part_o + b * kHeadDim) + lane);
       }
     }
 #pragma unroll
-    for (int k = 0; k < U; ++k) push(l[k], v[k]);
+    for (int k = 0; k < U; ++k) {
+      if (l[k] == kNegInf) continue;
+      if (l[k] > m) {
+        const float sc = fast_exp2(m - l[k]);  // m = -inf -> 0
+        acc.x *= sc; acc.y *= sc; acc.z *= sc; acc.w *= sc;
+        den *= sc;
+        m = l[k];
+      }
+      const float w = fast_exp2(l[k] - m);
+      acc.x += w * v[k].x; acc.y += w * v[k].y; acc.z += w * v[k].z; acc.w += w * v[k].w;
+      den += w;
+    }
   }
   if (lane == 0) {
     s_m[warp] = m;
@@ -702,14 +1029,15 @@ __global__ void __launch_bounds__(128)
   }
   s_acc[warp][lane] = acc;
   __syncthreads();
+  if (threadIdx.x >= kHeadDim) return;
   const int d = threadIdx.x;
   float M = kNegInf;
 #pragma unroll
-  for (int w = 0; w < 4; ++w) M = fmaxf(M, s_m[w]);
+  for (int w = 0; w < kMergeWarps; ++w) M = fmaxf(M, s_m[w]);
   float D = 0.f, A = 0.f;
   if (M != kNegInf) {
 #pragma unroll
-    for (int w = 0; w < 4; ++w) {
+    for (int w = 0; w < kMergeWarps; ++w) {
       if (s_m[w] == kNegInf) continue;
       const float e = fast_exp2(s_m[w] - M);
       D += s_den[w] * e;
@@ -733,7 +1061,9 @@ __global__ void __launch_bounds__(128)
   }
   if (p.value_center != nullptr)
     v += __half2float(p.value_center[static_cast<int64_t>(r) * p.vc_stride_b + h * kHeadDim + d]);
-  __syncthreads();  // out / lse_out may alias extra_o / extra_lse
+  // out / lse_out may alias extra_o / extra_lse: all 128 output threads
+  // have read them above; sync the four output warps before writing.
+  asm volatile("bar.sync 1, 128;" ::: "memory");
   p.out[static_cast<int64_t>(r) * p.out_stride_b + static_cast<int64_t>(qh) * p.out_stride_h + d] =
       __float2half_rn(v);
   if (d == 0 && p.lse_out != nullptr) p.lse_out[static_cast<int64_t>(r) * hq + qh] = lse;

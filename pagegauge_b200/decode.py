@@ -64,7 +64,7 @@ class PageGaugeDecode:
     def run(self, q: torch.Tensor, key_codes, value_codes, key_scales, value_scales,
             exact_key, exact_value, value_center: torch.Tensor | None,
             out: torch.Tensor | None = None, lse: torch.Tensor | None = None,
-            sm_scale: float | None = None) -> torch.Tensor:
+            sm_scale: float | None = None, fused_merge: bool = False) -> torch.Tensor:
         plan = self.work_plan
         segs = [None, None]
         if self._old_indices is not None:
@@ -82,7 +82,7 @@ class PageGaugeDecode:
                                          or not value_center.is_contiguous()):
             raise ValueError("value_center must be contiguous float16")
         launch_decode(plan, q, segs, self.sm_scale if sm_scale is None else sm_scale, out, lse,
-                      value_center=value_center)
+                      value_center=value_center, fused_merge=fused_merge)
         return out
 
 

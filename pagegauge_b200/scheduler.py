@@ -64,7 +64,7 @@ def record(batch: int, context: int, results: dict[int, float], path: Path = TAB
 
 
 def sweep(batch: int, context: int, repeats: int = 60, seeds=(20261001, 20261002, 20261003),
-          write: bool = True) -> dict[int, float]:
+          write: bool = True, path: Path = TABLE_PATH) -> dict[int, float]:
     """Time every candidate split on the current GPU (cache-neutral p50 over
     seeds) and record the winner."""
     import torch
@@ -106,8 +106,9 @@ def sweep(batch: int, context: int, repeats: int = 60, seeds=(20261001, 20261002
         del cache
     p50 = {k: statistics.median(v) for k, v in results.items()}
     if write:
-        record(batch, context, p50, meta={"gpu": torch.cuda.get_device_name(), "repeats": repeats,
-                                           "seeds": list(seeds), "mode": "cache_neutral"})
+        record(batch, context, p50, path=path,
+               meta={"gpu": torch.cuda.get_device_name(), "repeats": repeats,
+                     "seeds": list(seeds), "mode": "cache_neutral"})
     return p50
 
 
@@ -117,13 +118,14 @@ def main() -> None:
     parser.add_argument("--batch", type=int, nargs="*", default=[1])
     parser.add_argument("--context", type=int, nargs="*", default=[49152])
     parser.add_argument("--repeats", type=int, default=60)
+    parser.add_argument("--table", type=Path, default=TABLE_PATH)
     args = parser.parse_args()
     if not args.sweep:
-        print(json.dumps(load_table(), indent=1))
+        print(json.dumps(load_table(args.table), indent=1))
         return
     for b in args.batch:
         for c in args.context:
-            print(b, c, json.dumps(sweep(b, c, args.repeats)), flush=True)
+            print(b, c, json.dumps(sweep(b, c, args.repeats, path=args.table)), flush=True)
 
 
 if __name__ == "__main__":

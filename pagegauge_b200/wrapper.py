@@ -79,9 +79,10 @@ class _Workspace:
 
         items_b = align(max(num_items, 1) * ITEM_BYTES)
         off_b = align(num_offsets * 4)
+        sem_b = align(num_offsets * 4)
         lse_b = align(max(num_items, 1) * group * 4)
         o_b = align(max(num_items, 1) * group * HEAD_DIM * 4)
-        total = items_b + off_b + lse_b + o_b
+        total = items_b + off_b + sem_b + lse_b + o_b
         if total > self.buffer.numel():
             raise RuntimeError(
                 f"workspace of {self.buffer.numel()} bytes is too small for {num_items} work items "
@@ -89,9 +90,10 @@ class _Workspace:
         base = self.buffer
         items = base[:items_b]
         off = base[items_b:items_b + off_b]
-        lse = base[items_b + off_b:items_b + off_b + lse_b]
-        part_o = base[items_b + off_b + lse_b:total]
-        return items, off, lse, part_o
+        sem = base[items_b + off_b:items_b + off_b + sem_b]
+        lse = base[items_b + off_b + sem_b:items_b + off_b + sem_b + lse_b]
+        part_o = base[items_b + off_b + sem_b + lse_b:total]
+        return items, off, sem, lse, part_o
 
 
 class PagedDecodePlan:
@@ -104,13 +106,15 @@ class PagedDecodePlan:
         self.split_pages = (int(info.split_pages[0]), int(info.split_pages[1]))
         self.warps = int(info.warps_per_cta)
         self.batch, self.kv_heads, self.group = batch, kv_heads, group
-        d_items, d_off, d_lse, d_o = ws.layout(self.num_items, off.size, group)
+        d_items, d_off, d_sem, d_lse, d_o = ws.layout(self.num_items, off.size, group)
+        d_sem.zero_()  # per-head arrival counters of the fused merge
         if self.num_items:
             src = torch.from_numpy(items.view(np.uint8).reshape(-1))
             d_items[:src.numel()].copy_(src, non_blocking=False)
         d_off[:off.size * 4].copy_(torch.from_numpy(off.view(np.uint8)), non_blocking=False)
         self.items_ptr = d_items.data_ptr()
         self.off_ptr = d_off.data_ptr()
+        self.sem_ptr = d_sem.data_ptr()
         self.lse_ptr = d_lse.data_ptr()
         self.o_ptr = d_o.data_ptr()
         self.host_items = items
@@ -137,7 +141,8 @@ def check_cache(cache: torch.Tensor, name: str, dtype: torch.dtype, kv_heads: in
 
 def launch_decode(plan: PagedDecodePlan, q: torch.Tensor, segments, sm_scale: float,
                   out: torch.Tensor, lse: torch.Tensor | None, extra=None,
-                  value_center: torch.Tensor | None = None, final_ok: bool = True) -> None:
+                  value_center: torch.Tensor | None = None, final_ok: bool = True,
+                  fused_merge: bool = False) -> None:
     """Fill the C argument block and launch split decode (+ merge)."""
     if q.dtype != torch.float16 or q.dim() != 3 or q.stride(2) != 1:
         raise ValueError("q must be float16 [B,Hq,128] with a contiguous last dimension")
@@ -156,6 +161,7 @@ def launch_decode(plan: PagedDecodePlan, q: torch.Tensor, segments, sm_scale: fl
     a.part_o = plan.o_ptr
     a.part_lse = plan.lse_ptr
     a.final_mode = 1 if (final_ok and plan.single and plan.num_items > 0) else 0
+    a.merge_sem = plan.sem_ptr if fused_merge else None
     a.out = out.data_ptr()
     a.out_stride_b, a.out_stride_h = out.stride(0), out.stride(1)
     a.lse_out = None if lse is None else lse.data_ptr()

@@ -67,9 +67,12 @@ def test_planner_chunks_and_offsets(lib):
 
 
 def test_planner_single_item_and_auto_split(lib):
+    items, off, info = plan_items(1, 8, np.array([0, 100], np.int32), None, 1 << 20, 0, 148)
+    assert info.single_item_per_head and info.num_items == 8
+    # a fixed split above 32 pages per warp is capped (4 warps -> 128 pages)
     indptr = np.array([0, 3056], np.int32)
     items, off, info = plan_items(1, 8, indptr, None, 1 << 20, 0, 148)
-    assert info.single_item_per_head and info.num_items == 8
+    assert info.split_pages[0] == 128 and info.num_items == 8 * 24
     items, off, info = plan_items(1, 8, indptr, None, 0, 0, 148)
     # one full wave of 3 CTAs per SM (444 slots) with the smallest items
     assert info.split_pages[0] == 56

@@ -253,3 +253,29 @@ def test_cuda_graph_capture_and_replay(cuda_lib):
     exp, _ = oracle_decode(q, cache, tables, lengths, 0)
     assert_close_decode(out[0], exp)
     del graph
+
+
+@pytest.mark.parametrize("fused", [True, False])
+def test_fused_last_cta_merge_matches_merge_kernel(cuda_lib, fused):
+    """The split kernel's in-kernel merge (last CTA per head) and the
+    separate merge kernel give the same result; repeated launches re-arm the
+    arrival counters."""
+    from pagegauge_b200.wrapper import _segment, launch_decode
+    lengths = [6000, 3000]
+    q, dk, dv, cache, tables = make_case(lengths, seed=23)
+    dec = PageGaugeDecode(workspace())
+    dec.plan(tables.old_indptr, tables.old_indices, tables.exact_indptr, tables.exact_indices,
+             tables.exact_last_page_len, 32, 8, old_split_pages=7, exact_split_pages=3)
+    segs = (_segment(cache.key_codes, cache.value_codes, dec._old_indices, dec._old_last,
+                     cache.key_scales, cache.value_scales),
+            _segment(cache.exact_key, cache.exact_value, dec._exact_indices, dec._exact_last))
+    for _ in range(3):
+        out = torch.zeros_like(q)
+        lse = torch.zeros(2, 32, device="cuda", dtype=torch.float32)
+        launch_decode(dec.work_plan, q, segs, 128 ** -0.5, out, lse, value_center=cache.value_center,
+                      fused_merge=fused)
+        torch.cuda.synchronize()
+        for r in range(2):
+            exp, exp_lse = oracle_decode(q, cache, tables, lengths, r)
+            assert_close_decode(out[r], exp)
+            np.testing.assert_allclose(cpu(lse[r]), exp_lse, atol=LSE_ATOL, rtol=0)
