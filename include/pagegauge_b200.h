@@ -187,6 +187,27 @@ typedef struct pg_decode_args {
 
 int32_t pg_decode_run(const pg_decode_args* args, void* stream);
 
+/* Allocation-free variant of pg_decode_plan + pg_decode_run (no counterpart
+ * in the reference).  For callers that cannot allocate device memory - a
+ * plugin inside a host process whose allocator owns the GPU, or a path that
+ * must not allocate while it runs - the work list, the per-head item ranges
+ * and the split partial states live in one file-scope device array of
+ * 8 MiB inside the library instead of a caller workspace.  The caller passes
+ * inputs and outputs in `args` (items, item_off, num_items, part_o,
+ * part_lse, final_mode and merge_sem are ignored) plus the host indptr
+ * arrays pg_decode_plan takes.  Limits: at most 4096 work items and 8192
+ * (request, kv head) pairs, and the partial states must fit the array
+ * (about 2 KiB per item at GQA group 4); larger plans fail with
+ * PG_ERR_CAPACITY and a message.  No cudaMalloc/cudaFree is called.  The
+ * first call on each device looks up the array's device address, so make
+ * it before any stream capture.  Calls on one device share that device's
+ * array and it keeps the last call's contents (nothing in it has to start
+ * at zero: every call rewrites what it reads); two calls that run at the
+ * same time on one GPU, e.g. on two streams, race on it. */
+int32_t pg_decode_static(const pg_decode_args* args, const int32_t* indptr0,
+                         const int32_t* indptr1, int32_t split_pages0,
+                         int32_t split_pages1, int32_t num_sms, void* stream);
+
 /* (v_a, s_a) <- merge((v_a, s_a), (v_b, s_b)); rows of 128 fp16, lse base 2. */
 int32_t pg_merge_state_in_place(void* v_a, float* s_a, const void* v_b,
                                 const float* s_b, int64_t rows,

@@ -664,4 +664,96 @@ int32_t pg_quantize_pages(const void* key, const void* value,
   return cuda_check(cudaGetLastError(), "quantize launch");
 }
 
+// --------------------------------------------- allocation-free decode
+// Some callers cannot allocate device memory: a plugin loaded into a host
+// process whose allocator owns the device (or forbids allocation while it
+// runs), or code that must not allocate inside a latency-critical path.
+// pg_decode_static gives them the planned split decode + merge with its
+// scratch (work list, per-head item ranges, split partial states) in this
+// file-scope device array instead of a caller workspace.  Every GPU that
+// loads the library holds the array until the process exits.
+constexpr size_t kStaticScratchBytes = size_t(8) << 20;  // 8 MiB
+constexpr int64_t kStaticMaxItems = 4096;
+constexpr int64_t kStaticMaxHeads = 8192;  // batch * kv_heads
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+namespace {
+std::mutex g_static_mu;
+unsigned char* g_static_dev[64] = {nullptr};  // device address, per device
+// Host staging of the plan (no heap allocation on the call path).
+pg_decode_item g_static_items[kStaticMaxItems];
+int32_t g_static_off[kStaticMaxHeads + 1];
+
+size_t align256(size_t x) { return (x + 255) / 256 * 256; }
+}  // namespace
+
+int32_t pg_decode_static(const pg_decode_args* args, const int32_t* indptr0,
+                         const int32_t* indptr1, int32_t split_pages0,
+                         int32_t split_pages1, int32_t num_sms, void* stream) {
+  PG_REQUIRE(args != nullptr, "null arguments");
+  PG_REQUIRE(static_cast<int64_t>(args->batch) * args->kv_heads <= kStaticMaxHeads,
+             "pg_decode_static supports at most %lld (request, kv head) pairs",
+             static_cast<long long>(kStaticMaxHeads));
+  std::lock_guard<std::mutex> lock(g_static_mu);
+  int dev = 0;
+  int32_t rc = cuda_check(cudaGetDevice(&dev), "cudaGetDevice");
+  if (rc != PG_OK) return rc;
+  PG_REQUIRE(dev >= 0 && dev < 64, "device ordinal out of range");
+  if (g_static_dev[dev] == nullptr) {
+    // One-time set-up per device, with that device current: the symbol's
+    // device address (the host-side name is only a stand-in).
+    void* ptr = nullptr;
+    rc = cuda_check(cudaGetSymbolAddress(&ptr, g_static_scratch),
+                    "cudaGetSymbolAddress(static decode scratch)");
+    if (rc != PG_OK) return rc;
+    g_static_dev[dev] = static_cast<unsigned char*>(ptr);
+  }
+  unsigned char* base = g_static_dev[dev];
+  pg_plan_info info{};
+  rc = pg_decode_plan(args->batch, args->kv_heads, indptr0, indptr1, split_pages0,
+                      split_pages1, num_sms, args->warps_per_cta, g_static_items,
+                      kStaticMaxItems, g_static_off, &info);
+  if (rc == PG_ERR_CAPACITY)
+    return fail(PG_ERR_CAPACITY,
+                "pg_decode_static: the plan needs %lld work items; the static scratch holds at "
+                "most %lld (use a larger split)",
+                static_cast<long long>(info.num_items), static_cast<long long>(kStaticMaxItems));
+  if (rc != PG_OK) return rc;
+  const int64_t n = info.num_items;
+  const int64_t heads = static_cast<int64_t>(args->batch) * args->kv_heads;
+  const size_t items_b = align256(static_cast<size_t>(kStaticMaxItems) * sizeof(pg_decode_item));
+  const size_t off_b = align256(static_cast<size_t>(kStaticMaxHeads + 1) * sizeof(int32_t));
+  const size_t lse_b = align256(static_cast<size_t>(n) * args->group * sizeof(float));
+  const size_t o_b = static_cast<size_t>(n) * args->group * pg::kHeadDim * sizeof(float);
+  if (items_b + off_b + lse_b + o_b > kStaticScratchBytes)
+    return fail(PG_ERR_CAPACITY,
+                "pg_decode_static: %lld work items need %zu bytes of scratch; the static array "
+                "holds %zu (use a larger split)",
+                static_cast<long long>(n), items_b + off_b + lse_b + o_b, kStaticScratchBytes);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // Pageable host -> device copies are staged before returning, so the host
+  // plan buffers may be rewritten by the next call right away.
+  if (n > 0) {
+    rc = cuda_check(cudaMemcpyAsync(base, g_static_items, static_cast<size_t>(n) * sizeof(pg_decode_item),
+                                    cudaMemcpyHostToDevice, st),
+                    "copy work items");
+    if (rc != PG_OK) return rc;
+  }
+  rc = cuda_check(cudaMemcpyAsync(base + items_b, g_static_off, static_cast<size_t>(heads + 1) * sizeof(int32_t),
+                                  cudaMemcpyHostToDevice, st),
+                  "copy item offsets");
+  if (rc != PG_OK) return rc;
+  pg_decode_args a = *args;
+  a.items = reinterpret_cast<const pg_decode_item*>(base);
+  a.item_off = reinterpret_cast<const int32_t*>(base + items_b);
+  a.num_items = static_cast<int32_t>(n);
+  a.warps_per_cta = info.warps_per_cta;
+  a.part_lse = reinterpret_cast<float*>(base + items_b + off_b);
+  a.part_o = reinterpret_cast<float*>(base + items_b + off_b + lse_b);
+  a.final_mode = info.single_item_per_head;
+  a.merge_sem = nullptr;  // separate merge launch: nothing has to start at zero
+  a.stage_mask = 0;
+  return pg_decode_run(&a, stream);
+}
+
 }  // extern "C"
