@@ -1,28 +1,35 @@
 #!/usr/bin/env python3
-"""PageGauge-B200 decode-attention benchmark (one JSON line on rank 0).
+"""PageGauge-B200 decode benchmark (one JSON line on rank 0).
 
 A step is one PageGauge decode attention over one layer's cache: INT8
 page-affine old pages + the 256-token exact FP16 tail + LSE merge + value-
-centre restore (B=1, context 49,152, Hq/Hkv 32/8,
-head_dim 128, page 16).  Four layers' caches (4 x 101 MB > the 126 MB L2)
-are cycled so every step streams its cache from HBM.
+centre restore, 32 Q / 8 KV heads, head_dim 128, page 16.  The headline
+workload is BASELINE configs[1] (B=1, context 49,152); several layers'
+caches (more bytes than the 126 MB L2) are cycled so every step streams its
+cache from HBM.  The same line carries, under ``workloads``, the B8 ragged
+decode and the fused append step measured in the
+same run (``--only`` skips them).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload b1_49k|b8_ragged|b1_4k] [--split PAGES]
+                    [--workload b1_49k|b8_ragged|b1_4k] [--split PAGES] [--only]
 
-With N > 1 (torchrun, one process per GPU) every rank runs its own replica
-of the workload (the path has no cross-GPU exchange for one request);
-``value`` is the whole-job bytes/s, timed on the device, max over ranks.
+Multi-GPU (torchrun, one process per GPU, no data-path collective):
+B1/49K and B1/4K run one replica per rank; B8 ragged is weak-scaled, a
+global batch of 8*N ragged requests drawn from the seed and split across
+ranks by longest-first bin packing on decode bytes.  ``value`` is the
+whole-job bytes/s: all ranks' bytes over the max-over-ranks device time.
 """
 
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import math
 import os
 import statistics
 import subprocess
+import sys
 import threading
 import time
 
@@ -33,6 +40,7 @@ PAGE = 16
 DIM = 128
 HQ, HKV = 32, 8
 SEED = 20261001
+TAIL_PAGES = 16
 
 
 def parse_args():
@@ -47,19 +55,12 @@ def parse_args():
     p.add_argument("--layers", type=int, default=4)
     p.add_argument("--merge", choices=("kernel", "fused"), default="kernel",
                    help="cross-CTA merge: separate merge kernel or last-CTA merge in the split kernel")
+    p.add_argument("--only", action="store_true", help="skip the secondary workloads")
     p.add_argument("--no-cpu-baseline", action="store_true")
     return p.parse_args()
 
 
-def workload_lengths(name: str, seed: int = SEED) -> list[int]:
-    if name == "b1_49k":
-        return [49152]
-    if name == "b1_4k":
-        return [4096]
-    rng = np.random.default_rng(seed)
-    return [int(x) for x in rng.integers(4096, 32768 + 1, size=8)]
-
-
+# ----------------------------------------------------------------- helpers
 def algorithmic_bytes(old_tokens, exact_tokens, hkv=HKV) -> int:
     """INT8 codes (K+V) + per-(page, head) K/V scales + FP16 exact tokens."""
     total = 0
@@ -67,6 +68,57 @@ def algorithmic_bytes(old_tokens, exact_tokens, hkv=HKV) -> int:
         pages = o // PAGE
         total += 2 * o * hkv * DIM + pages * hkv * 2 * 2 + 2 * e * hkv * DIM * 2
     return total
+
+
+def workload_lengths(name: str, world: int = 1, rank: int = 0):
+    """(this rank's request lengths, global lengths, shards)."""
+    from pagegauge_b200.shard import ragged_lengths, shard_requests
+
+    if name == "b1_49k":
+        return [49152], [49152] * world, None
+    if name == "b1_4k":
+        return [4096], [4096] * world, None
+    glob = ragged_lengths(8 * world, SEED)
+    shards = shard_requests(glob, world)
+    return [glob[i] for i in shards[rank]], glob, shards
+
+
+class Dist:
+    """Barrier / max / sum over ranks (no-ops for one process)."""
+
+    def __init__(self, world: int):
+        self.world = world
+        if world > 1:
+            import torch.distributed as dist
+            self.dist = dist
+        else:
+            self.dist = None
+
+    def barrier(self):
+        if self.dist is not None:
+            self.dist.barrier()
+
+    def reduce(self, x: float, op: str) -> float:
+        if self.dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX if op == "max" else self.dist.ReduceOp.SUM)
+        return float(t.item())
+
+
+def peak_hbm():
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        return float(json.load(open(path))["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def profile_traffic(workload: str):
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "profiles",
+                        f"decode_split_kernel_{workload}_traffic.json")
+    if os.path.exists(path):
+        return json.load(open(path)).get("dram_bytes_per_launch")
+    return None
 
 
 class ClockSampler:
@@ -124,10 +176,11 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+# ------------------------------------------------------------ CPU baseline
 def cpu_baseline(lengths, seconds_budget: float = 15.0) -> dict:
     """The CPU oracle (float64 numpy restatement) on a bounded sample: whole
-    decode steps of the same workload, request by request, until the
-    budget is used (at least one request)."""
+    decode steps of the first request of the workload until the budget is
+    used (at least one step)."""
     from oracle import pagegauge_oracle as O
     from pagegauge_b200.cache import synthetic_dense_cache
 
@@ -135,51 +188,377 @@ def cpu_baseline(lengths, seconds_budget: float = 15.0) -> dict:
     n = lengths[0]
     q, dk, dv = synthetic_dense_cache([n], seed=SEED)
     q, dk, dv = q.numpy(), dk.numpy(), dv.numpy()
-    pages = n // PAGE
-    tail = 16
-    center_k = dk.reshape(-1, HKV, DIM).astype(np.float32).mean(0).astype(np.float16)
-    center_v = dv.reshape(-1, HKV, DIM).astype(np.float32).mean(0).astype(np.float16)
+    pages = -(-n // PAGE)
+    tail = min(TAIL_PAGES, pages)
+    center_k = dk.reshape(-1, HKV, DIM)[:n].astype(np.float32).mean(0).astype(np.float16)
+    center_v = dv.reshape(-1, HKV, DIM)[:n].astype(np.float32).mean(0).astype(np.float16)
     ck, sk = O.quantize_pages_bulk(dk, center_k)
     cv, sv = O.quantize_pages_bulk(dv, center_v)
     ek = (dk[pages - tail:].astype(np.float32) - center_k.astype(np.float32)).astype(np.float16)
     ev = (dv[pages - tail:].astype(np.float32) - center_v.astype(np.float32)).astype(np.float16)
     old = list(range(pages - tail))
+    exact_tokens = n - len(old) * PAGE
     steps = 0
     t0 = time.perf_counter()
     while True:
         O.page_gauge_decode(q[0], ck, cv, sk, sv, old, len(old) * PAGE, ek, ev, list(range(tail)),
-                            tail * PAGE, center_v, 1.0 / math.sqrt(DIM))
+                            exact_tokens, center_v, 1.0 / math.sqrt(DIM))
         steps += 1
         if time.perf_counter() - t0 > seconds_budget or steps >= 20:
             break
     dt = (time.perf_counter() - t0) / steps
-    nbytes = algorithmic_bytes([len(old) * PAGE], [tail * PAGE])
+    nbytes = algorithmic_bytes([len(old) * PAGE], [exact_tokens])
     return {"value": nbytes / dt / 1e9, "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
-            "sample": f"{steps} full decode steps of B=1 ctx {n} (float64 numpy oracle), "
-                      f"{dt * 1e3:.1f} ms/step"}
+            "sample": f"{steps} full decode steps of one request, ctx {n} (float64 numpy "
+                      f"oracle, {torch.get_num_threads()} threads), {dt * 1e3:.1f} ms/step"}
 
 
 def run_reference(args) -> None:
+    """The reference arm: the CPU restatement of the reference's path (the
+    oracle port) on this box's host cores, rank 0 only."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    lengths = workload_lengths(args.workload)
-    if args.workload == "b8_ragged":
-        lengths = lengths[:1]  # bounded: one request of the ragged batch per step
-    budget = 10.0
-    base = cpu_baseline(lengths, seconds_budget=budget)
+    lengths, _, _ = workload_lengths(args.workload)
+    base = cpu_baseline(lengths[:1], seconds_budget=10.0)
     line = {
         "impl": "reference", "metric": f"decode-attn HBM GB/s ({args.workload})",
         "value": base["value"], "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int8/fp16 storage, f64 math",
-        "data": "synthetic", "config": {"workload": args.workload, "lengths": lengths},
+        "data": "synthetic", "config": {"workload": args.workload, "lengths": lengths[:1]},
         "cpu_baseline": base,
         "e2e": {"value": base["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
+# --------------------------------------------------------- attention bench
+class AttentionBench:
+    """One workload's caches (``layers`` copies), its plan, and CUDA graphs
+    of the public-API decode step."""
+
+    def __init__(self, lengths, layers: int, split: int, fused_merge: bool, seed: int):
+        from pagegauge_b200 import scheduler
+        from pagegauge_b200.cache import build_gauge_cache, rope_tables, synthetic_dense_cache
+        from pagegauge_b200.decode import PageGaugeDecode
+
+        self.lengths = lengths
+        self.layers = max(1, layers)
+        self.fused = fused_merge
+        cap = max(-(-n // PAGE) for n in lengths)
+        self.caches = []
+        self.q = self.tables = None
+        for layer in range(self.layers):
+            qi, dk, dv = synthetic_dense_cache(lengths, seed=seed + layer, device="cuda")
+            cache, tables = build_gauge_cache(dk, dv, lengths, capacity_pages=cap)
+            del dk, dv
+            self.caches.append(cache)
+            self.q = qi if self.q is None else self.q
+            self.tables = tables
+        self.capacity_pages = cap
+        torch.cuda.synchronize()
+        if split < 0:
+            split = scheduler.lookup(len(lengths), max(lengths))
+        self.ws = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+        self.dec = PageGaugeDecode(self.ws)
+        t = self.tables
+        self.dec.plan(t.old_indptr, t.old_indices, t.exact_indptr, t.exact_indices,
+                      t.exact_last_page_len, HQ, HKV, old_split_pages=split, exact_split_pages=0)
+        self.plan = self.dec.work_plan
+        self.out = torch.empty_like(self.q)
+        self.nbytes = algorithmic_bytes(t.old_tokens, t.exact_tokens)
+        self.launches_per_step = 1 if (self.plan.single and self.plan.num_items) else 2
+        self.rope = rope_tables(cap * PAGE, device="cuda")
+        self.stream = torch.cuda.Stream()
+        self.chunk = 8 * self.layers
+
+    def step(self, layer: int, q=None, out=None):
+        c = self.caches[layer]
+        self.dec.run(self.q if q is None else q, c.key_codes, c.value_codes, c.key_scales,
+                     c.value_scales, c.exact_key, c.exact_value, c.value_center,
+                     out=self.out if out is None else out, fused_merge=self.fused)
+
+    def capture(self):
+        with torch.cuda.stream(self.stream):
+            for layer in range(self.layers):
+                self.step(layer)
+            torch.cuda.synchronize()
+            self.chunk_graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.chunk_graph, stream=self.stream):
+                for i in range(self.chunk):
+                    self.step(i % self.layers)
+            self.single = []
+            for layer in range(self.layers):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=self.stream):
+                    self.step(layer)
+                self.single.append(g)
+        torch.cuda.synchronize()
+
+    def run_steps(self, k: int) -> None:
+        """Exactly k steps cycling the layers: graphs of ``chunk`` steps,
+        then single-step graphs for the remainder."""
+        for _ in range(k // self.chunk):
+            self.chunk_graph.replay()
+        for i in range(k - k % self.chunk, k):
+            self.single[i % self.layers].replay()
+
+    def time_steps(self, steps: int, warmup: int, dist: Dist, clocks=None) -> float:
+        self.run_steps(max(warmup, 3))
+        torch.cuda.synchronize()
+        dist.barrier()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ctx = clocks if clocks is not None else _Null()
+        with ctx:
+            torch.cuda.synchronize()
+            start.record()
+            self.run_steps(steps)
+            end.record()
+            torch.cuda.synchronize()
+        dist.barrier()
+        return dist.reduce(start.elapsed_time(end) / steps, "max")
+
+    def kernel_ms(self, steps: int) -> float:
+        """The split-KV decode kernel alone (partials only), graphs of
+        ``chunk`` launches cycling the layers, CUDA events on the replay
+        stream."""
+        from pagegauge_b200 import _lib
+        from pagegauge_b200 import wrapper as W
+
+        plan, dec, q, out = self.plan, self.dec, self.q, self.out
+        lib = _lib.load()
+        blocks = []
+        for c in self.caches:
+            a = _lib.PgDecodeArgs()
+            a.q = q.data_ptr()
+            a.q_stride_b, a.q_stride_h = q.stride(0), q.stride(1)
+            a.batch, a.kv_heads, a.group = plan.batch, plan.kv_heads, plan.group
+            a.sm_scale = dec.sm_scale
+            a.seg[0] = W._segment(c.key_codes, c.value_codes, dec._old_indices, dec._old_last,
+                                  c.key_scales, c.value_scales)
+            a.seg[1] = W._segment(c.exact_key, c.exact_value, dec._exact_indices, dec._exact_last)
+            a.items, a.item_off, a.num_items = plan.items_ptr, plan.off_ptr, plan.num_items
+            a.warps_per_cta = plan.warps
+            a.part_o, a.part_lse = plan.o_ptr, plan.lse_ptr
+            a.final_mode = 1 if plan.single else 0
+            a.out = out.data_ptr()
+            a.out_stride_b, a.out_stride_h = out.stride(0), out.stride(1)
+            a.stage_mask = 1  # split kernel only
+            blocks.append(a)
+        with torch.cuda.stream(self.stream):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=self.stream):
+                for i in range(self.chunk):
+                    _lib.check(lib.pg_decode_run(ctypes.byref(blocks[i % self.layers]),
+                                                 torch.cuda.current_stream().cuda_stream))
+        torch.cuda.synchronize()
+        g.replay()
+        reps = max(4, steps // self.chunk)
+        ks, ke = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        ks.record()
+        for _ in range(reps):
+            g.replay()
+        ke.record()
+        torch.cuda.synchronize()
+        del g
+        return ks.elapsed_time(ke) / (reps * self.chunk)
+
+    def e2e(self, steps: int, dist: Dist) -> dict:
+        """End to end through the public API with host buffers: per step
+        the new token's q/k/v of every request go host->device from pinned
+        memory, the fused RoPE/append (per-request positions) writes the
+        exact ring and closes the page of requests at a page end, the
+        decode runs, and the output comes back to pinned host memory.
+        Reported for a CUDA graph of that public-API sequence (how the
+        reference drives its decode step) and for eager calls."""
+        from pagegauge_b200.runtime import load_append_extension
+
+        ext = load_append_extension()
+        B = len(self.lengths)
+        g = torch.Generator().manual_seed(SEED + 77)
+        hq = torch.randn(B, HQ, DIM, generator=g).half().pin_memory()
+        hk = torch.randn(B, HKV, DIM, generator=g).half().pin_memory()
+        hv = torch.randn(B, HKV, DIM, generator=g).half().pin_memory()
+        hout = torch.empty(B, HQ, DIM, dtype=torch.float16).pin_memory()
+        dq = torch.empty(B, HQ, DIM, dtype=torch.float16, device="cuda")
+        dk = torch.empty(B, HKV, DIM, dtype=torch.float16, device="cuda")
+        dv = torch.empty_like(dk)
+        rq = torch.empty_like(dq)
+        out = torch.empty_like(dq)
+        # Each step re-appends the last token of every request (its page
+        # stays in the exact window), so the cache shape is unchanged.
+        positions = torch.tensor([n - 1 for n in self.lengths], dtype=torch.int32, device="cuda")
+        cos, sin = self.rope
+
+        def one(layer: int):
+            c = self.caches[layer]
+            dq.copy_(hq, non_blocking=True)
+            dk.copy_(hk, non_blocking=True)
+            dv.copy_(hv, non_blocking=True)
+            ext.rope_append_page_gauge_batched(dq, dk, dv, cos, sin, positions, c.key_center,
+                                               c.value_center, rq, c.exact_key, c.exact_value,
+                                               c.key_codes, c.value_codes, c.key_scales,
+                                               c.value_scales, 0)
+            self.step(layer, q=rq, out=out)
+            hout.copy_(out, non_blocking=True)
+
+        def timed(fn, n):
+            for i in range(3):
+                fn(i)
+            torch.cuda.synchronize()
+            dist.barrier()
+            es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            es.record()
+            for i in range(n):
+                fn(i)
+            ee.record()
+            torch.cuda.synchronize()
+            dist.barrier()
+            return dist.reduce(es.elapsed_time(ee) / n, "max")
+
+        with torch.cuda.stream(self.stream):
+            eager_ms = timed(lambda i: one(i % self.layers), steps)
+            graph_ms, err = None, None
+            try:
+                graphs = []
+                for layer in range(self.layers):
+                    gr = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(gr, stream=self.stream):
+                        one(layer)
+                    graphs.append(gr)
+                torch.cuda.synchronize()
+                ok = 1.0
+            except RuntimeError as exc:  # capture of pinned copies refused
+                ok, err = 0.0, str(exc).splitlines()[0][:200]
+                torch.cuda.synchronize()
+            if dist.reduce(ok, "sum") == dist.world:
+                graph_ms = timed(lambda i: graphs[i % self.layers].replay(), steps)
+        h2d = (hq.numel() + hk.numel() + hv.numel()) * 2
+        return {"eager_ms": eager_ms, "graph_ms": graph_ms, "graph_error": err,
+                "h2d": h2d, "d2h": hout.numel() * 2, "launches_per_step": 1 + self.launches_per_step}
+
+
+class _Null:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        return False
+
+
+# ------------------------------------------------------------ append bench
+def measure_append(dist: Dist, batch: int = 8, layers: int = 32, samples: int = 100) -> dict:
+    """one decode step's fused RoPE + centred append +
+    page finalisation for B=8 requests in each of 32 layers (one launch per
+    layer), half of the requests at the last token of a page (position %
+    16 == 15, so their page is finalised to INT8 in the same launch), the
+    other half mid-page; against the fused RoPE + FP16 append comparator
+    on the same inputs.  Cache-neutral: a 256 MiB scrub before every sample;
+    samples alternate A/B then B/A; p50."""
+    from pagegauge_b200.cache import rope_tables
+    from pagegauge_b200.runtime import load_append_extension
+
+    ext = load_append_extension()
+    ppr, ring = 64, TAIL_PAGES
+    positions = torch.tensor([16 * (4 * r + 3) + (15 if r % 2 == 0 else 7) for r in range(batch)],
+                             dtype=torch.int32, device="cuda")
+    closes = int(((positions % 16) == 15).sum())
+    cos, sin = rope_tables(ppr * PAGE, device="cuda")
+    g = torch.Generator(device="cuda").manual_seed(SEED + 3)
+    per = []
+    for _ in range(layers):
+        offset = torch.randn(HKV, DIM, generator=g, device="cuda")
+        d = dict(
+            q=torch.randn(batch, HQ, DIM, generator=g, device="cuda").half(),
+            k=(torch.randn(batch, HKV, DIM, generator=g, device="cuda") + offset).half(),
+            v=(torch.randn(batch, HKV, DIM, generator=g, device="cuda") + 0.5 * offset).half(),
+            kc=offset.half().expand(batch, HKV, DIM).contiguous(),
+            vc=(0.5 * offset).half().expand(batch, HKV, DIM).contiguous(),
+            rq=torch.empty(batch, HQ, DIM, dtype=torch.float16, device="cuda"),
+            ek=torch.zeros(batch * ring, PAGE, HKV, DIM, dtype=torch.float16, device="cuda"),
+            codes_k=torch.zeros(batch * ppr, PAGE, HKV, DIM, dtype=torch.int8, device="cuda"),
+            sk=torch.zeros(batch * ppr, HKV, dtype=torch.float16, device="cuda"),
+            fk=torch.zeros(batch * ppr, PAGE, HKV, DIM, dtype=torch.float16, device="cuda"),
+        )
+        d["ev"] = torch.zeros_like(d["ek"])
+        d["codes_v"] = torch.zeros_like(d["codes_k"])
+        d["sv"] = torch.zeros_like(d["sk"])
+        d["fv"] = torch.zeros_like(d["fk"])
+        d["rq16"] = torch.empty_like(d["rq"])
+        per.append(d)
+
+    def gauge():
+        for d in per:
+            ext.rope_append_page_gauge_batched(d["q"], d["k"], d["v"], cos, sin, positions, d["kc"],
+                                               d["vc"], d["rq"], d["ek"], d["ev"], d["codes_k"],
+                                               d["codes_v"], d["sk"], d["sv"], 0)
+
+    def fp16():
+        for d in per:
+            ext.rope_append_fp16_batched(d["q"], d["k"], d["v"], cos, sin, positions, d["rq16"],
+                                         d["fk"], d["fv"])
+
+    stream = torch.cuda.Stream()
+    graphs = {}
+    with torch.cuda.stream(stream):
+        for name, fn in (("gauge", gauge), ("fp16", fp16)):
+            fn()
+            torch.cuda.synchronize()
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=stream):
+                fn()
+            graphs[name] = gr
+        torch.cuda.synchronize()
+        scrub = torch.zeros(256 << 18, dtype=torch.int32, device="cuda")
+        times = {"gauge": [], "fp16": []}
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        dist.barrier()
+        for i in range(samples):
+            order = ("gauge", "fp16") if i % 2 == 0 else ("fp16", "gauge")
+            for name in order:
+                scrub.add_(1)
+                ev[0].record()
+                graphs[name].replay()
+                ev[1].record()
+                ev[1].synchronize()
+                times[name].append(ev[0].elapsed_time(ev[1]))
+        hot = {}
+        for name in ("gauge", "fp16"):
+            graphs[name].replay()
+            torch.cuda.synchronize()
+            ev[0].record()
+            for _ in range(50):
+                graphs[name].replay()
+            ev[1].record()
+            ev[1].synchronize()
+            hot[name] = ev[0].elapsed_time(ev[1]) / 50
+        dist.barrier()
+    del graphs
+    p50 = {k: dist.reduce(statistics.median(v), "max") for k, v in times.items()}
+    hot = {k: dist.reduce(v, "max") for k, v in hot.items()}
+    # Algorithmic bytes per layer: q read + rotated q write, k/v read,
+    # centres, one cos/sin row per request, ring writes, and per closed page
+    # the ring page re-read, the codes write and the two scales.
+    b = batch
+    per_layer = (2 * b * HQ * DIM * 2 + 2 * b * HKV * DIM * 2 + 2 * b * HKV * DIM * 2
+                 + 2 * b * DIM * 2 + 2 * b * HKV * DIM * 2
+                 + closes * HKV * (2 * PAGE * DIM * 2 + 2 * PAGE * DIM + 2 * 2))
+    return {
+        "batch": batch, "layers": layers, "closing_requests": closes,
+        "us_per_step": p50["gauge"] * 1e3, "us_per_layer": p50["gauge"] * 1e3 / layers,
+        "fp16_append_us_per_step": p50["fp16"] * 1e3,
+        "increment_us_per_step": (p50["gauge"] - p50["fp16"]) * 1e3,
+        "hot_us_per_step": hot["gauge"] * 1e3, "hot_fp16_us_per_step": hot["fp16"] * 1e3,
+        "algorithmic_bytes_per_layer": per_layer,
+        "achieved_gbs": per_layer * layers / (p50["gauge"] * 1e-3) / 1e9,
+        "timing": f"p50 of {samples} cache-neutral samples (256 MiB scrub before each), "
+                  "A/B then B/A order; one CUDA graph of 32 launches per sample",
+    }
+
+
+# -------------------------------------------------------------------- main
 def main() -> None:
     args = parse_args()
     if args.impl == "reference":
@@ -189,201 +568,73 @@ def main() -> None:
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
-    dist = None
     if world > 1:
         import datetime
 
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
+        import torch.distributed as tdist
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                 device_id=torch.device("cuda", local))
+    dist = Dist(world)
 
-    from pagegauge_b200 import scheduler
-    from pagegauge_b200.cache import build_gauge_cache, synthetic_dense_cache
-    from pagegauge_b200.decode import PageGaugeDecode
-    from pagegauge_b200.runtime import load_append_extension, read_device_error
+    from pagegauge_b200.runtime import read_device_error
 
-    lengths = workload_lengths(args.workload)
-    layers = max(1, args.layers)
-    caches = []
-    q = tables = None
-    for layer in range(layers):
-        qi, dk, dv = synthetic_dense_cache(lengths, seed=SEED + layer + 1000 * rank, device="cuda")
-        cache, tables = build_gauge_cache(dk, dv, lengths)
-        del dk, dv
-        caches.append(cache)
-        q = qi if q is None else q
-    torch.cuda.synchronize()
-    split = args.split
-    if split < 0:
-        split = scheduler.lookup(len(lengths), max(lengths))
-    ws = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
-    dec = PageGaugeDecode(ws)
-    dec.plan(tables.old_indptr, tables.old_indices, tables.exact_indptr, tables.exact_indices,
-             tables.exact_last_page_len, HQ, HKV, old_split_pages=split, exact_split_pages=0)
-    out = torch.empty_like(q)
+    peak, peak_src = peak_hbm()
+    lengths, glob, shards = workload_lengths(args.workload, world, rank)
+    bench = AttentionBench(lengths, args.layers, args.split, args.merge == "fused",
+                           seed=SEED + 1000 * rank)
+    bench.capture()
+    clocks = ClockSampler(local)
+    ms = bench.time_steps(args.steps, args.warmup, dist, clocks)
+    total_bytes = dist.reduce(float(bench.nbytes), "sum")
+    value = total_bytes / (ms * 1e-3) / 1e9
+    kernel_ms = dist.reduce(bench.kernel_ms(args.steps), "max")
+    achieved = bench.nbytes / (kernel_ms * 1e-3) / 1e9
+    e2e = bench.e2e(max(10, args.steps // 4), dist)
+    e2e_ms = e2e["graph_ms"] if e2e["graph_ms"] is not None else e2e["eager_ms"]
 
-    def step(layer: int):
-        c = caches[layer]
-        dec.run(q, c.key_codes, c.value_codes, c.key_scales, c.value_scales, c.exact_key,
-                c.exact_value, c.value_center, out=out, fused_merge=args.merge == "fused")
-
-    # Steps are captured into CUDA graphs (plan stays outside capture, as in
-    # the reference): one graph of CHUNK consecutive steps cycling the
-    # layers, replayed K // CHUNK times, plus single-step graphs for the
-    # remainder, so host launch overhead is amortised and exactly K steps
-    # are timed on the device.
-    stream = torch.cuda.Stream()
-    chunk = 8 * layers
-    with torch.cuda.stream(stream):
-        for layer in range(layers):
-            step(layer)
-        torch.cuda.synchronize()
-        chunk_graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(chunk_graph, stream=stream):
-            for i in range(chunk):
-                step(i % layers)
-        single = []
-        for layer in range(layers):
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=stream):
-                step(layer)
-            single.append(g)
-    torch.cuda.synchronize()
-
-    def run_steps(k: int) -> None:
-        for _ in range(k // chunk):
-            chunk_graph.replay()
-        for i in range(k - k % chunk, k):
-            single[i % layers].replay()
-
-    run_steps(max(args.warmup, 3))
-    torch.cuda.synchronize()
-    if dist is not None:
-        dist.barrier()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
-        torch.cuda.synchronize()
-        start.record()
-        run_steps(args.steps)
-        end.record()
-        torch.cuda.synchronize()
-    if dist is not None:
-        dist.barrier()
-    ms = start.elapsed_time(end) / args.steps
-    if dist is not None:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    nbytes = algorithmic_bytes(tables.old_tokens, tables.exact_tokens)
-    value = world * nbytes / (ms * 1e-3) / 1e9
-    err = read_device_error()
-
-    # Dominant kernel alone: the split-KV decode launch (partials only), one
-    # graph per layer, timed with events on the replay stream.
-    plan = dec.work_plan
-    lib_launches = 1 if (plan.single and plan.num_items) else 2
-    from pagegauge_b200 import wrapper as W
-
-    def decode_only(layer: int):
-        c = caches[layer]
-        segs = (W._segment(c.key_codes, c.value_codes, dec._old_indices, dec._old_last,
-                           c.key_scales, c.value_scales),
-                W._segment(c.exact_key, c.exact_value, dec._exact_indices, dec._exact_last))
-        import ctypes
-        from pagegauge_b200 import _lib
-        a = _lib.PgDecodeArgs()
-        a.q = q.data_ptr()
-        a.q_stride_b, a.q_stride_h = q.stride(0), q.stride(1)
-        a.batch, a.kv_heads, a.group = plan.batch, plan.kv_heads, plan.group
-        a.sm_scale = dec.sm_scale
-        a.seg[0], a.seg[1] = segs
-        a.items, a.item_off, a.num_items, a.warps_per_cta = plan.items_ptr, plan.off_ptr, plan.num_items, plan.warps
-        a.part_o, a.part_lse = plan.o_ptr, plan.lse_ptr
-        a.final_mode = 1 if plan.single else 0
-        a.out = out.data_ptr()
-        a.out_stride_b, a.out_stride_h = out.stride(0), out.stride(1)
-        a.stage_mask = 1  # split kernel only (partials; no fused merge)
-        _lib.check(_lib.load().pg_decode_run(ctypes.byref(a), torch.cuda.current_stream().cuda_stream))
-
-    with torch.cuda.stream(stream):
-        kernel_graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(kernel_graph, stream=stream):
-            for i in range(chunk):
-                decode_only(i % layers)
-    torch.cuda.synchronize()
-    kernel_graph.replay()
-    ks, ke = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    kreps = max(4, args.steps // chunk)
-    ks.record()
-    for _ in range(kreps):
-        kernel_graph.replay()
-    ke.record()
-    torch.cuda.synchronize()
-    kernel_ms = ks.elapsed_time(ke) / (kreps * chunk)
-
-    peaks_path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "MEASURED_PEAKS.json")
-    if os.path.exists(peaks_path):
-        peak = json.load(open(peaks_path))["hbm_gbs"]
-        peak_src = "measured"
-    else:
-        peak, peak_src = 6650.0, "fallback"
-    achieved = nbytes / (kernel_ms * 1e-3) / 1e9
-    traffic_path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "profiles",
-                                f"decode_split_kernel_{args.workload}_traffic.json")
-    traffic = None
-    if os.path.exists(traffic_path):
-        traffic = json.load(open(traffic_path)).get("dram_bytes_per_launch")
-
-    # End to end through the public API with host buffers: per step the new
-    # token's q/k/v go host->device (pinned), the fused append writes the
-    # exact ring, the decode runs, and the output comes back to the host.
-    ext = load_append_extension()
-    pos = lengths[0] - 1
-    cos, sin = (torch.ones(DIM, dtype=torch.float16, device="cuda"),
-                torch.zeros(DIM, dtype=torch.float16, device="cuda"))
-    hq_in = torch.randn(len(lengths), HQ, DIM).half().pin_memory()
-    hk_in = torch.randn(len(lengths), HKV, DIM).half().pin_memory()
-    hv_in = torch.randn(len(lengths), HKV, DIM).half().pin_memory()
-    h_out = torch.empty(len(lengths), HQ, DIM, dtype=torch.float16).pin_memory()
-    dq, dk1, dv1 = torch.empty_like(q), torch.empty(len(lengths), HKV, DIM, dtype=torch.float16, device="cuda"), \
-        torch.empty(len(lengths), HKV, DIM, dtype=torch.float16, device="cuda")
-    rq = torch.empty_like(q)
-    e2e_steps = max(10, args.steps // 4)
-
-    def e2e_step(i):
-        c = caches[i % layers]
-        dq.copy_(hq_in, non_blocking=True)
-        dk1.copy_(hk_in, non_blocking=True)
-        dv1.copy_(hv_in, non_blocking=True)
-        # The append rewrites the last token of the (exact) last page, which
-        # also exercises the page-close finalisation every step.
-        ext.rope_append_page_gauge(dq, dk1, dv1, cos, sin, c.key_center, c.value_center, rq,
-                                   c.exact_key, c.exact_value, c.key_codes, c.value_codes,
-                                   c.key_scales, c.value_scales, 0, pos)
-        dec.run(rq, c.key_codes, c.value_codes, c.key_scales, c.value_scales, c.exact_key,
-                c.exact_value, c.value_center, out=out)
-        h_out.copy_(out, non_blocking=True)
-
-    e2e_value = None
-    if len(lengths) == 1:
-        for i in range(3):
-            e2e_step(i)
-        torch.cuda.synchronize()
-        es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        es.record()
-        for i in range(e2e_steps):
-            e2e_step(i)
-        ee.record()
-        torch.cuda.synchronize()
-        e2e_ms = es.elapsed_time(ee) / e2e_steps
-        e2e_value = world * nbytes / (e2e_ms * 1e-3) / 1e9
+    workloads = {}
+    if not args.only and args.workload == "b1_49k":
+        b8_len, b8_glob, b8_shards = workload_lengths("b8_ragged", world, rank)
+        b8 = AttentionBench(b8_len, args.layers, -1, False, seed=SEED + 1000 * rank + 500)
+        b8.capture()
+        b8_steps = max(200, args.steps // 10)
+        b8_ms = b8.time_steps(b8_steps, args.warmup, dist)
+        b8_total = dist.reduce(float(b8.nbytes), "sum")
+        b8_kms = dist.reduce(b8.kernel_ms(b8_steps), "max")
+        workloads["b8_ragged"] = {
+            "metric": "decode-attn HBM GB/s (b8_ragged)", "unit": "GB/s",
+            "value": round(b8_total / (b8_ms * 1e-3) / 1e9, 2), "us_per_step": b8_ms * 1e3,
+            "steps": b8_steps, "kernel_us": b8_kms * 1e3,
+            "roofline_frac": round(b8.nbytes / (b8_kms * 1e-3) / 1e9 / peak, 4),
+            "algorithmic_bytes_per_step_per_rank": b8.nbytes,
+            "global_batch": len(b8_glob), "lengths_rank0": b8_len,
+            "shards": b8_shards, "split_pages": b8.plan.split_pages[0],
+            "work_items": b8.plan.num_items, "scaling": "weak",
+        }
+        attn_layer_us = b8_ms * 1e3
+        del b8
+        torch.cuda.empty_cache()
+        app = measure_append(dist)
+        app["attention_us_per_layer_b8"] = attn_layer_us
+        app["pct_of_attention_step"] = round(100 * app["us_per_layer"] / attn_layer_us, 2)
+        app["increment_pct_of_attention_step"] = round(
+            100 * app["increment_us_per_step"] / app["layers"] / attn_layer_us, 2)
+        workloads["append_b8_32l"] = app
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(lengths if len(lengths) == 1 else lengths[:1])
+        cpu = cpu_baseline(lengths[:1])
+    err = read_device_error()
 
     if rank == 0:
+        cfg = {"workload": args.workload, "lengths": lengths, "hq": HQ, "hkv": HKV,
+               "head_dim": DIM, "page": PAGE, "exact_tail_tokens": TAIL_PAGES * PAGE,
+               "split_pages": bench.plan.split_pages[0], "work_items": bench.plan.num_items,
+               "layers_cycled": bench.layers,
+               "l2": f"{bench.layers} layer caches cycled "
+                     f"({bench.layers * bench.nbytes / 1e6:.0f} MB > 126 MB L2)",
+               "parallelism": (f"replicas x{world}" if shards is None
+                               else f"requests sharded over {world} (weak, global batch {len(glob)})")}
         line = {
             "metric": f"decode-attn HBM GB/s ({args.workload})",
             "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -391,31 +642,32 @@ def main() -> None:
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "int8 codes + fp16 tail, fp16 mma / fp32 softmax",
             "data": "synthetic (seeded; K=RoPE(N(mu,1)), mu~N(0,2); V,Q~N(0,1))",
-            "config": {"workload": args.workload, "lengths": lengths, "hq": HQ, "hkv": HKV,
-                       "head_dim": DIM, "page": PAGE, "exact_tail_tokens": 256,
-                       "split_pages": plan.split_pages[0], "work_items": plan.num_items,
-                       "layers_cycled": layers,
-                       "l2": f"{layers} layer caches cycled ({layers * nbytes / 1e6:.0f} MB > 126 MB L2)",
-                       "parallelism": f"replicas x{world}"},
-            "algorithmic_bytes_per_step": nbytes,
+            "config": cfg,
+            "algorithmic_bytes_per_step": bench.nbytes,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
-                         "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic,
-                         "peak_source": peak_src, "kernel": "pg_decode_split_kernel",
-                         "kernel_us": kernel_ms * 1e3},
-            "gpu_launches": lib_launches * args.steps,
-            "e2e": None if e2e_value is None else {
-                "value": round(e2e_value, 2), "unit": "GB/s",
-                "h2d_bytes_per_step": hq_in.numel() * 2 + hk_in.numel() * 2 + hv_in.numel() * 2,
-                "d2h_bytes_per_step": h_out.numel() * 2},
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "traffic": profile_traffic(args.workload), "peak_source": peak_src,
+                         "kernel": "pg_decode_split_kernel", "kernel_us": kernel_ms * 1e3},
+            "gpu_launches": bench.launches_per_step * args.steps,
+            "e2e": {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
+                    "us_per_step": e2e_ms * 1e3,
+                    "mode": ("CUDA graph of the public-API step" if e2e["graph_ms"] is not None
+                             else "eager public-API calls"),
+                    "eager_value": round(total_bytes / (e2e["eager_ms"] * 1e-3) / 1e9, 2),
+                    "eager_us_per_step": e2e["eager_ms"] * 1e3,
+                    "graph_error": e2e["graph_error"],
+                    "launches_per_step": e2e["launches_per_step"]},
             "cpu_baseline": cpu,
             "clocks": clocks.summary(),
             "device_guard": err,
+            "workloads": workloads,
         }
         print(json.dumps(line), flush=True)
-    if dist is not None:
-        del chunk_graph, single, kernel_graph
+    if world > 1:
+        del bench
         dist.barrier()
-        dist.destroy_process_group()
+        dist.dist.destroy_process_group()
 
 
 if __name__ == "__main__":

@@ -104,6 +104,38 @@ int32_t pg_rope_append_page_gauge(
     const int32_t* device_position, int64_t rope_row_stride,
     int64_t rope_rows, void* stream);
 
+/* Per-request-position forms of the two appends above: positions is a
+ * device int32 [B] tensor (request r appends at positions[r]) and
+ * cosine/sine are [rope_rows,128] tables.  A ragged serving batch has one
+ * position per request; the reference's extension takes one position for
+ * the whole batch, and its per-request append is the Triton
+ * append_finalize_page_gauge (scripts/benchmark_page_gauge_overheads.py:113-205,
+ * page ids and in-page offsets per request, no RoPE).  An out-of-range
+ * position skips that request and sets the device guard word.              */
+int32_t pg_rope_append_fp16_batched(const void* query, const void* key,
+                                    const void* value, const void* cosine,
+                                    const void* sine, void* rotated_query,
+                                    void* key_pages, void* value_pages,
+                                    int64_t query_batch_stride,
+                                    int64_t key_batch_stride,
+                                    int64_t value_batch_stride, int32_t batch,
+                                    int32_t query_heads, int32_t kv_heads,
+                                    int64_t num_pages, const int32_t* positions,
+                                    int64_t rope_row_stride, int64_t rope_rows,
+                                    void* stream);
+
+int32_t pg_rope_append_page_gauge_batched(
+    const void* query, const void* key, const void* value,
+    const void* cosine, const void* sine, const void* key_center,
+    const void* value_center, void* rotated_query, void* exact_key_pages,
+    void* exact_value_pages, void* key_codes, void* value_codes,
+    void* key_scales, void* value_scales, int64_t query_batch_stride,
+    int64_t key_batch_stride, int64_t value_batch_stride,
+    int64_t center_batch_stride, int32_t batch, int32_t query_heads,
+    int32_t kv_heads, int64_t exact_pages, int64_t code_pages,
+    int64_t exact_sink_pages, const int32_t* positions,
+    int64_t rope_row_stride, int64_t rope_rows, void* stream);
+
 /* Exact FP16 tail attention merged into (old_output, old_lse) in place,
  * plus the value centre.  exact_page_indices [B*n] int32,
  * exact_last_page_len [B] int32 (device), old_lse base 2 [B,Hq].          */

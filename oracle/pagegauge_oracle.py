@@ -187,6 +187,40 @@ def rope_append_page_gauge(
     return rq
 
 
+def rope_append_page_gauge_batched(
+    state: GaugeState,
+    q: np.ndarray,
+    k: np.ndarray,
+    v: np.ndarray,
+    cos_table: np.ndarray,
+    sin_table: np.ndarray,
+    key_center: np.ndarray,
+    value_center: np.ndarray,
+    exact_sink_pages: int,
+    positions,
+) -> np.ndarray:
+    """``rope_append_page_gauge`` with one position per request: request r
+    runs the single-request step at ``positions[r]`` on its own slice of the
+    request-major storage.  Per-request page ids and in-page offsets are the
+    reference's Triton append_finalize_page_gauge
+    (scripts/benchmark_page_gauge_overheads.py:113-205); the arithmetic per
+    request is the extension kernel's (.cu:244-383)."""
+    B = q.shape[0]
+    exact_ppr = state.exact_k.shape[0] // B
+    code_ppr = state.codes_k.shape[0] // B
+    shared = np.asarray(key_center).ndim == 2
+    out = np.empty_like(np.asarray(q, np.float16))
+    for r, pos in enumerate(positions):
+        e, c = slice(r * exact_ppr, (r + 1) * exact_ppr), slice(r * code_ppr, (r + 1) * code_ppr)
+        sub = GaugeState(state.exact_k[e], state.exact_v[e], state.codes_k[c], state.codes_v[c],
+                         state.scales_k[c], state.scales_v[c])
+        kc = key_center if shared else key_center[r:r + 1]
+        vc = value_center if shared else value_center[r:r + 1]
+        out[r] = rope_append_page_gauge(sub, q[r:r + 1], k[r:r + 1], v[r:r + 1], cos_table[pos],
+                                        sin_table[pos], kc, vc, exact_sink_pages, int(pos))[0]
+    return out
+
+
 def rope_append_fp16(
     key_pages: np.ndarray,
     value_pages: np.ndarray,
@@ -208,6 +242,19 @@ def rope_append_fp16(
         key_pages[r * ppr + page, token] = rk[r]
         value_pages[r * ppr + page, token] = v[r]
     return rq
+
+
+def rope_append_fp16_batched(key_pages, value_pages, q, k, v, cos_table, sin_table, positions):
+    """FP16 comparator with one position per request (request r writes page
+    ``r*ppr + positions[r]//16``)."""
+    B = q.shape[0]
+    ppr = key_pages.shape[0] // B
+    out = np.empty_like(np.asarray(q, np.float16))
+    for r, pos in enumerate(positions):
+        sl = slice(r * ppr, (r + 1) * ppr)
+        out[r] = rope_append_fp16(key_pages[sl], value_pages[sl], q[r:r + 1], k[r:r + 1],
+                                  v[r:r + 1], cos_table[pos], sin_table[pos], int(pos))[0]
+    return out
 
 
 # --------------------------------------------------------------- attention

@@ -62,6 +62,11 @@ _SIGNATURES = {
         c_i32,
         [c_vp] * 14 + [c_i64] * 4 + [c_i32] * 3 + [c_i64] * 4 + [c_vp, c_i64, c_i64, c_vp],
     ),
+    "pg_rope_append_fp16_batched": (c_i32, [c_vp] * 8 + [c_i64] * 3 + [c_i32] * 3 + [c_i64, c_vp, c_i64, c_i64, c_vp]),
+    "pg_rope_append_page_gauge_batched": (
+        c_i32,
+        [c_vp] * 14 + [c_i64] * 4 + [c_i32] * 3 + [c_i64] * 3 + [c_vp, c_i64, c_i64, c_vp],
+    ),
     "pg_exact_tail_merge_center": (
         c_i32,
         [c_vp, c_vp, c_vp, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, c_i64, c_i32, c_i32, c_i32,

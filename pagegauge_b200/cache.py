@@ -74,14 +74,21 @@ class DecodeTables:
 
 def build_gauge_cache(dense_k: torch.Tensor, dense_v: torch.Tensor, lengths: list[int],
                       exact_tail_pages: int = 16, exact_sink_pages: int = 0,
-                      prefix_tokens: list[int] | None = None) -> tuple[GaugeCache, DecodeTables]:
+                      prefix_tokens: list[int] | None = None,
+                      capacity_pages: int | None = None) -> tuple[GaugeCache, DecodeTables]:
     """Quantise a dense request-major cache [sum(pages), 16, Hkv, 128].
 
     Request r owns the ``ceil(lengths[r]/16)`` consecutive pages after those
     of requests < r.  The last ``exact_tail_pages`` logical pages (and the
     first ``exact_sink_pages``) are exact; the rest are read as INT8.
     Tokens past a request's length inside its last page are ignored by
-    attention (masked by last_page_len)."""
+    attention (masked by last_page_len).
+
+    With ``capacity_pages`` the INT8 cache gives every request the same
+    capacity (request r's logical page p at r*capacity_pages + p), the
+    request-major layout of request_major_page_table
+    (scripts/benchmark_page_gauge_transformer.py:383-407) that the append
+    kernels address; otherwise the requests' pages are packed."""
     device = dense_k.device
     hkv = dense_k.shape[2]
     batch = len(lengths)
@@ -89,12 +96,19 @@ def build_gauge_cache(dense_k: torch.Tensor, dense_v: torch.Tensor, lengths: lis
     starts = [sum(pages[:r]) for r in range(batch)]
     if dense_k.shape[0] < sum(pages):
         raise ValueError("dense cache is smaller than the requested lengths")
+    if capacity_pages is not None:
+        if capacity_pages < max(pages):
+            raise ValueError("capacity_pages is smaller than the longest request")
+        dst = [r * capacity_pages for r in range(batch)]
+        code_pages = batch * capacity_pages
+    else:
+        dst, code_pages = starts, dense_k.shape[0]
     prefix_tokens = prefix_tokens or lengths
     key_center = torch.empty(batch, hkv, DIM, device=device, dtype=torch.float16)
     value_center = torch.empty_like(key_center)
-    key_codes = torch.empty_like(dense_k, dtype=torch.int8)
-    value_codes = torch.empty_like(dense_v, dtype=torch.int8)
-    key_scales = torch.empty(dense_k.shape[0], hkv, device=device, dtype=torch.float16)
+    key_codes = torch.zeros(code_pages, PAGE, hkv, DIM, device=device, dtype=torch.int8)
+    value_codes = torch.zeros_like(key_codes)
+    key_scales = torch.zeros(code_pages, hkv, device=device, dtype=torch.float16)
     value_scales = torch.empty_like(key_scales)
     storage = exact_sink_pages + exact_tail_pages
     exact_key = torch.zeros(batch * storage, PAGE, hkv, DIM, device=device, dtype=torch.float16)
@@ -108,12 +122,13 @@ def build_gauge_cache(dense_k: torch.Tensor, dense_v: torch.Tensor, lengths: lis
         flat_v = dense_v[s:s + n].reshape(-1, hkv, DIM)[:prefix_tokens[r]]
         key_center[r] = flat_k.float().mean(dim=0).half()
         value_center[r] = flat_v.float().mean(dim=0).half()
+        d = dst[r]
         quantize_pages_into(dense_k[s:s + n], dense_v[s:s + n], key_center[r], value_center[r],
-                            key_codes[s:s + n], value_codes[s:s + n], key_scales[s:s + n],
-                            value_scales[s:s + n], 0, "half_away")
+                            key_codes[d:d + n], value_codes[d:d + n], key_scales[d:d + n],
+                            value_scales[d:d + n], 0, "half_away")
         n_old = max(n - exact_tail_pages - exact_sink_pages, 0)
         sink = min(exact_sink_pages, n)
-        old_idx.extend(range(s + sink, s + sink + n_old))
+        old_idx.extend(range(d + sink, d + sink + n_old))
         old_counts.append(n_old)
         ex_logical = list(range(sink)) + list(range(sink + n_old, n))
         ring = []

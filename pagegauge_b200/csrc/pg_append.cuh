@@ -31,6 +31,7 @@ struct AppendParams {
   const __half* cos;
   const __half* sin;
   const int32_t* device_position;  // null: use host_position
+  int64_t position_stride;          // 0: one position for the batch, 1: per request
   int64_t host_position;
   int64_t rope_row_stride;
   int64_t rope_rows;
@@ -115,7 +116,7 @@ __device__ __forceinline__ float cta64_max(float v, float* scratch) {
   return r;
 }
 
-__device__ __forceinline__ bool resolve_position(const AppendParams& p,
+__device__ __forceinline__ bool resolve_position(const AppendParams& p, int r,
                                                  int64_t capacity_tokens,
                                                  int64_t& pos,
                                                  const __half*& cosr,
@@ -126,7 +127,7 @@ __device__ __forceinline__ bool resolve_position(const AppendParams& p,
     sinr = p.sin;
     return pos >= 0 && pos < capacity_tokens;
   }
-  pos = __ldg(p.device_position);
+  pos = __ldg(p.device_position + r * p.position_stride);
   if (pos < 0 || pos >= capacity_tokens || pos >= p.rope_rows) return false;
   cosr = p.cos + pos * p.rope_row_stride;
   sinr = p.sin + pos * p.rope_row_stride;
@@ -152,7 +153,7 @@ __global__ void __launch_bounds__(64)
   const int j = threadIdx.x;
   int64_t pos;
   const __half *cosr, *sinr;
-  if (!resolve_position(p, p.exact_pages_per_request * kPage, pos, cosr, sinr)) {
+  if (!resolve_position(p, r, p.exact_pages_per_request * kPage, pos, cosr, sinr)) {
     if (j == 0 && p.device_position != nullptr)
       record_error(p.error_flag, kDevBadPosition);
     return;
@@ -178,7 +179,7 @@ __global__ void __launch_bounds__(64)
   const int j = threadIdx.x;
   int64_t pos;
   const __half *cosr, *sinr;
-  if (!resolve_position(p, p.code_pages_per_request * kPage, pos, cosr, sinr)) {
+  if (!resolve_position(p, r, p.code_pages_per_request * kPage, pos, cosr, sinr)) {
     if (j == 0 && p.device_position != nullptr)
       record_error(p.error_flag, kDevBadPosition);
     return;

@@ -204,18 +204,19 @@ int32_t pg_read_device_error(int32_t* code_out) {
 }
 
 // ------------------------------------------------------------------ append
-int32_t pg_rope_append_fp16(const void* query, const void* key,
-                            const void* value, const void* cosine,
-                            const void* sine, void* rotated_query,
-                            void* key_pages, void* value_pages,
-                            int64_t query_batch_stride,
-                            int64_t key_batch_stride,
-                            int64_t value_batch_stride, int32_t batch,
-                            int32_t query_heads, int32_t kv_heads,
-                            int64_t num_pages, int64_t position,
-                            const int32_t* device_position,
-                            int64_t rope_row_stride, int64_t rope_rows,
-                            void* stream) {
+static int32_t append_fp16_impl(const void* query, const void* key,
+                                const void* value, const void* cosine,
+                                const void* sine, void* rotated_query,
+                                void* key_pages, void* value_pages,
+                                int64_t query_batch_stride,
+                                int64_t key_batch_stride,
+                                int64_t value_batch_stride, int32_t batch,
+                                int32_t query_heads, int32_t kv_heads,
+                                int64_t num_pages, int64_t position,
+                                const int32_t* device_position,
+                                int64_t position_stride,
+                                int64_t rope_row_stride, int64_t rope_rows,
+                                void* stream) {
   PG_REQUIRE(batch > 0, "Q/K/V batch sizes must match and be positive");
   PG_REQUIRE(query_heads > 0 && kv_heads > 0, "head counts must be positive");
   if (device_position == nullptr) {
@@ -247,6 +248,7 @@ int32_t pg_rope_append_fp16(const void* query, const void* key,
   p.cos = static_cast<const __half*>(cosine);
   p.sin = static_cast<const __half*>(sine);
   p.device_position = device_position;
+  p.position_stride = position_stride;
   p.host_position = position;
   p.rope_row_stride = rope_row_stride;
   p.rope_rows = rope_rows;
@@ -263,7 +265,43 @@ int32_t pg_rope_append_fp16(const void* query, const void* key,
   return cuda_check(cudaGetLastError(), "rope_append_fp16 launch");
 }
 
-int32_t pg_rope_append_page_gauge(
+int32_t pg_rope_append_fp16(const void* query, const void* key,
+                            const void* value, const void* cosine,
+                            const void* sine, void* rotated_query,
+                            void* key_pages, void* value_pages,
+                            int64_t query_batch_stride,
+                            int64_t key_batch_stride,
+                            int64_t value_batch_stride, int32_t batch,
+                            int32_t query_heads, int32_t kv_heads,
+                            int64_t num_pages, int64_t position,
+                            const int32_t* device_position,
+                            int64_t rope_row_stride, int64_t rope_rows,
+                            void* stream) {
+  return append_fp16_impl(query, key, value, cosine, sine, rotated_query, key_pages,
+                          value_pages, query_batch_stride, key_batch_stride,
+                          value_batch_stride, batch, query_heads, kv_heads, num_pages,
+                          position, device_position, 0, rope_row_stride, rope_rows, stream);
+}
+
+int32_t pg_rope_append_fp16_batched(const void* query, const void* key,
+                                    const void* value, const void* cosine,
+                                    const void* sine, void* rotated_query,
+                                    void* key_pages, void* value_pages,
+                                    int64_t query_batch_stride,
+                                    int64_t key_batch_stride,
+                                    int64_t value_batch_stride, int32_t batch,
+                                    int32_t query_heads, int32_t kv_heads,
+                                    int64_t num_pages, const int32_t* positions,
+                                    int64_t rope_row_stride, int64_t rope_rows,
+                                    void* stream) {
+  PG_REQUIRE(positions != nullptr, "per-request positions must be a device int32 [B] tensor");
+  return append_fp16_impl(query, key, value, cosine, sine, rotated_query, key_pages,
+                          value_pages, query_batch_stride, key_batch_stride,
+                          value_batch_stride, batch, query_heads, kv_heads, num_pages, 0,
+                          positions, 1, rope_row_stride, rope_rows, stream);
+}
+
+static int32_t append_page_gauge_impl(
     const void* query, const void* key, const void* value,
     const void* cosine, const void* sine, const void* key_center,
     const void* value_center, void* rotated_query, void* exact_key_pages,
@@ -273,8 +311,8 @@ int32_t pg_rope_append_page_gauge(
     int64_t center_batch_stride, int32_t batch, int32_t query_heads,
     int32_t kv_heads, int64_t exact_pages, int64_t code_pages,
     int64_t exact_sink_pages, int64_t position,
-    const int32_t* device_position, int64_t rope_row_stride,
-    int64_t rope_rows, void* stream) {
+    const int32_t* device_position, int64_t position_stride,
+    int64_t rope_row_stride, int64_t rope_rows, void* stream) {
   PG_REQUIRE(batch > 0, "Q/K/V batch sizes must match and be positive");
   PG_REQUIRE(query_heads > 0 && kv_heads > 0, "head counts must be positive");
   if (device_position == nullptr) {
@@ -314,6 +352,7 @@ int32_t pg_rope_append_page_gauge(
   p.cos = static_cast<const __half*>(cosine);
   p.sin = static_cast<const __half*>(sine);
   p.device_position = device_position;
+  p.position_stride = position_stride;
   p.host_position = position;
   p.rope_row_stride = rope_row_stride;
   p.rope_rows = rope_rows;
@@ -337,6 +376,46 @@ int32_t pg_rope_append_page_gauge(
   pg::pg_rope_append_page_gauge_kernel<<<batch * kv_heads, 64, 0,
                                          static_cast<cudaStream_t>(stream)>>>(p);
   return cuda_check(cudaGetLastError(), "rope_append_page_gauge launch");
+}
+
+int32_t pg_rope_append_page_gauge(
+    const void* query, const void* key, const void* value,
+    const void* cosine, const void* sine, const void* key_center,
+    const void* value_center, void* rotated_query, void* exact_key_pages,
+    void* exact_value_pages, void* key_codes, void* value_codes,
+    void* key_scales, void* value_scales, int64_t query_batch_stride,
+    int64_t key_batch_stride, int64_t value_batch_stride,
+    int64_t center_batch_stride, int32_t batch, int32_t query_heads,
+    int32_t kv_heads, int64_t exact_pages, int64_t code_pages,
+    int64_t exact_sink_pages, int64_t position,
+    const int32_t* device_position, int64_t rope_row_stride,
+    int64_t rope_rows, void* stream) {
+  return append_page_gauge_impl(
+      query, key, value, cosine, sine, key_center, value_center, rotated_query,
+      exact_key_pages, exact_value_pages, key_codes, value_codes, key_scales, value_scales,
+      query_batch_stride, key_batch_stride, value_batch_stride, center_batch_stride, batch,
+      query_heads, kv_heads, exact_pages, code_pages, exact_sink_pages, position,
+      device_position, 0, rope_row_stride, rope_rows, stream);
+}
+
+int32_t pg_rope_append_page_gauge_batched(
+    const void* query, const void* key, const void* value,
+    const void* cosine, const void* sine, const void* key_center,
+    const void* value_center, void* rotated_query, void* exact_key_pages,
+    void* exact_value_pages, void* key_codes, void* value_codes,
+    void* key_scales, void* value_scales, int64_t query_batch_stride,
+    int64_t key_batch_stride, int64_t value_batch_stride,
+    int64_t center_batch_stride, int32_t batch, int32_t query_heads,
+    int32_t kv_heads, int64_t exact_pages, int64_t code_pages,
+    int64_t exact_sink_pages, const int32_t* positions,
+    int64_t rope_row_stride, int64_t rope_rows, void* stream) {
+  PG_REQUIRE(positions != nullptr, "per-request positions must be a device int32 [B] tensor");
+  return append_page_gauge_impl(
+      query, key, value, cosine, sine, key_center, value_center, rotated_query,
+      exact_key_pages, exact_value_pages, key_codes, value_codes, key_scales, value_scales,
+      query_batch_stride, key_batch_stride, value_batch_stride, center_batch_stride, batch,
+      query_heads, kv_heads, exact_pages, code_pages, exact_sink_pages, 0, positions, 1,
+      rope_row_stride, rope_rows, stream);
 }
 
 // -------------------------------------------------------------- tail merge

@@ -10,13 +10,15 @@ single-launch heterogeneous ABI (scripts/page_gauge_heterogeneous_fa2.py).
 
 from __future__ import annotations
 
+import ctypes
 import math
 
 import numpy as np
 import torch
 
-from .wrapper import (HEAD_DIM, PAGE, PagedDecodePlan, _segment, _Workspace, check_cache,
-                      host_indptr, launch_decode, num_sms, plan_items)
+from . import _lib
+from .wrapper import (HEAD_DIM, PAGE, PagedDecodePlan, _segment, _stream, _Workspace,
+                      check_cache, host_indptr, launch_decode, num_sms, plan_items)
 
 
 class PageGaugeDecode:
@@ -27,6 +29,12 @@ class PageGaugeDecode:
         self._warps = warps_per_cta
         self._plan: PagedDecodePlan | None = None
         self.sm_scale = 1.0 / math.sqrt(HEAD_DIM)
+        # Argument block of the last launch and the tensors it was built
+        # from: a run with identical tensors relaunches it without
+        # re-validating (the per-layer decode loop calls run() with the
+        # same buffers every step).
+        self._last_key = None
+        self._last_args = None
 
     def plan(self, old_indptr, old_indices, exact_indptr, exact_indices, exact_last_page_len,
              num_qo_heads: int = 32, num_kv_heads: int = 8, old_split_pages: int = 0,
@@ -45,6 +53,7 @@ class PageGaugeDecode:
                                       int(exact_split_pages), num_sms(dev), self._warps)
         self._plan = PagedDecodePlan(self._ws, items, off, info, batch, num_kv_heads,
                                      num_qo_heads // num_kv_heads)
+        self._last_key = self._last_args = None
         self._old_indices = old_indices
         self._exact_indices = exact_indices
         self._exact_last = exact_last_page_len
@@ -66,6 +75,17 @@ class PageGaugeDecode:
             out: torch.Tensor | None = None, lse: torch.Tensor | None = None,
             sm_scale: float | None = None, fused_merge: bool = False) -> torch.Tensor:
         plan = self.work_plan
+        key = None
+        if out is not None:
+            key = (q.data_ptr(), q.shape, q.stride(), key_codes.data_ptr(), key_codes.shape,
+                   value_codes.data_ptr(), key_scales.data_ptr(), value_scales.data_ptr(),
+                   exact_key.data_ptr(), exact_key.shape, exact_value.data_ptr(),
+                   None if value_center is None else (value_center.data_ptr(), value_center.shape),
+                   out.data_ptr(), out.shape, out.stride(), None if lse is None else lse.data_ptr(),
+                   sm_scale, fused_merge, q.dtype, out.dtype)
+            if key == self._last_key:
+                _lib.check(_lib.load().pg_decode_run(self._last_args_ref, _stream(q)))
+                return out
         segs = [None, None]
         if self._old_indices is not None:
             check_cache(key_codes, "key_codes", torch.int8, self._num_kv_heads)
@@ -81,8 +101,11 @@ class PageGaugeDecode:
         if value_center is not None and (value_center.dtype != torch.float16
                                          or not value_center.is_contiguous()):
             raise ValueError("value_center must be contiguous float16")
-        launch_decode(plan, q, segs, self.sm_scale if sm_scale is None else sm_scale, out, lse,
-                      value_center=value_center, fused_merge=fused_merge)
+        args = launch_decode(plan, q, segs, self.sm_scale if sm_scale is None else sm_scale, out,
+                             lse, value_center=value_center, fused_merge=fused_merge)
+        if key is not None:
+            self._last_key, self._last_args = key, args
+            self._last_args_ref = ctypes.byref(args)
         return out
 
 

@@ -82,6 +82,19 @@ def _check_dynamic(query, cosine, sine, position) -> None:
              "dynamic position, RoPE tables, and Q/K/V must share one device")
 
 
+def _check_positions(query, cosine, sine, positions) -> None:
+    """Per-request positions: device int32 [B] plus [positions,128] tables."""
+    check_tensor(cosine, "cosine", torch.float16, 2)
+    check_tensor(sine, "sine", torch.float16, 2)
+    check_tensor(positions, "positions", torch.int32, 1)
+    _require(cosine.shape == sine.shape and cosine.size(0) > 0 and cosine.size(1) == HEAD_DIM,
+             "dynamic RoPE tables must be matching [positions,128] tensors")
+    _require(positions.numel() == query.size(0), "positions must hold one int32 per request")
+    _require(cosine.device == query.device and sine.device == query.device
+             and positions.device == query.device,
+             "dynamic position, RoPE tables, and Q/K/V must share one device")
+
+
 def _check_pages(pages_k, pages_v, key, name_k, name_v, message) -> None:
     check_tensor(pages_k, name_k, torch.float16, 4)
     check_tensor(pages_v, name_v, torch.float16, 4)
@@ -198,6 +211,44 @@ class AppendExtension:
                          rotated_query, exact_key_pages, exact_value_pages, key_codes,
                          value_codes, key_scales, value_scales, cstride, exact_sink_pages, 0,
                          position.data_ptr(), cosine.stride(0), cosine.size(0))
+
+    def rope_append_fp16_batched(self, query, key, value, cosine, sine, positions,
+                                 rotated_query, key_pages, value_pages) -> None:
+        """rope_append_fp16_dynamic with one position per request
+        (``positions`` int32 [B] on the device)."""
+        _check_qkv(query, key, value, rotated_query)
+        _check_pages(key_pages, value_pages, key, "key_pages", "value_pages",
+                     "page cache must be NHD [pages,16,Hkv,128]")
+        _check_positions(query, cosine, sine, positions)
+        _lib.call(
+            "pg_rope_append_fp16_batched", query.data_ptr(), key.data_ptr(), value.data_ptr(),
+            cosine.data_ptr(), sine.data_ptr(), rotated_query.data_ptr(), key_pages.data_ptr(),
+            value_pages.data_ptr(), query.stride(0), key.stride(0), value.stride(0),
+            query.size(0), query.size(1), key.size(1), key_pages.size(0),
+            positions.data_ptr(), cosine.stride(0), cosine.size(0), _stream(query))
+
+    def rope_append_page_gauge_batched(self, query, key, value, cosine, sine, positions,
+                                       key_center, value_center, rotated_query, exact_key_pages,
+                                       exact_value_pages, key_codes, value_codes, key_scales,
+                                       value_scales, exact_sink_pages: int) -> None:
+        """rope_append_page_gauge_dynamic with one position per request
+        (``positions`` int32 [B] on the device): request r appends at
+        positions[r] and closes its page when positions[r] % 16 == 15."""
+        _check_qkv(query, key, value, rotated_query)
+        _check_pages(exact_key_pages, exact_value_pages, key, "exact_key_pages",
+                     "exact_value_pages", "exact page cache must be NHD [pages,16,Hkv,128]")
+        _check_positions(query, cosine, sine, positions)
+        cstride = _check_gauge_storage(query, key, key_center, value_center, key_codes,
+                                       value_codes, key_scales, value_scales)
+        _lib.call(
+            "pg_rope_append_page_gauge_batched", query.data_ptr(), key.data_ptr(),
+            value.data_ptr(), cosine.data_ptr(), sine.data_ptr(), key_center.data_ptr(),
+            value_center.data_ptr(), rotated_query.data_ptr(), exact_key_pages.data_ptr(),
+            exact_value_pages.data_ptr(), key_codes.data_ptr(), value_codes.data_ptr(),
+            key_scales.data_ptr(), value_scales.data_ptr(), query.stride(0), key.stride(0),
+            value.stride(0), cstride, query.size(0), query.size(1), key.size(1),
+            exact_key_pages.size(0), key_codes.size(0), int(exact_sink_pages),
+            positions.data_ptr(), cosine.stride(0), cosine.size(0), _stream(query))
 
     def _gauge_call(self, query, key, value, cosine, sine, key_center, value_center,
                     rotated_query, exact_k, exact_v, codes_k, codes_v, scales_k, scales_v,

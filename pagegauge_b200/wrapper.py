@@ -142,8 +142,9 @@ def check_cache(cache: torch.Tensor, name: str, dtype: torch.dtype, kv_heads: in
 def launch_decode(plan: PagedDecodePlan, q: torch.Tensor, segments, sm_scale: float,
                   out: torch.Tensor, lse: torch.Tensor | None, extra=None,
                   value_center: torch.Tensor | None = None, final_ok: bool = True,
-                  fused_merge: bool = False) -> None:
-    """Fill the C argument block and launch split decode (+ merge)."""
+                  fused_merge: bool = False) -> "_lib.PgDecodeArgs":
+    """Fill the C argument block and launch split decode (+ merge); returns
+    the argument block so a caller may relaunch it unchanged."""
     if q.dtype != torch.float16 or q.dim() != 3 or q.stride(2) != 1:
         raise ValueError("q must be float16 [B,Hq,128] with a contiguous last dimension")
     a = _lib.PgDecodeArgs()
@@ -174,6 +175,7 @@ def launch_decode(plan: PagedDecodePlan, q: torch.Tensor, segments, sm_scale: fl
         a.value_center = value_center.data_ptr()
         a.vc_stride_b = 0 if value_center.dim() == 2 else value_center.stride(0)
     _lib.check(_lib.load().pg_decode_run(ctypes.byref(a), _stream(q)))
+    return a
 
 
 class BatchDecodeWithPagedKVCacheWrapper:

@@ -14,9 +14,11 @@ ATOL = 2e-3        # max-abs 2e-3 in FP16 ...
 MIN_COSINE = 0.9999  # ... and cosine >= 0.9999
 
 
-def make_case(lengths, hkv=8, group=4, tail_pages=16, sink_pages=0, seed=20261001):
+def make_case(lengths, hkv=8, group=4, tail_pages=16, sink_pages=0, seed=20261001,
+              capacity_pages=None):
     q, dk, dv = synthetic_dense_cache(lengths, hkv=hkv, seed=seed, group=group)
-    cache, tables = build_gauge_cache(dk.cuda(), dv.cuda(), lengths, tail_pages, sink_pages)
+    cache, tables = build_gauge_cache(dk.cuda(), dv.cuda(), lengths, tail_pages, sink_pages,
+                                      capacity_pages=capacity_pages)
     return q.cuda(), dk, dv, cache, tables
 
 

@@ -110,6 +110,86 @@ def test_append_page_gauge_bit_exact_vs_oracle(cuda_lib, batch, logical_pages, p
     assert rel < 0.02
 
 
+@pytest.mark.parametrize("shared_center", [False, True])
+def test_batched_positions_bit_exact_vs_oracle(cuda_lib, shared_center):
+    """Per-request positions (ragged serving batch): requests start at
+    staggered in-page phases, so every step closes pages for some requests
+    only (configs[3]'s mixed close pattern)."""
+    batch = 1 if shared_center else 8
+    exact_ppr, code_ppr, steps = 3, 8, 40
+    g = torch.Generator().manual_seed(20261011 + batch)
+    cos, sin = rope_tables(code_ppr * 16)
+    q = torch.randn(steps, batch, 32, 128, generator=g).half()
+    keys = (torch.randn(steps, batch, 8, 128, generator=g) * 2.0).half()
+    values = torch.randn(steps, batch, 8, 128, generator=g).half()
+    cshape = (8, 128) if shared_center else (batch, 8, 128)
+    kc = (torch.randn(*cshape, generator=g) * 0.5).half()
+    vc = (torch.randn(*cshape, generator=g) * 0.1).half()
+    start = np.array([(r * 16) // batch + 7 * r for r in range(batch)], np.int32)
+    ext = load_append_extension()
+    buf = _gauge_buffers(batch, exact_ppr, code_ppr)
+    f16k = torch.zeros(batch * code_ppr, 16, 8, 128, dtype=torch.float16, device="cuda")
+    f16v = torch.zeros_like(f16k)
+    st = _oracle_state(batch, exact_ppr, code_ppr)
+    ok = np.zeros((batch * code_ppr, 16, 8, 128), np.float16)
+    ov = np.zeros_like(ok)
+    dcos, dsin, dkc, dvc = cos.cuda(), sin.cuda(), kc.cuda(), vc.cuda()
+    rq = torch.empty(batch, 32, 128, dtype=torch.float16, device="cuda")
+    rq16 = torch.empty_like(rq)
+    pos_dev = torch.empty(batch, dtype=torch.int32, device="cuda")
+    closes = 0
+    for step in range(steps):
+        pos = start + step
+        closes += int((pos % 16 == 15).sum())
+        pos_dev.copy_(torch.from_numpy(pos))
+        dq, dk, dv = q[step].cuda(), keys[step].cuda(), values[step].cuda()
+        ext.rope_append_page_gauge_batched(dq, dk, dv, dcos, dsin, pos_dev, dkc, dvc, rq,
+                                           buf["exact_k"], buf["exact_v"], buf["codes_k"],
+                                           buf["codes_v"], buf["scales_k"], buf["scales_v"], 0)
+        ext.rope_append_fp16_batched(dq, dk, dv, dcos, dsin, pos_dev, rq16, f16k, f16v)
+        orq = O.rope_append_page_gauge_batched(st, q[step].numpy(), keys[step].numpy(),
+                                               values[step].numpy(), cos.numpy(), sin.numpy(),
+                                               kc.numpy(), vc.numpy(), 0, pos)
+        orq16 = O.rope_append_fp16_batched(ok, ov, q[step].numpy(), keys[step].numpy(),
+                                           values[step].numpy(), cos.numpy(), sin.numpy(), pos)
+        torch.cuda.synchronize()
+        assert np.array_equal(u16(cpu(rq)), u16(orq))
+        assert np.array_equal(u16(cpu(rq16)), u16(orq16))
+    assert closes >= 2 * batch
+    assert read_device_error() == 0
+    _assert_state_equal(buf, st)
+    assert np.array_equal(u16(cpu(f16k)), u16(ok))
+    assert np.array_equal(u16(cpu(f16v)), u16(ov))
+
+
+def test_batched_position_out_of_range_skips_only_that_request(cuda_lib):
+    ext = load_append_extension()
+    batch, exact_ppr, code_ppr = 4, 2, 4
+    cos, sin = rope_tables(code_ppr * 16)
+    g = torch.Generator().manual_seed(7)
+    q = torch.randn(batch, 32, 128, generator=g).half().cuda()
+    k = torch.randn(batch, 8, 128, generator=g).half().cuda()
+    v = torch.randn(batch, 8, 128, generator=g).half().cuda()
+    kc = torch.zeros(batch, 8, 128, dtype=torch.float16, device="cuda")
+    buf = _gauge_buffers(batch, exact_ppr, code_ppr)
+    rq = torch.zeros_like(q)
+    pos = torch.tensor([3, code_ppr * 16, 5, -1], dtype=torch.int32, device="cuda")
+    read_device_error()
+    ext.rope_append_page_gauge_batched(q, k, v, cos.cuda(), sin.cuda(), pos, kc, kc, rq,
+                                       buf["exact_k"], buf["exact_v"], buf["codes_k"],
+                                       buf["codes_v"], buf["scales_k"], buf["scales_v"], 0)
+    torch.cuda.synchronize()
+    assert read_device_error() == 2  # kDevBadPosition
+    ring = buf["exact_k"].view(batch, exact_ppr, 16, 8, 128)
+    assert ring[0, 0, 3].abs().sum() > 0 and ring[2, 0, 5].abs().sum() > 0
+    assert ring[1].abs().sum() == 0 and ring[3].abs().sum() == 0
+    assert rq[1].abs().sum() == 0 and rq[3].abs().sum() == 0
+    with pytest.raises(RuntimeError, match="one int32 per request"):
+        ext.rope_append_page_gauge_batched(q, k, v, cos.cuda(), sin.cuda(), pos[:2], kc, kc, rq,
+                                           buf["exact_k"], buf["exact_v"], buf["codes_k"],
+                                           buf["codes_v"], buf["scales_k"], buf["scales_v"], 0)
+
+
 def test_rope_matches_golden_torch_expression(cuda_lib):
     """RoPE of the append kernel equals the reference's torch FP16 pin."""
     g = np.load(GOLDEN / "rope.npz")

@@ -57,10 +57,13 @@ def test_b1_4k_configs0_all_splits(cuda_lib, split):
 
 
 @pytest.mark.parametrize("lengths", [[1000, 333, 2050], [17, 256, 257, 4095], [5000], [1]])
-def test_ragged_partial_pages(cuda_lib, lengths):
+@pytest.mark.parametrize("uniform_capacity", [False, True])
+def test_ragged_partial_pages(cuda_lib, lengths, uniform_capacity):
     """Ragged requests with partial last pages, tail-only requests (<=256
-    tokens: no INT8 pages) and a single-token request."""
-    q, dk, dv, cache, tables = make_case(lengths, seed=7)
+    tokens: no INT8 pages) and a single-token request; INT8 pages packed or
+    at a uniform per-request capacity (the append kernels' layout)."""
+    cap = max(-(-n // 16) for n in lengths) + 3 if uniform_capacity else None
+    q, dk, dv, cache, tables = make_case(lengths, seed=7, capacity_pages=cap)
     out, lse, _ = run_fused(q, cache, tables, split_old=5, split_exact=3)
     for r in range(len(lengths)):
         exp, exp_lse = oracle_decode(q, cache, tables, lengths, r)
@@ -279,3 +282,31 @@ def test_fused_last_cta_merge_matches_merge_kernel(cuda_lib, fused):
             exp, exp_lse = oracle_decode(q, cache, tables, lengths, r)
             assert_close_decode(out[r], exp)
             np.testing.assert_allclose(cpu(lse[r]), exp_lse, atol=LSE_ATOL, rtol=0)
+
+
+def test_repeated_run_relaunches_with_new_contents(cuda_lib):
+    """A second run() with the same tensors relaunches the cached argument
+    block; it must read the tensors' current contents (new q, new cache
+    values), and a run with a different output tensor rebuilds it."""
+    lengths = [3000, 700]
+    q, dk, dv, cache, tables = make_case(lengths, seed=21)
+    dec = PageGaugeDecode(workspace())
+    dec.plan(tables.old_indptr, tables.old_indices, tables.exact_indptr, tables.exact_indices,
+             tables.exact_last_page_len, 32, 8, old_split_pages=13)
+    out = torch.empty_like(q)
+    args = (cache.key_codes, cache.value_codes, cache.key_scales, cache.value_scales,
+            cache.exact_key, cache.exact_value, cache.value_center)
+    for trial in range(3):
+        if trial:
+            q.copy_(torch.randn(q.shape, generator=torch.Generator().manual_seed(trial)).half())
+            cache.exact_value.mul_(0.5)
+        dec.run(q, *args, out=out)
+        torch.cuda.synchronize()
+        for r in range(len(lengths)):
+            exp, _ = oracle_decode(q, cache, tables, lengths, r)
+            assert_close_decode(out[r], exp)
+    other = torch.empty_like(q)
+    dec.run(q, *args, out=other)
+    torch.cuda.synchronize()
+    assert torch.equal(other, out)
+    assert read_device_error() == 0
