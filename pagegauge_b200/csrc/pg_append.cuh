@@ -146,110 +146,228 @@ __device__ __forceinline__ void rotate_queries(const AppendParams& p, int r,
   }
 }
 
-__global__ void __launch_bounds__(64)
+constexpr int kAppendThreads = 256;
+
+// Loads of one append CTA that do not depend on the position: the token's
+// k/v dimension pair (2j, 2j+1) of this KV head and the rotate-half
+// partners, issued before the position/RoPE row round trip.
+struct AppendInputs {
+  uint32_t x, partner;  // k (role 0) or v (role 1) pair, and the k partner
+  uint32_t q, qpartner;  // one query head's pair (qh < 0: none)
+  int qh;
+};
+
+__device__ __forceinline__ uint32_t rope_apply(uint32_t x, uint32_t partner, int j,
+                                               uint32_t c, uint32_t s) {
+  if (j < 32) partner ^= 0x80008000u;  // -x[d + 64] for d < 64
+  return hadd2_rn(hmul2_rn(x, c), hmul2_rn(partner, s));
+}
+
+// Thread t = (g, j), g = t / 64: query head h + g*Hkv (+ 4*Hkv ...) and, for
+// g = 0 / 1, the key / value pair j of KV head h.
+__device__ __forceinline__ AppendInputs load_append_inputs(const AppendParams& p, int r,
+                                                           int h, int g, int j) {
+  AppendInputs in{};
+  in.qh = h + g * p.hkv;
+  if (in.qh < p.hq) {
+    const uint32_t* q32 = reinterpret_cast<const uint32_t*>(
+        p.q + r * p.q_stride_b + static_cast<int64_t>(in.qh) * kHeadDim);
+    in.q = q32[j];
+    in.qpartner = q32[(j + 32) & 63];
+  } else {
+    in.qh = -1;
+  }
+  if (g == 0) {
+    const uint32_t* k32 = reinterpret_cast<const uint32_t*>(
+        p.k + r * p.k_stride_b + static_cast<int64_t>(h) * kHeadDim);
+    in.x = k32[j];
+    in.partner = k32[(j + 32) & 63];
+  } else if (g == 1) {
+    in.x = reinterpret_cast<const uint32_t*>(
+        p.v + r * p.v_stride_b + static_cast<int64_t>(h) * kHeadDim)[j];
+  }
+  return in;
+}
+
+__device__ __forceinline__ void rotate_query_heads(const AppendParams& p, int r, int h, int g,
+                                                   int j, const AppendInputs& in, uint32_t c,
+                                                   uint32_t s) {
+  if (in.qh < 0) return;
+  __half* out = p.rotated_q + (static_cast<int64_t>(r) * p.hq) * kHeadDim;
+  reinterpret_cast<uint32_t*>(out + static_cast<int64_t>(in.qh) * kHeadDim)[j] =
+      rope_apply(in.q, in.qpartner, j, c, s);
+  // Groups larger than 4 query heads per KV head: the remaining heads.
+  for (int qh = in.qh + 4 * p.hkv; qh < p.hq; qh += 4 * p.hkv) {
+    const __half* src = p.q + r * p.q_stride_b + static_cast<int64_t>(qh) * kHeadDim;
+    reinterpret_cast<uint32_t*>(out + static_cast<int64_t>(qh) * kHeadDim)[j] =
+        rope_pair(src, j, c, s);
+  }
+}
+
+__global__ void __launch_bounds__(kAppendThreads)
     pg_rope_append_fp16_kernel(const __grid_constant__ AppendParams p) {
   const int r = blockIdx.x / p.hkv;
   const int h = blockIdx.x % p.hkv;
-  const int j = threadIdx.x;
+  const int g = threadIdx.x >> 6, j = threadIdx.x & 63;
+  const AppendInputs in = load_append_inputs(p, r, h, g, j);
   int64_t pos;
   const __half *cosr, *sinr;
   if (!resolve_position(p, r, p.exact_pages_per_request * kPage, pos, cosr, sinr)) {
-    if (j == 0 && p.device_position != nullptr)
+    if (threadIdx.x == 0 && p.device_position != nullptr)
       record_error(p.error_flag, kDevBadPosition);
     return;
   }
   const uint32_t c = reinterpret_cast<const uint32_t*>(cosr)[j];
   const uint32_t s = reinterpret_cast<const uint32_t*>(sinr)[j];
-  rotate_queries(p, r, h, j, c, s);
+  rotate_query_heads(p, r, h, g, j, in, c, s);
+  if (g > 1) return;
   const int64_t page = pos / kPage, token = pos % kPage;
   const int64_t phys = r * p.exact_pages_per_request + page;
   const int64_t dst = ((phys * kPage + token) * p.hkv + h) * kHeadDim;
-  const __half* kin = p.k + r * p.k_stride_b + static_cast<int64_t>(h) * kHeadDim;
-  const __half* vin = p.v + r * p.v_stride_b + static_cast<int64_t>(h) * kHeadDim;
-  reinterpret_cast<uint32_t*>(p.key_pages + dst)[j] = rope_pair(kin, j, c, s);
-  reinterpret_cast<uint32_t*>(p.value_pages + dst)[j] =
-      reinterpret_cast<const uint32_t*>(vin)[j];
+  if (g == 0)
+    reinterpret_cast<uint32_t*>(p.key_pages + dst)[j] = rope_apply(in.x, in.partner, j, c, s);
+  else
+    reinterpret_cast<uint32_t*>(p.value_pages + dst)[j] = in.x;
 }
 
-__global__ void __launch_bounds__(64)
+// Reduce a max across the 256-thread CTA (8 warps).
+__device__ __forceinline__ float cta256_max(float v, float* scratch) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  if ((threadIdx.x & 31) == 0) scratch[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float m = scratch[0];
+#pragma unroll
+  for (int w = 1; w < kAppendThreads / 32; ++w) m = fmaxf(m, scratch[w]);
+  return m;
+}
+
+__device__ __forceinline__ float absmax_half8(const uint4& v) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  float m = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) m = fmaxf(m, absmax2(w[i]));
+  return m;
+}
+
+// clamp(round_half_away(x / scale)) with the quotient rounded to FP32 as
+// an IEEE division would, computed as x * rcp (rcp = 1/scale rounded).
+// |x*rcp - x/scale| and |RN(x/scale) - x/scale| are both below 2^-15 for
+// |x/scale| <= 128, and the code only changes where the quotient crosses a
+// point k + 0.5 (to within one FP32 ulp of |q| + 0.5, <= 2^-16).  So when
+// x*rcp lies more than 2^-12 from every k + 0.5 the two quotients give the
+// same code; otherwise the exact division decides.
+__device__ __forceinline__ int quantize_rcp(float x, float scale, float rcp) {
+  const float q = x * rcp;
+  const float a = fabsf(q);
+  const float f = a - floorf(a);
+  if (fabsf(f - 0.5f) <= 0x1p-12f) return quantize_one(x, scale, 0);
+  int z = static_cast<int>(floorf(__fadd_rn(a, 0.5f)));
+  z = z > 127 ? 127 : z;
+  return q < 0.f ? -z : z;
+}
+
+// Eight FP16 values -> eight INT8 codes (half away from zero), packed.
+__device__ __forceinline__ uint2 quantize_half8(const uint4& v, float scale, float rcp) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  uint32_t out[2] = {0u, 0u};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __half2 hv = *reinterpret_cast<const __half2*>(&w[i]);
+    const uint32_t lo = static_cast<uint8_t>(quantize_rcp(__low2float(hv), scale, rcp));
+    const uint32_t hi = static_cast<uint8_t>(quantize_rcp(__high2float(hv), scale, rcp));
+    out[i >> 1] |= (lo | (hi << 8)) << (16 * (i & 1));
+  }
+  return make_uint2(out[0], out[1]);
+}
+
+// One CTA of 256 threads per (request, KV head).  Append: thread (g, j)
+// rotates query head h + g*Hkv's pair j; g = 0 rotates and centres the key
+// pair, g = 1 centres the value pair, both into the ring slot.  Page close
+// (token 15): thread t owns 8 consecutive dims (16 B) of token t/16 of the
+// page for K and V; the 15 older tokens are read from the ring as soon as
+// the position is known (in parallel with the RoPE work), the new token
+// comes through shared memory; the CTA reduces the two abs-maxima, and each
+// thread quantises and writes its 8 + 8 codes (8-byte stores).
+__global__ void __launch_bounds__(kAppendThreads)
     pg_rope_append_page_gauge_kernel(const __grid_constant__ AppendParams p) {
-  __shared__ float red[2];
+  __shared__ float red[2][kAppendThreads / 32];
+  __shared__ __align__(16) uint32_t newest[2][kHeadDim / 2];
   const int r = blockIdx.x / p.hkv;
   const int h = blockIdx.x % p.hkv;
-  const int j = threadIdx.x;
+  const int g = threadIdx.x >> 6, j = threadIdx.x & 63;
+  const AppendInputs in = load_append_inputs(p, r, h, g, j);
+  uint32_t center = 0u;
+  if (g < 2) {
+    const int64_t cofs = r * p.center_stride_b + static_cast<int64_t>(h) * kHeadDim;
+    center = reinterpret_cast<const uint32_t*>((g == 0 ? p.key_center : p.value_center) + cofs)[j];
+  }
   int64_t pos;
   const __half *cosr, *sinr;
   if (!resolve_position(p, r, p.code_pages_per_request * kPage, pos, cosr, sinr)) {
-    if (j == 0 && p.device_position != nullptr)
+    if (threadIdx.x == 0 && p.device_position != nullptr)
       record_error(p.error_flag, kDevBadPosition);
     return;
   }
   const uint32_t c = reinterpret_cast<const uint32_t*>(cosr)[j];
   const uint32_t s = reinterpret_cast<const uint32_t*>(sinr)[j];
-  rotate_queries(p, r, h, j, c, s);
+  rotate_query_heads(p, r, h, g, j, in, c, s);
 
-  const int64_t page = pos / kPage;
+  const int page = static_cast<int>(pos / kPage);
   const int token = static_cast<int>(pos % kPage);
-  const int64_t tail_pages = p.exact_pages_per_request - p.exact_sink_pages;
-  const int64_t local =
-      page < p.exact_sink_pages ? page : p.exact_sink_pages + page % tail_pages;
+  const int sink = static_cast<int>(p.exact_sink_pages);
+  const int tail_pages = static_cast<int>(p.exact_pages_per_request) - sink;
+  const int local = page < sink ? page : sink + page % tail_pages;
   const int64_t ring_page = r * p.exact_pages_per_request + local;
-  const int64_t code_page = r * p.code_pages_per_request + page;
-
-  const __half* kin = p.k + r * p.k_stride_b + static_cast<int64_t>(h) * kHeadDim;
-  const __half* vin = p.v + r * p.v_stride_b + static_cast<int64_t>(h) * kHeadDim;
-  const int64_t cofs = r * p.center_stride_b + static_cast<int64_t>(h) * kHeadDim;
-  const uint32_t kc = reinterpret_cast<const uint32_t*>(p.key_center + cofs)[j];
-  const uint32_t vc = reinterpret_cast<const uint32_t*>(p.value_center + cofs)[j];
-  const uint32_t ck = center_pair(rope_pair(kin, j, c, s), kc);
-  const uint32_t cv = center_pair(reinterpret_cast<const uint32_t*>(vin)[j], vc);
-
   const int64_t row_stride = static_cast<int64_t>(p.hkv) * kHeadDim;  // per token
   __half* kring = p.key_pages + (ring_page * kPage * p.hkv + h) * kHeadDim;
   __half* vring = p.value_pages + (ring_page * kPage * p.hkv + h) * kHeadDim;
-  reinterpret_cast<uint32_t*>(kring + token * row_stride)[j] = ck;
-  reinterpret_cast<uint32_t*>(vring + token * row_stride)[j] = cv;
-
   // The 16th token closes the page: its INT8 copy is produced now, so it is
   // ready when the page later leaves the exact window.
-  if (token != kPage - 1) return;
-  uint32_t kv[kPage], vv[kPage];
-#pragma unroll
-  for (int tk = 0; tk < kPage - 1; ++tk) {
-    kv[tk] = reinterpret_cast<const uint32_t*>(kring + tk * row_stride)[j];
-    vv[tk] = reinterpret_cast<const uint32_t*>(vring + tk * row_stride)[j];
+  const bool close = token == kPage - 1;  // uniform over the CTA
+  const int tk = threadIdx.x >> 4, col = (threadIdx.x & 15) * 8;
+  uint4 kx = make_uint4(0u, 0u, 0u, 0u), vx = kx;
+  if (close && tk < kPage - 1) {
+    kx = *reinterpret_cast<const uint4*>(kring + tk * row_stride + col);
+    vx = *reinterpret_cast<const uint4*>(vring + tk * row_stride + col);
   }
-  kv[kPage - 1] = ck;
-  vv[kPage - 1] = cv;
-  float km = 0.f, vm = 0.f;
-#pragma unroll
-  for (int tk = 0; tk < kPage; ++tk) {
-    km = fmaxf(km, absmax2(kv[tk]));
-    vm = fmaxf(vm, absmax2(vv[tk]));
+  if (g < 2) {
+    const uint32_t val = g == 0 ? center_pair(rope_apply(in.x, in.partner, j, c, s), center)
+                                : center_pair(in.x, center);
+    reinterpret_cast<uint32_t*>((g == 0 ? kring : vring) + token * row_stride)[j] = val;
+    if (close) newest[g][j] = val;
   }
-  km = cta64_max(km, red);
-  vm = cta64_max(vm, red);
+  if (!close) return;
+  __syncthreads();
+  if (tk == kPage - 1) {
+    kx = *reinterpret_cast<const uint4*>(&newest[0][col / 2]);
+    vx = *reinterpret_cast<const uint4*>(&newest[1][col / 2]);
+  }
+  float km = absmax_half8(kx), vm = absmax_half8(vx);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    km = fmaxf(km, __shfl_xor_sync(0xffffffffu, km, o));
+    vm = fmaxf(vm, __shfl_xor_sync(0xffffffffu, vm, o));
+  }
+  if ((threadIdx.x & 31) == 0) {
+    red[0][threadIdx.x >> 5] = km;
+    red[1][threadIdx.x >> 5] = vm;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int w = 0; w < kAppendThreads / 32; ++w) {
+    km = fmaxf(km, red[0][w]);
+    vm = fmaxf(vm, red[1][w]);
+  }
   const __half ks_h = __float2half_rn(fmaxf(__fdiv_rn(km, 127.f), 0x1p-20f));
   const __half vs_h = __float2half_rn(fmaxf(__fdiv_rn(vm, 127.f), 0x1p-20f));
-  if (j == 0) {
-    p.key_scales[code_page * p.hkv + h] = ks_h;
-    p.value_scales[code_page * p.hkv + h] = vs_h;
-  }
+  const int64_t code_page = r * p.code_pages_per_request + page;
+  if (threadIdx.x == 0) p.key_scales[code_page * p.hkv + h] = ks_h;
+  if (threadIdx.x == 1) p.value_scales[code_page * p.hkv + h] = vs_h;
+  const int64_t cbase = (code_page * kPage * p.hkv + h) * kHeadDim + tk * row_stride + col;
   const float ksf = __half2float(ks_h), vsf = __half2float(vs_h);
-  int8_t* kcode = p.key_codes + (code_page * kPage * p.hkv + h) * kHeadDim;
-  int8_t* vcode = p.value_codes + (code_page * kPage * p.hkv + h) * kHeadDim;
-#pragma unroll
-  for (int tk = 0; tk < kPage; ++tk) {
-    const __half2 kh = *reinterpret_cast<const __half2*>(&kv[tk]);
-    const __half2 vh = *reinterpret_cast<const __half2*>(&vv[tk]);
-    char2 kz, vz;
-    kz.x = quantize_one(__low2float(kh), ksf, 0);
-    kz.y = quantize_one(__high2float(kh), ksf, 0);
-    vz.x = quantize_one(__low2float(vh), vsf, 0);
-    vz.y = quantize_one(__high2float(vh), vsf, 0);
-    reinterpret_cast<char2*>(kcode + tk * row_stride)[j] = kz;
-    reinterpret_cast<char2*>(vcode + tk * row_stride)[j] = vz;
-  }
+  *reinterpret_cast<uint2*>(p.key_codes + cbase) = quantize_half8(kx, ksf, __frcp_rn(ksf));
+  *reinterpret_cast<uint2*>(p.value_codes + cbase) = quantize_half8(vx, vsf, __frcp_rn(vsf));
 }
 
 // ------------------------------------------------ bulk page quantisation

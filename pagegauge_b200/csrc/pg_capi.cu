@@ -260,7 +260,7 @@ static int32_t append_fp16_impl(const void* query, const void* key,
   p.hkv = kv_heads;
   p.exact_pages_per_request = ppr;
   p.error_flag = device_error_ptr();
-  pg::pg_rope_append_fp16_kernel<<<batch * kv_heads, 64, 0,
+  pg::pg_rope_append_fp16_kernel<<<batch * kv_heads, pg::kAppendThreads, 0,
                                    static_cast<cudaStream_t>(stream)>>>(p);
   return cuda_check(cudaGetLastError(), "rope_append_fp16 launch");
 }
@@ -338,6 +338,11 @@ static int32_t append_page_gauge_impl(
                  aligned(exact_value_pages, 4) && aligned(key_codes, 2) &&
                  aligned(value_codes, 2) && aligned(rotated_query, 4),
              "tensors must be 4-byte aligned");
+  // The page close reads the ring page in 16-byte rows and writes codes in
+  // 8-byte rows.
+  PG_REQUIRE(aligned(exact_key_pages, 16) && aligned(exact_value_pages, 16) &&
+                 aligned(key_codes, 8) && aligned(value_codes, 8),
+             "exact pages must be 16-byte and INT8 codes 8-byte aligned");
   PG_REQUIRE(query_batch_stride % 2 == 0 && key_batch_stride % 2 == 0 &&
                  value_batch_stride % 2 == 0 && rope_row_stride % 2 == 0 &&
                  center_batch_stride % 2 == 0,
@@ -373,7 +378,7 @@ static int32_t append_page_gauge_impl(
   p.exact_sink_pages = exact_sink_pages;
   p.code_pages_per_request = code_ppr;
   p.error_flag = device_error_ptr();
-  pg::pg_rope_append_page_gauge_kernel<<<batch * kv_heads, 64, 0,
+  pg::pg_rope_append_page_gauge_kernel<<<batch * kv_heads, pg::kAppendThreads, 0,
                                          static_cast<cudaStream_t>(stream)>>>(p);
   return cuda_check(cudaGetLastError(), "rope_append_page_gauge launch");
 }

@@ -190,6 +190,40 @@ def test_batched_position_out_of_range_skips_only_that_request(cuda_lib):
                                            buf["codes_v"], buf["scales_k"], buf["scales_v"], 0)
 
 
+def test_page_close_exact_ties_bit_exact(cuda_lib):
+    """Centred values on exact code ties (x / scale = k + 0.5): page abs-max
+    127/16 gives scale 1/16 exactly and values are multiples of 1/32, so
+    half of them sit on a tie and the page close must round them as the
+    IEEE quotient does (half away from zero)."""
+    batch, exact_ppr, code_ppr = 2, 2, 2
+    n = code_ppr * 16
+    g = torch.Generator().manual_seed(99)
+    cos = torch.ones(n, 128, dtype=torch.float16)
+    sin = torch.zeros(n, 128, dtype=torch.float16)
+    keys = (torch.randint(-254, 255, (n, batch, 8, 128), generator=g).float() / 32).half()
+    values = (torch.randint(-254, 255, (n, batch, 8, 128), generator=g).float() / 32).half()
+    for t in range(0, n, 16):
+        keys[t, :, :, 0] = 127 / 16
+        values[t, :, :, 1] = -127 / 16
+    q = torch.randn(batch, 32, 128, generator=g).half()
+    zero = torch.zeros(batch, 8, 128, dtype=torch.float16)
+    ext = load_append_extension()
+    buf = _gauge_buffers(batch, exact_ppr, code_ppr)
+    st = _oracle_state(batch, exact_ppr, code_ppr)
+    dq, dz, rq = q.cuda(), zero.cuda(), torch.empty(batch, 32, 128, dtype=torch.float16, device="cuda")
+    for p in range(n):
+        ext.rope_append_page_gauge(dq, keys[p].cuda(), values[p].cuda(), cos[p].cuda(), sin[p].cuda(),
+                                   dz, dz, rq, buf["exact_k"], buf["exact_v"], buf["codes_k"],
+                                   buf["codes_v"], buf["scales_k"], buf["scales_v"], 0, p)
+        O.rope_append_page_gauge(st, q.numpy(), keys[p].numpy(), values[p].numpy(), cos[p].numpy(),
+                                 sin[p].numpy(), zero.numpy(), zero.numpy(), 0, p)
+    torch.cuda.synchronize()
+    assert np.all(u16(st.scales_k) == u16(np.float16(1 / 16)))
+    ties = (np.abs(st.exact_k.astype(np.float32) * 16) % 1 == 0.5).sum()
+    assert ties > 1000
+    _assert_state_equal(buf, st)
+
+
 def test_rope_matches_golden_torch_expression(cuda_lib):
     """RoPE of the append kernel equals the reference's torch FP16 pin."""
     g = np.load(GOLDEN / "rope.npz")
