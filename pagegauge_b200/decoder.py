@@ -41,7 +41,7 @@ from dataclasses import dataclass, field
 import numpy as np
 import torch
 
-from . import _lib
+from . import _lib, scheduler
 from .cache import GaugeCache, apply_rope_fp16, rope_tables
 from .decode import PageGaugeDecode
 from .quantize import quantize_pages_into
@@ -414,9 +414,10 @@ class PageGaugeDecoder:
         old_idx = torch.from_numpy(o_idx).to(dev)
         ex_idx = torch.from_numpy(e_idx).to(dev)
         has_old = bool(o_ptr[-1] > 0)
+        split = scheduler.lookup(self.batch, int(max(positions)) + 1)
         dec.plan(torch.from_numpy(o_ptr) if has_old else None, old_idx if has_old else None,
                  torch.from_numpy(e_ptr), ex_idx, self.last_len, self.hq, self.hkv,
-                 old_last_page_len=self._old_last if has_old else None)
+                 old_split_pages=split, old_last_page_len=self._old_last if has_old else None)
         entry = {"dec": dec, "old": old_idx, "exact": ex_idx, "graph": None}
         self._bank[key] = entry
         while len(self._bank) > self._bank_size:

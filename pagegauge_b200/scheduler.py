@@ -43,10 +43,10 @@ def lookup(batch: int, context: int, path: Path = TABLE_PATH) -> int:
 
 
 def candidates(old_pages_per_request: int) -> list[int]:
-    """Split sizes giving num_splits in {1,2,4,...,64} per (request, head),
-    plus 0 for the heuristic."""
+    """Split sizes giving num_splits in 1..64 per (request, head), plus 0
+    for the one-wave heuristic."""
     out = {0}
-    for splits in (1, 2, 4, 8, 16, 32, 48, 64):
+    for splits in (1, 2, 4, 8, 12, 16, 24, 32, 40, 48, 56, 64):
         out.add(max(1, math.ceil(old_pages_per_request / splits)))
     return sorted(out)
 
@@ -63,52 +63,88 @@ def record(batch: int, context: int, results: dict[int, float], path: Path = TAB
     return best
 
 
-def sweep(batch: int, context: int, repeats: int = 60, seeds=(20261001, 20261002, 20261003),
-          write: bool = True, path: Path = TABLE_PATH) -> dict[int, float]:
-    """Time every candidate split on the current GPU (cache-neutral p50 over
-    seeds) and record the winner."""
+def sweep(batch: int, context: int, repeats: int = 30, seeds=(20261001, 20261002, 20261003),
+          write: bool = True, path: Path = TABLE_PATH, lengths: list[int] | None = None,
+          burst: int = 16) -> dict[int, float]:
+    """Time every candidate split on the current GPU and record the winner.
+
+    Each candidate's decode (split kernel + merge) is captured in a CUDA
+    graph behind a 256 MiB scrub (so every step starts from a cold L2); a
+    sample replays that graph ``burst`` times between CUDA events, minus
+    the same burst of a scrub-only graph, divided by ``burst`` (one replay
+    alone is below the event timer's resolution).  The p50 over
+    ``repeats`` samples per seed is averaged over the seeds.  ``lengths``
+    (default ``[context] * batch``) gives ragged batches; the table bucket
+    is (batch, max length)."""
     import torch
 
     from .cache import build_gauge_cache, synthetic_dense_cache
     from .decode import PageGaugeDecode
 
-    lengths = [context] * batch
+    lengths = list(lengths) if lengths is not None else [context] * batch
+    batch, context = len(lengths), max(lengths)
     scrub = torch.zeros(256 << 18, dtype=torch.int32, device="cuda")  # 256 MiB
     ws = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        scrub.add_(1)
+        scrub_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(scrub_graph, stream=stream):
+            scrub.add_(1)
+    torch.cuda.synchronize()
+
+    def burst_us(graph) -> float:
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(burst):
+            graph.replay()
+        e.record()
+        e.synchronize()
+        return s.elapsed_time(e) * 1e3
+
     results: dict[int, list[float]] = {}
     for seed in seeds:
         q, dk, dv = synthetic_dense_cache(lengths, seed=seed, device="cuda")
         cache, tables = build_gauge_cache(dk, dv, lengths)
         del dk, dv
-        old_pages = tables.old_tokens[0] // PAGE
+        old_pages = max(t // PAGE for t in tables.old_tokens)
+        out = torch.empty_like(q)
         for split in candidates(old_pages):
             dec = PageGaugeDecode(ws)
-            dec.plan(tables.old_indptr, tables.old_indices, tables.exact_indptr, tables.exact_indices,
-                     tables.exact_last_page_len, 32, 8, old_split_pages=split)
-            out = torch.empty_like(q)
+            dec.plan(tables.old_indptr, tables.old_indices, tables.exact_indptr,
+                     tables.exact_indices, tables.exact_last_page_len, 32, 8,
+                     old_split_pages=split)
 
             def run():
-                dec.run(q, cache.key_codes, cache.value_codes, cache.key_scales, cache.value_scales,
-                        cache.exact_key, cache.exact_value, cache.value_center, out=out)
+                dec.run(q, cache.key_codes, cache.value_codes, cache.key_scales,
+                        cache.value_scales, cache.exact_key, cache.exact_value,
+                        cache.value_center, out=out)
 
-            for _ in range(5):
-                run()
-            times = []
-            for _ in range(repeats):
-                scrub.add_(1)
-                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                s.record()
-                run()
-                e.record()
-                e.synchronize()
-                times.append(s.elapsed_time(e) * 1e3)
+            with torch.cuda.stream(stream):
+                for _ in range(3):
+                    run()
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=stream):
+                    scrub.add_(1)
+                    run()
+                for _ in range(3):
+                    graph.replay()
+                times = []
+                for _ in range(repeats):
+                    both = burst_us(graph)
+                    only = burst_us(scrub_graph)
+                    times.append((both - only) / burst)
+            torch.cuda.synchronize()
+            del graph
             results.setdefault(split, []).append(statistics.median(times))
         del cache
-    p50 = {k: statistics.median(v) for k, v in results.items()}
+    p50 = {k: statistics.fmean(v) for k, v in results.items()}
     if write:
         record(batch, context, p50, path=path,
                meta={"gpu": torch.cuda.get_device_name(), "repeats": repeats,
-                     "seeds": list(seeds), "mode": "cache_neutral"})
+                     "seeds": list(seeds), "lengths": lengths,
+                     "burst": burst,
+                     "mode": "cache-neutral: CUDA graph of scrub + decode, minus scrub alone"})
     return p50
 
 
@@ -118,6 +154,8 @@ def main() -> None:
     parser.add_argument("--batch", type=int, nargs="*", default=[1])
     parser.add_argument("--context", type=int, nargs="*", default=[49152])
     parser.add_argument("--repeats", type=int, default=60)
+    parser.add_argument("--ragged", type=int, default=0,
+                        help="also sweep a ragged batch of this size (contexts U[4096, 32768])")
     parser.add_argument("--table", type=Path, default=TABLE_PATH)
     args = parser.parse_args()
     if not args.sweep:
@@ -126,6 +164,11 @@ def main() -> None:
     for b in args.batch:
         for c in args.context:
             print(b, c, json.dumps(sweep(b, c, args.repeats, path=args.table)), flush=True)
+    if args.ragged:
+        from .shard import ragged_lengths
+        lengths = ragged_lengths(args.ragged, 20261001)
+        print("ragged", lengths, json.dumps(sweep(0, 0, args.repeats, path=args.table,
+                                                  lengths=lengths)), flush=True)
 
 
 if __name__ == "__main__":

@@ -1,0 +1,111 @@
+"""Tensor-parallel PageGauge decoder on two GPUs (NCCL): each rank holds half
+of the KV heads, FFN columns and vocabulary; the gathered logits of the
+prefill and of graph-captured decode steps must match the single-model
+CPU oracle.  Skipped unless two GPUs are visible."""
+
+from __future__ import annotations
+
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+WORLD = 2
+STEPS = 6
+
+
+def _cfg():
+    from pagegauge_b200.decoder import DecoderConfig
+    return DecoderConfig(layers=2, hidden=512, heads=8, kv_heads=2, intermediate=1024, vocab=512)
+
+
+def _rank(rank, port, prompt, result):
+    import torch.distributed as dist
+
+    from pagegauge_b200.decoder import PageGaugeDecoder, TensorParallel, random_decoder_weights
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=WORLD,
+                            timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        cfg = _cfg()
+        w = random_decoder_weights(cfg, 41, device="cuda", gen_device="cpu",
+                                   tp=TensorParallel.of(cfg, rank, WORLD))
+        dec = PageGaugeDecoder(w, batch=prompt.shape[0], max_context=512,
+                               process_group=dist.group.WORLD)
+        logits = [dec.prefill(prompt.cuda()).float()]
+        tokens = [dec.tokens.clone()]
+        # This rank's caches after the prefill (its KV heads), for the oracle.
+        mine = [{k: getattr(c, k).cpu().numpy() for k in
+                 ("exact_key", "exact_value", "key_codes", "value_codes", "key_scales",
+                  "value_scales", "key_center", "value_center")} for c in dec.caches]
+        caches = [None] * WORLD
+        dist.all_gather_object(caches, mine)
+        for _ in range(STEPS):
+            dec.step(use_graph=True)
+            logits.append(dec.logits.float().clone())
+            tokens.append(dec.tokens.clone())
+        local = torch.stack(logits)  # [steps+1, B, V/2]
+        parts = [torch.empty_like(local) for _ in range(WORLD)]
+        dist.all_gather(parts, local)
+        if rank == 0:
+            full = {}
+            for l in range(cfg.layers):
+                for k in caches[0][l]:
+                    axis = 1 if k in ("key_scales", "value_scales", "key_center",
+                                      "value_center") else 2
+                    full[f"{l}_{k}"] = np.concatenate([c[l][k] for c in caches], axis=axis)
+            np.savez(result, logits=torch.cat(parts, -1).cpu().numpy(),
+                     tokens=torch.stack(tokens).cpu().numpy(),
+                     cos=dec.cos.cpu().numpy(), sin=dec.sin.cpu().numpy(),
+                     capacity=dec.capacity_pages, **full)
+        dist.barrier()
+        del dec
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs two GPUs")
+def test_two_gpu_tensor_parallel_decoder_matches_oracle(cuda_lib, tmp_path):
+    from oracle import decoder_oracle as D
+    from oracle import pagegauge_oracle as O
+
+    from test_decoder_oracle import oracle_cfg, oracle_weights
+
+    cfg = _cfg()
+    prompt = torch.randint(0, cfg.vocab, (2, 200), generator=torch.Generator().manual_seed(12))
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    path = str(tmp_path / "tp.npz")
+    mp.spawn(_rank, args=(port, prompt, path), nprocs=WORLD, join=True)
+    got = np.load(path)
+    logits, tokens = got["logits"], got["tokens"]
+    w, ocfg = oracle_weights(cfg, seed=41), oracle_cfg(cfg)
+    for r in range(2):
+        exp, _ = D.dense_forward(w, ocfg, prompt[r].numpy())
+        err = np.abs(logits[0, r] - exp).max()
+        assert err < 2e-3, err
+    # Greedy tokens are the argmax of the gathered logits at every step.
+    assert np.array_equal(tokens, logits.argmax(-1))
+    # Decode steps from the gathered post-prefill caches, teacher-forced
+    # with the GPU's tokens.
+    caches = []
+    for l in range(cfg.layers):
+        g = lambda k: got[f"{l}_{k}"].copy()
+        caches.append({"state": O.GaugeState(g("exact_key"), g("exact_value"), g("key_codes"),
+                                             g("value_codes"), g("key_scales"), g("value_scales")),
+                       "key_center": g("key_center"), "value_center": g("value_center")})
+    ocfg["rope"] = (got["cos"], got["sin"])
+    for i in range(STEPS):
+        exp = D.decode_step(w, ocfg, caches, tokens[i], [200 + i] * 2, int(got["capacity"]))
+        err = np.abs(logits[i + 1] - exp).max()
+        assert err < 2e-3, (i, err)
