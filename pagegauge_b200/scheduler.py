@@ -24,8 +24,9 @@ PAGE = 16
 
 
 def bucket(batch: int, context: int) -> str:
-    """Batch exact, context rounded up to a power of two (>= 1024)."""
-    c = 1 << max(10, math.ceil(math.log2(max(context, 1))))
+    """Batch exact, context rounded down to a power of two (>= 1024): a
+    bucket c covers contexts [c, 2c)."""
+    c = 1 << max(10, int(math.floor(math.log2(max(context, 1)))))
     return f"b{batch}_c{c}"
 
 

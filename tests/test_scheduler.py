@@ -1,0 +1,40 @@
+"""Split scheduler host logic: buckets, the committed measured table, and
+record/lookup round trips (no GPU)."""
+
+from __future__ import annotations
+
+from pagegauge_b200 import scheduler as S
+
+
+def test_buckets_cover_power_of_two_ranges():
+    assert S.bucket(1, 16384) == S.bucket(1, 32767) == "b1_c16384"
+    assert S.bucket(1, 49152) == "b1_c32768"
+    assert S.bucket(8, 100) == "b8_c1024"
+
+
+def test_committed_table_has_the_benchmark_shapes():
+    entries = S.load_table()["entries"]
+    for key in ("b1_c4096", "b1_c16384", "b1_c32768", "b8_c16384", "b32_c16384"):
+        e = entries[key]
+        assert e["split_pages"] == min(e["candidates_us"], key=lambda k: e["candidates_us"][k]) \
+            or str(e["split_pages"]) == min(e["candidates_us"], key=e["candidates_us"].get)
+        assert e["p50_us"] == min(e["candidates_us"].values())
+    assert S.lookup(1, 49152) == entries["b1_c32768"]["split_pages"]
+
+
+def test_unmeasured_bucket_falls_back_to_heuristic(tmp_path):
+    assert S.lookup(3, 5000, path=tmp_path / "none.json") == 0
+
+
+def test_record_keeps_the_argmin(tmp_path):
+    path = tmp_path / "t.json"
+    assert S.record(2, 8192, {0: 12.0, 64: 10.5, 128: 11.0}, path=path) == 64
+    assert S.lookup(2, 9000, path=path) == 64
+    assert S.record(2, 8192, {0: 9.0, 64: 10.5}, path=path) == 0
+    assert S.lookup(2, 8192, path=path) == 0
+
+
+def test_candidates_span_one_to_64_splits():
+    c = S.candidates(3056)
+    assert c[0] == 0 and 3056 in c and 48 in c and 64 in c
+    assert all(-(-3056 // s) <= 64 for s in c if s)
