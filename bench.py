@@ -57,6 +57,9 @@ def parse_args():
     p.add_argument("--merge", choices=("kernel", "fused"), default="kernel",
                    help="cross-CTA merge: separate merge kernel or last-CTA merge in the split kernel")
     p.add_argument("--only", action="store_true", help="skip the secondary workloads")
+    p.add_argument("--decoder-batch", type=int, nargs="*", default=[32, 1],
+                   help="decoder workload: batch sizes (the first is the headline)")
+    p.add_argument("--decoder-steps", type=int, default=16)
     p.add_argument("--no-cpu-baseline", action="store_true")
     return p.parse_args()
 
@@ -671,11 +674,13 @@ def measure_decoder(dist: Dist, batch: int, context: int = 16384, steps: int = 1
     torch.cuda.synchronize()
     dist.barrier()
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    torch.cuda.nvtx.range_push("pg_timed")
     ev[0].record(dec.stream)
     for _ in range(steps):
         dec.step()
     ev[1].record(dec.stream)
     torch.cuda.synchronize()
+    torch.cuda.nvtx.range_pop()
     dist.barrier()
     ms = dist.reduce(ev[0].elapsed_time(ev[1]) / steps, "max")
     # End to end: every step's tokens come back to pinned host memory and the
@@ -695,6 +700,7 @@ def measure_decoder(dist: Dist, batch: int, context: int = 16384, steps: int = 1
     out = {
         "batch": batch, "context": context, "tp": world, "steps": steps,
         "tokens_per_s": round(batch / (ms * 1e-3), 2), "ms_per_step": ms,
+        "kernel_launches_per_step": dec.launches_per_step(),
         "e2e_tokens_per_s": round(batch / e2e_s, 2),
         "hbm_bytes_per_step_per_rank": nbytes, "achieved_gbs_per_rank": round(achieved, 1),
         "roofline_frac": round(achieved / peak, 4), "prefill_s": round(prefill_s, 2),
@@ -708,13 +714,17 @@ def measure_decoder(dist: Dist, batch: int, context: int = 16384, steps: int = 1
 def run_decoder(args, dist: Dist, local: int) -> None:
     rank = int(os.environ.get("RANK", "0"))
     clocks = ClockSampler(local)
+    batches = args.decoder_batch or [32]
+    results = {}
     with clocks:
-        b32 = measure_decoder(dist, 32)
-    b1 = measure_decoder(dist, 1)
+        results[batches[0]] = measure_decoder(dist, batches[0], steps=args.decoder_steps)
+    for b in batches[1:]:
+        results[b] = measure_decoder(dist, b, steps=args.decoder_steps)
+    b32 = results[batches[0]]
     peak, peak_src = peak_hbm()
     if rank == 0:
         line = {
-            "metric": "decoder tokens/s (Mistral-7B-shaped, B=32, ctx 16384)",
+            "metric": f"decoder tokens/s (Mistral-7B-shaped, B={batches[0]}, ctx 16384)",
             "value": b32["tokens_per_s"], "unit": "tokens/s", "n_gpus": dist.world,
             "steps": b32["steps"], "warmup": 1, "ms_per_step": b32["ms_per_step"],
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
@@ -727,9 +737,9 @@ def run_decoder(args, dist: Dist, local: int) -> None:
                          "unit": "GB/s", "frac": b32["roofline_frac"], "traffic": None,
                          "peak_source": peak_src, "kernel": "whole decode step"},
             "e2e": {"value": b32["e2e_tokens_per_s"], "unit": "tokens/s",
-                    "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 8 * 32},
+                    "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 8 * batches[0]},
             "clocks": clocks.summary(),
-            "workloads": {"decoder_b32": b32, "decoder_b1": b1},
+            "workloads": {f"decoder_b{b}": r for b, r in results.items()},
         }
         print(json.dumps(line), flush=True)
 

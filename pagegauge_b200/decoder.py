@@ -459,6 +459,17 @@ class PageGaugeDecoder:
         _call("pg_step_positions", self.positions.data_ptr(), self.last_len.data_ptr(), B, 1,
               _stream())
 
+    def launches_per_step(self) -> int:
+        """Kernel launches of this library in one decode step (append,
+        split decode, merge, two norms and SiLU*up per layer; the final norm
+        and the position update)."""
+        entry = next(iter(self._bank.values()), None)
+        attn = 2
+        if entry is not None:
+            plan = entry["dec"].work_plan
+            attn = 1 if (plan.single and plan.num_items) else 2
+        return self.cfg.layers * (4 + attn) + 2
+
     def _capture(self, entry: dict) -> None:
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=self.stream):
