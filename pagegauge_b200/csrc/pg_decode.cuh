@@ -532,22 +532,165 @@ __device__ __forceinline__ void issue_page(const CUtensorMap* tk,
   }
 }
 
-template <int SEG>
-__device__ __forceinline__ void prefetch_page(const CUtensorMap* tk,
-                                              const CUtensorMap* tv, int id, int h) {
-  if (SEG == 0) {
-    tma_prefetch_l2_3d(tk, 0, h, id * kPage);
-    tma_prefetch_l2_3d(tv, 0, h, id * kPage);
-  } else {
-    tma_prefetch_l2_3d(tk, 0, 2 * h, id * kPage);
-    tma_prefetch_l2_3d(tk, 0, 2 * h + 1, id * kPage);
-    tma_prefetch_l2_3d(tv, 0, 2 * h, id * kPage);
-    tma_prefetch_l2_3d(tv, 0, 2 * h + 1, id * kPage);
+// INT8 pages of one warp, two at a time.  The 4-stage ring is used as two
+// pair slots, each with one mbarrier that completes when both pages' K and
+// V tiles have landed (one wait per pair), and one elected lane issues a
+// pair's four tile copies.  When the warp's pages fit the id window (<= 64)
+// the V-scale reference s_ref is the maximum over all of them, known before
+// the first page, so P * s_V / s_ref never needs a mid-stream rescale and
+// the ratios sit in the window; longer runs raise s_ref as they go.
+__device__ __forceinline__ void issue_pair_int8(const CUtensorMap* tk, const CUtensorMap* tv,
+                                                uint8_t* dst, uint64_t* bar, int n, int id0,
+                                                int id1, int h) {
+  mbar_arrive_expect_tx(bar, n * 4096);
+  tma_load_3d(dst, tk, 0, h, id0 * kPage, bar);
+  tma_load_3d(dst + 2048, tv, 0, h, id0 * kPage, bar);
+  if (n == 2) {
+    tma_load_3d(dst + 4096, tk, 0, h, id1 * kPage, bar);
+    tma_load_3d(dst + 6144, tv, 0, h, id1 * kPage, bar);
   }
 }
 
-// Pages prefetched into L2 ahead of the shared-memory ring (per warp).
-constexpr int kL2Ahead = 0;
+__device__ __forceinline__ bool run_warp_pages_int8(
+    const DecodeParams& p, const CUtensorMap* tk, const CUtensorMap* tv,
+    WarpState& st, uint8_t* ring, uint64_t* bars, QInt8& qi, int r,
+    int h, int idx_begin, int n_pages, bool has_last, int warp, int W,
+    int lane) {
+  const int g = lane >> 2, t = lane & 3;
+  const SegmentDesc& sd = p.seg[0];
+  const int n_w = n_pages > warp ? (n_pages - warp + W - 1) / W : 0;
+  if (n_w == 0) return true;
+  const int n_pairs = (n_w + 1) >> 1;
+
+  PageWindow win;
+  win.base = 0;
+  win.two = n_w > 32;
+  load_window_set<0>(p, sd, idx_begin, warp, W, n_w, h, 0, lane, win.id_a, win.sk_a,
+                     win.sv_a);
+  win.id_b = 0;
+  win.sk_b = win.sv_b = 0.f;
+  if (win.two)
+    load_window_set<0>(p, sd, idx_begin, warp, W, n_w, h, 32, lane, win.id_b, win.sk_b,
+                       win.sv_b);
+
+  // Prologue: pairs 0 and 1 (pages 0-3).
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    if (q < n_pairs) {
+      const int u = 2 * q;
+      const int n = u + 1 < n_w ? 2 : 1;
+      const int id0 = win_id(win, u);
+      const int id1 = win_id(win, n == 2 ? u + 1 : u);
+      if (lane == 0) issue_pair_int8(tk, tv, ring + q * 8192, bars + q, n, id0, id1, h);
+    }
+  }
+
+  uint32_t vaddr[4];
+  {
+    const int j = lane >> 3, row = lane & 7;
+    const int tok = 8 * (j & 1) + row;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) vaddr[k] = tok * 128 + (((2 * k + (j >> 1)) ^ row) << 4);
+  }
+  pdl_wait_primary();
+  int last_valid = kPage;
+  if (has_last) {
+    const int lv = __ldg(sd.last_len + r);
+    last_valid = lv < 1 ? 1 : (lv > kPage ? kPage : lv);
+  }
+  // The warp's last page is the request's last page when it is the item's.
+  const bool last_here = has_last && warp + W * (n_w - 1) == n_pages - 1;
+  load_q_int8(p, r, h, g, t, qi);
+
+  // V-scale reference and per-page ratios s_V / s_ref.
+  const bool fixed_ref = n_w <= 64;
+  if (fixed_ref) {
+    float m = fmaxf(win.sv_a, win.sv_b);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    st.sref = m;
+    const float inv = m > 0.f ? 1.f / m : 1.f;
+    win.sv_a = m > 0.f ? win.sv_a * inv : 1.f;
+    win.sv_b = m > 0.f ? win.sv_b * inv : 1.f;
+  } else {
+    st.sref = win_f(win, win.sv_a, win.sv_b, 0);
+  }
+
+  bool ok = true;
+  int q = 0;
+  for (; q < n_pairs; ++q) {
+    const int u = 2 * q;
+    const bool two = u + 1 < n_w;
+    const bool waited = mbar_wait_bounded(bars + (q & 1), static_cast<uint32_t>(q >> 1) & 1u);
+    if (!__all_sync(0xffffffffu, waited)) {
+      ok = false;
+      break;
+    }
+    const uint8_t* stg[2] = {ring + (q & 1) * 8192, ring + (q & 1) * 8192 + 4096};
+    float sk[2], rr[2];
+    int valid[2] = {kPage, kPage};
+    sk[0] = win_f(win, win.sk_a, win.sk_b, u - win.base);
+    sk[1] = win_f(win, win.sk_a, win.sk_b, (two ? u + 1 : u) - win.base);
+    if (fixed_ref) {
+      rr[0] = win_f(win, win.sv_a, win.sv_b, u - win.base);
+      rr[1] = win_f(win, win.sv_a, win.sv_b, (two ? u + 1 : u) - win.base);
+    } else {
+      const float sv0 = win_f(win, win.sv_a, win.sv_b, u - win.base);
+      const float sv1 = win_f(win, win.sv_a, win.sv_b, (two ? u + 1 : u) - win.base);
+      const float svmax = fmaxf(sv0, sv1);
+      if (svmax > st.sref) {
+        // Keep P * (s_V / s_ref) <= P in FP16 by raising the reference.
+        const float f = st.sref / svmax;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) st.o[i] *= f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) st.o1[i] *= f;
+        st.sref = svmax;
+      }
+      const float inv_ref = st.sref > 0.f ? __fdividef(1.f, st.sref) : 1.f;
+      rr[0] = st.sref > 0.f ? sv0 * inv_ref : 1.f;
+      rr[1] = st.sref > 0.f ? sv1 * inv_ref : 1.f;
+    }
+    if (last_here && q == n_pairs - 1) {
+      if (two)
+        valid[1] = last_valid;
+      else
+        valid[0] = last_valid;
+    }
+    if (two)
+      pages_int8<2>(st, stg, qi, sk, rr, valid, g, t, vaddr);
+    else
+      pages_int8<1>(st, stg, qi, sk, rr, valid, g, t, vaddr);
+    __syncwarp();
+    // Refill this pair slot with pair q + 2.
+    const int nq = q + 2;
+    if (nq < n_pairs) {
+      const int nu = 2 * nq;
+      const int n = nu + 1 < n_w ? 2 : 1;
+      const int id0 = win_id(win, nu);
+      const int id1 = win_id(win, n == 2 ? nu + 1 : nu);
+      if (lane == 0) issue_pair_int8(tk, tv, ring + (q & 1) * 8192, bars + (q & 1), n, id0, id1, h);
+    }
+    // Slide the id window once the consumer leaves its first half (the
+    // refill above may read up to 3 pages ahead of the consumer).
+    if (win.two && u + 2 - win.base >= 32) {
+      win.base += 32;
+      win.id_a = win.id_b;
+      win.sk_a = win.sk_b;
+      win.sv_a = win.sv_b;
+      load_window_set<0>(p, sd, idx_begin, warp, W, n_w, h, win.base + 32, lane, win.id_b,
+                         win.sk_b, win.sv_b);
+    }
+  }
+  if (!ok) {
+    record_error(p.error_flag, kDevWaitTimeout);
+    // Drain copies still in flight into this warp's ring before exiting.
+    const int issued_end = q + 2 < n_pairs ? q + 2 : n_pairs;
+    for (int v = q; v < issued_end; ++v)
+      mbar_wait_bounded(bars + (v & 1), static_cast<uint32_t>(v >> 1) & 1u);
+  }
+  return ok;
+}
 
 template <int SEG, typename QFrag>
 __device__ __forceinline__ bool run_warp_pages(
@@ -579,15 +722,11 @@ __device__ __forceinline__ bool run_warp_pages(
     load_window_set<SEG>(p, sd, idx_begin, warp, W, n_w, h, 32, lane, win.id_b,
                          win.sk_b, win.sv_b);
 
-  // Prologue: fill the ring, then start the L2 prefetch window behind it.
+  // Prologue: fill the ring.
   const int pro = n_w < S ? n_w : S;
   for (int u = 0; u < pro; ++u) {
     const int id = win_id(win, u);
     if (lane == 0) issue_page<SEG>(tk, tv, ring, bars, u, id, h);
-  }
-  for (int u = S; u < S + kL2Ahead && u < n_w; ++u) {
-    const int id = win_id(win, u);
-    if (lane == 0) prefetch_page<SEG>(tk, tv, id, h);
   }
 
   // ldmatrix row addresses for the V tile (see pv_int8): lane l reads row
@@ -666,11 +805,6 @@ __device__ __forceinline__ bool run_warp_pages(
       if (nu < n_w) {
         const int id = win_id(win, nu);
         if (lane == 0) issue_page<SEG>(tk, tv, ring, bars, (u + j) % S, id, h);
-      }
-      const int pu = nu + kL2Ahead;
-      if (pu < n_w) {
-        const int id = win_id(win, pu);
-        if (lane == 0) prefetch_page<SEG>(tk, tv, id, h);
       }
     }
     u += np;
@@ -775,7 +909,9 @@ __device__ __forceinline__ void merge_head(const DecodeParams& p, int r, int h,
   }
 }
 
-__global__ void __launch_bounds__(kMaxWarps * 32, 1)
+// 168 registers per thread at most: three 4-warp CTAs per SM (the host
+// planner's slot count assumes it).
+__global__ void __maxnreg__(168)
     pg_decode_split_kernel(const __grid_constant__ CUtensorMap tm_k8,
                            const __grid_constant__ CUtensorMap tm_v8,
                            const __grid_constant__ CUtensorMap tm_k16,
@@ -829,8 +965,8 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1)
   bool ok;
   if (seg == 0) {
     QInt8 qi;
-    ok = run_warp_pages<0>(p, &tm_k8, &tm_v8, st, ring, bars, qi, r, h,
-                           item.idx_begin, n_pages, has_last, warp, W, lane);
+    ok = run_warp_pages_int8(p, &tm_k8, &tm_v8, st, ring, bars, qi, r, h,
+                             item.idx_begin, n_pages, has_last, warp, W, lane);
     // Remove the +1152 code bias of the PV operand: O -= 1152 * sum(P'').
     const float sp0 = 1152.f * __shfl_sync(0xffffffffu, st.o1[0], t);
     const float sp1 = 1152.f * __shfl_sync(0xffffffffu, st.o1[1], t);
