@@ -54,6 +54,7 @@ def parse_args():
     p.add_argument("--split", type=int, default=-1,
                    help="pages per work item (-1: measured scheduler table, 0: heuristic)")
     p.add_argument("--layers", type=int, default=4)
+    p.add_argument("--warps", type=int, default=4, help="warps per split-KV CTA")
     p.add_argument("--merge", choices=("kernel", "fused"), default="kernel",
                    help="cross-CTA merge: separate merge kernel or last-CTA merge in the split kernel")
     p.add_argument("--only", action="store_true", help="skip the secondary workloads")
@@ -309,7 +310,8 @@ class AttentionBench:
     """One workload's caches (``layers`` copies), its plan, and CUDA graphs
     of the public-API decode step."""
 
-    def __init__(self, lengths, layers: int, split: int, fused_merge: bool, seed: int):
+    def __init__(self, lengths, layers: int, split: int, fused_merge: bool, seed: int,
+                 warps: int = 4):
         from pagegauge_b200 import scheduler
         from pagegauge_b200.cache import build_gauge_cache, rope_tables, synthetic_dense_cache
         from pagegauge_b200.decode import PageGaugeDecode
@@ -332,7 +334,7 @@ class AttentionBench:
         if split < 0:
             split = scheduler.lookup(len(lengths), max(lengths))
         self.ws = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
-        self.dec = PageGaugeDecode(self.ws)
+        self.dec = PageGaugeDecode(self.ws, warps_per_cta=warps)
         t = self.tables
         self.dec.plan(t.old_indptr, t.old_indices, t.exact_indptr, t.exact_indices,
                       t.exact_last_page_len, HQ, HKV, old_split_pages=split, exact_split_pages=0)
@@ -449,15 +451,17 @@ class AttentionBench:
         ext = load_append_extension()
         B = len(self.lengths)
         g = torch.Generator().manual_seed(SEED + 77)
-        hq = torch.randn(B, HQ, DIM, generator=g).half().pin_memory()
-        hk = torch.randn(B, HKV, DIM, generator=g).half().pin_memory()
-        hv = torch.randn(B, HKV, DIM, generator=g).half().pin_memory()
+        # The new token's q | k | v rows packed per request (the layout of a
+        # fused qkv projection), one host->device copy per step.
+        width = (HQ + 2 * HKV) * DIM
+        hqkv = torch.randn(B, width, generator=g).half().pin_memory()
         hout = torch.empty(B, HQ, DIM, dtype=torch.float16).pin_memory()
-        dq = torch.empty(B, HQ, DIM, dtype=torch.float16, device="cuda")
-        dk = torch.empty(B, HKV, DIM, dtype=torch.float16, device="cuda")
-        dv = torch.empty_like(dk)
-        rq = torch.empty_like(dq)
-        out = torch.empty_like(dq)
+        dqkv = torch.empty(B, width, dtype=torch.float16, device="cuda")
+        dq = dqkv[:, :HQ * DIM].view(B, HQ, DIM)
+        dk = dqkv[:, HQ * DIM:(HQ + HKV) * DIM].view(B, HKV, DIM)
+        dv = dqkv[:, (HQ + HKV) * DIM:].view(B, HKV, DIM)
+        rq = torch.empty(B, HQ, DIM, dtype=torch.float16, device="cuda")
+        out = torch.empty_like(rq)
         # Each step re-appends the last token of every request (its page
         # stays in the exact window), so the cache shape is unchanged.
         positions = torch.tensor([n - 1 for n in self.lengths], dtype=torch.int32, device="cuda")
@@ -465,9 +469,7 @@ class AttentionBench:
 
         def one(layer: int):
             c = self.caches[layer]
-            dq.copy_(hq, non_blocking=True)
-            dk.copy_(hk, non_blocking=True)
-            dv.copy_(hv, non_blocking=True)
+            dqkv.copy_(hqkv, non_blocking=True)
             ext.rope_append_page_gauge_batched(dq, dk, dv, cos, sin, positions, c.key_center,
                                                c.value_center, rq, c.exact_key, c.exact_value,
                                                c.key_codes, c.value_codes, c.key_scales,
@@ -506,7 +508,7 @@ class AttentionBench:
                 torch.cuda.synchronize()
             if dist.reduce(ok, "sum") == dist.world:
                 graph_ms = timed(lambda i: graphs[i % self.layers].replay(), steps)
-        h2d = (hq.numel() + hk.numel() + hv.numel()) * 2
+        h2d = hqkv.numel() * 2
         return {"eager_ms": eager_ms, "graph_ms": graph_ms, "graph_error": err,
                 "h2d": h2d, "d2h": hout.numel() * 2, "launches_per_step": 1 + self.launches_per_step}
 
@@ -773,7 +775,7 @@ def main() -> None:
     peak, peak_src = peak_hbm()
     lengths, glob, shards = workload_lengths(args.workload, world, rank)
     bench = AttentionBench(lengths, args.layers, args.split, args.merge == "fused",
-                           seed=SEED + 1000 * rank)
+                           seed=SEED + 1000 * rank, warps=args.warps)
     bench.capture()
     clocks = ClockSampler(local)
     ms = bench.time_steps(args.steps, args.warmup, dist, clocks)

@@ -206,6 +206,9 @@ __device__ __forceinline__ void rotate_query_heads(const AppendParams& p, int r,
 
 __global__ void __launch_bounds__(kAppendThreads)
     pg_rope_append_fp16_kernel(const __grid_constant__ AppendParams p) {
+  // A dependent decode launch may start streaming completed INT8 pages now
+  // (it waits for this grid before reading anything written here).
+  pdl_launch_dependents();
   const int r = blockIdx.x / p.hkv;
   const int h = blockIdx.x % p.hkv;
   const int g = threadIdx.x >> 6, j = threadIdx.x & 63;
@@ -292,6 +295,11 @@ __device__ __forceinline__ uint2 quantize_half8(const uint4& v, float scale, flo
 __global__ void __launch_bounds__(kAppendThreads)
     pg_rope_append_page_gauge_kernel(const __grid_constant__ AppendParams p) {
   __shared__ float red[2][kAppendThreads / 32];
+  // A dependent decode launch may start streaming completed INT8 pages now:
+  // the page this launch may close is still in the exact window, so the
+  // decode reads it from the ring, and the decode waits for this grid
+  // before reading q or the ring.
+  pdl_launch_dependents();
   __shared__ __align__(16) uint32_t newest[2][kHeadDim / 2];
   const int r = blockIdx.x / p.hkv;
   const int h = blockIdx.x % p.hkv;
