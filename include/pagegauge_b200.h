@@ -260,6 +260,44 @@ int32_t pg_quantize_pages(const void* key, const void* value,
 /* Decoder-layer element-wise steps around the attention path (the Mistral   */
 /* layer body of scripts/benchmark_page_gauge_transformer.py:2754-2804).    */
 
+/* Weight-streaming skinny GEMM of the decoder projections,
+ * Y[b, n] = sum_k X[b, k] W[n, k] for batch <= 32 rows (FP16 in, FP32
+ * accumulation), split over the GPU "stream-K" (equal k-block ranges per
+ * CTA, the last CTA of a split tile finishes it in a fixed order, so
+ * results are deterministic), with the layer's element-wise step fused:
+ *   mode 0  y = f16(acc)
+ *   mode 1  residual = f16(residual + f16(acc))         (o_proj, down_proj)
+ *   mode 2  y[b, j] = f16(f16(silu(f16(acc[b, j]))) * f16(acc[b, n/2 + j]))
+ *           for the packed gate|up projection (rows [0, n/2) gate, rest up).
+ * The reference runs these through cuBLAS (F.linear in
+ * scripts/benchmark_page_gauge_transformer.py:2754-2804).  partials and
+ * counters are caller-owned scratch sized by pg_skinny_gemm_workspace;
+ * counters must be zero before the first call and are left zero.  pdl = 1
+ * launches as a programmatic dependent: weights are requested before the
+ * previous kernel in the stream has finished, activations after.         */
+typedef struct pg_gemm_args {
+  const void* w;       /* [n, k] fp16 */
+  int64_t ldw;
+  const void* x;       /* [batch, k] fp16 */
+  int64_t ldx;
+  void* y;             /* mode 0: [batch, n]; mode 2: [batch, n/2] */
+  int64_t ldy;
+  void* residual;      /* mode 1: [batch, n], updated in place */
+  int64_t ldr;
+  int32_t n, k, batch, mode;
+  int32_t grid;        /* CTAs; 0: all resident slots */
+  int32_t pdl;
+  float* partials;
+  int64_t partial_floats;
+  int32_t* counters;
+  int32_t num_counters;
+} pg_gemm_args;
+
+int32_t pg_skinny_gemm_workspace(int32_t n, int32_t k, int32_t batch, int32_t mode,
+                                 int32_t grid, int32_t num_sms, int64_t* partial_floats,
+                                 int32_t* counters);
+int32_t pg_skinny_gemm(const pg_gemm_args* args, void* stream);
+
 /* residual = f16(residual + delta) in place (delta may be NULL), then
  * out = f16(weight * f16(residual * rsqrt(mean(residual^2) + eps))), FP32
  * reduction; rows x hidden FP16, hidden a multiple of 8 up to 16384.       */

@@ -52,6 +52,16 @@ class PgDecodeArgs(ctypes.Structure):
     ]
 
 
+class PgGemmArgs(ctypes.Structure):
+    _fields_ = [
+        ("w", c_vp), ("ldw", c_i64), ("x", c_vp), ("ldx", c_i64), ("y", c_vp), ("ldy", c_i64),
+        ("residual", c_vp), ("ldr", c_i64),
+        ("n", c_i32), ("k", c_i32), ("batch", c_i32), ("mode", c_i32), ("grid", c_i32),
+        ("pdl", c_i32), ("partials", c_vp), ("partial_floats", c_i64), ("counters", c_vp),
+        ("num_counters", c_i32),
+    ]
+
+
 # name -> (restype, argtypes); every entry point returns int32 status.
 _SIGNATURES = {
     "pg_last_error": (ctypes.c_char_p, []),
@@ -84,6 +94,9 @@ _SIGNATURES = {
                                ctypes.c_float, c_vp]),
     "pg_silu_mul": (c_i32, [c_vp, c_vp, c_i32, c_i32, c_i64, c_i64, c_vp]),
     "pg_step_positions": (c_i32, [c_vp, c_vp, c_i32, c_i32, c_vp]),
+    "pg_skinny_gemm_workspace": (c_i32, [c_i32, c_i32, c_i32, c_i32, c_i32, c_i32,
+                                         ctypes.POINTER(c_i64), c_i32p]),
+    "pg_skinny_gemm": (c_i32, [ctypes.POINTER(PgGemmArgs), c_vp]),
     "pg_quantize_pages": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, c_i64, c_i32, c_i32, c_vp]),
 }
 

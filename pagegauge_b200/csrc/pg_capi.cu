@@ -16,6 +16,7 @@
 #include "pg_append.cuh"
 #include "pg_decode.cuh"
 #include "pg_decoder.cuh"
+#include "pg_gemm.cuh"
 
 namespace {
 
@@ -802,6 +803,176 @@ int32_t pg_step_positions(int32_t* positions, int32_t* last_page_len, int32_t ba
   pg::pg_step_positions_kernel<<<(batch + 127) / 128, 128, 0, static_cast<cudaStream_t>(stream)>>>(
       positions, last_page_len, batch, advance);
   return cuda_check(cudaGetLastError(), "step_positions launch");
+}
+
+// ------------------------------------------------------- skinny GEMM
+namespace {
+
+int32_t make_2d_map(CUtensorMap* map, const void* base, int64_t inner, int64_t rows,
+                    int64_t row_stride_elems, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return fail(PG_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_stride_elems) * 2};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(pg::kGemmBK), static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims,
+                  strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(PG_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  return PG_OK;
+}
+
+int gemm_nt(int batch) { return batch <= 8 ? 1 : (batch <= 16 ? 2 : 4); }
+
+// Static shared memory of the kernel (epilogue tile) plus 1 KB per CTA.
+int gemm_ctas_per_sm(int nt) {
+  const int stat = pg::kGemmTileRows * (8 * nt + 1) * 4 + 16;
+  return std::max(1, (228 * 1024) / (pg::gemm_smem_bytes(nt) + stat + 1024));
+}
+
+struct GemmShape {
+  int32_t tiles, kblocks, grid, max_seg, total;
+};
+
+int32_t gemm_shape(int32_t n, int32_t k, int32_t batch, int32_t mode, int32_t grid,
+                   int32_t num_sms, GemmShape* out) {
+  PG_REQUIRE(batch >= 1 && batch <= 32, "batch must be 1..32");
+  PG_REQUIRE(k > 0 && k % pg::kGemmBK == 0, "k must be a positive multiple of 64");
+  PG_REQUIRE(mode >= 0 && mode <= 2, "mode must be 0 (store), 1 (residual) or 2 (silu_mul)");
+  if (mode == pg::kGemmSiluMul)
+    PG_REQUIRE(n > 0 && n % 64 == 0, "silu_mul needs n (gate + up rows) a positive multiple of 64");
+  else
+    PG_REQUIRE(n > 0 && n % pg::kGemmTileRows == 0, "n must be a positive multiple of 64");
+  GemmShape g{};
+  g.tiles = mode == pg::kGemmSiluMul ? (n / 2) / 32 : n / pg::kGemmTileRows;
+  g.kblocks = k / pg::kGemmBK;
+  const int64_t total = static_cast<int64_t>(g.tiles) * g.kblocks;
+  const int64_t slots = static_cast<int64_t>(std::max(num_sms, 1)) * gemm_ctas_per_sm(gemm_nt(batch));
+  int64_t grid_n = std::min<int64_t>(total, grid > 0 ? grid : slots);
+  // At most 16 CTAs may share a tile (the finishing CTA's slot table).
+  while (grid_n > 1 && (g.kblocks + total / grid_n - 1) / (total / grid_n) + 1 > pg::kGemmMaxContrib)
+    --grid_n;
+  PG_REQUIRE(total * grid_n < (int64_t(1) << 31), "GEMM too large for the stream-K indexing");
+  g.total = static_cast<int32_t>(total);
+  g.grid = static_cast<int32_t>(grid_n);
+  const int64_t lmax = (total + grid_n - 1) / grid_n;
+  g.max_seg = static_cast<int32_t>((g.kblocks - 1 + lmax + g.kblocks - 1) / g.kblocks);
+  *out = g;
+  return PG_OK;
+}
+
+int32_t ensure_gemm_smem() {
+  static std::mutex mu;
+  static bool done[64] = {false};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return fail(PG_ERR_CUDA, "cudaGetDevice failed");
+  std::lock_guard<std::mutex> lock(mu);
+  if (!done[dev]) {
+    int32_t rc = cuda_check(cudaFuncSetAttribute(pg::pg_skinny_gemm_kernel<1>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 pg::gemm_smem_bytes(1)),
+                            "cudaFuncSetAttribute(gemm 1)");
+    if (rc == PG_OK)
+      rc = cuda_check(cudaFuncSetAttribute(pg::pg_skinny_gemm_kernel<2>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           pg::gemm_smem_bytes(2)),
+                      "cudaFuncSetAttribute(gemm 2)");
+    if (rc == PG_OK)
+      rc = cuda_check(cudaFuncSetAttribute(pg::pg_skinny_gemm_kernel<4>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           pg::gemm_smem_bytes(4)),
+                      "cudaFuncSetAttribute(gemm 4)");
+    if (rc != PG_OK) return rc;
+    done[dev] = true;
+  }
+  return PG_OK;
+}
+
+int current_sms() {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess)
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms;
+}
+
+}  // namespace
+
+int32_t pg_skinny_gemm_workspace(int32_t n, int32_t k, int32_t batch, int32_t mode, int32_t grid,
+                                 int32_t num_sms, int64_t* partial_floats, int32_t* counters) {
+  GemmShape g;
+  int32_t rc = gemm_shape(n, k, batch, mode, grid, num_sms > 0 ? num_sms : current_sms(), &g);
+  if (rc != PG_OK) return rc;
+  if (partial_floats != nullptr)
+    *partial_floats = static_cast<int64_t>(g.grid) * g.max_seg * pg::kGemmTileRows * 8 * gemm_nt(batch);
+  if (counters != nullptr) *counters = g.tiles;
+  return PG_OK;
+}
+
+int32_t pg_skinny_gemm(const pg_gemm_args* a, void* stream) {
+  PG_REQUIRE(a != nullptr, "null arguments");
+  GemmShape g;
+  int32_t rc = gemm_shape(a->n, a->k, a->batch, a->mode, a->grid, current_sms(), &g);
+  if (rc != PG_OK) return rc;
+  const int nt = gemm_nt(a->batch);
+  PG_REQUIRE(a->w != nullptr && a->x != nullptr, "w and x are required");
+  PG_REQUIRE(aligned(a->w, 16) && aligned(a->x, 16), "w and x must be 16-byte aligned");
+  PG_REQUIRE(a->ldw >= a->k && a->ldw % 8 == 0 && a->ldx >= a->k && a->ldx % 8 == 0,
+             "row strides must cover k and be multiples of 8 elements");
+  if (a->mode == pg::kGemmResidual)
+    PG_REQUIRE(a->residual != nullptr && a->ldr >= a->n, "residual mode needs residual [batch, n]");
+  else
+    PG_REQUIRE(a->y != nullptr && a->ldy >= (a->mode == pg::kGemmSiluMul ? a->n / 2 : a->n),
+               "y [batch, n] (silu_mul: [batch, n/2]) is required");
+  const int64_t need = static_cast<int64_t>(g.grid) * g.max_seg * pg::kGemmTileRows * 8 * nt;
+  PG_REQUIRE(a->partials != nullptr && a->partial_floats >= need && a->counters != nullptr &&
+                 a->num_counters >= g.tiles,
+             "split-K workspace too small (query pg_skinny_gemm_workspace)");
+  rc = ensure_gemm_smem();
+  if (rc != PG_OK) return rc;
+  CUtensorMap tw, tx;
+  rc = make_2d_map(&tw, a->w, a->k, a->n, a->ldw, 32);
+  if (rc != PG_OK) return rc;
+  rc = make_2d_map(&tx, a->x, a->k, a->batch, a->ldx, 8 * nt);
+  if (rc != PG_OK) return rc;
+  pg::GemmParams p{};
+  p.n = a->n;
+  p.k = a->k;
+  p.batch = a->batch;
+  p.mode = a->mode;
+  p.tiles = g.tiles;
+  p.kblocks = g.kblocks;
+  p.total = g.total;
+  p.grid = g.grid;
+  p.max_seg = g.max_seg;
+  p.half_rows = a->n / 2;
+  p.y = static_cast<__half*>(a->y);
+  p.ldy = a->ldy;
+  p.residual = static_cast<__half*>(a->residual);
+  p.ldr = a->ldr;
+  p.partials = a->partials;
+  p.counters = a->counters;
+  p.error_flag = device_error_ptr();
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(g.grid);
+  cfg.blockDim = dim3(pg::kGemmWarps * 32);
+  cfg.dynamicSmemBytes = pg::gemm_smem_bytes(nt);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = a->pdl ? 1 : 0;
+  cudaError_t e;
+  if (nt == 1)
+    e = cudaLaunchKernelEx(&cfg, pg::pg_skinny_gemm_kernel<1>, tw, tx, p);
+  else if (nt == 2)
+    e = cudaLaunchKernelEx(&cfg, pg::pg_skinny_gemm_kernel<2>, tw, tx, p);
+  else
+    e = cudaLaunchKernelEx(&cfg, pg::pg_skinny_gemm_kernel<4>, tw, tx, p);
+  return cuda_check(e, "skinny gemm launch");
 }
 
 // --------------------------------------------- allocation-free decode

@@ -1,0 +1,321 @@
+// Weight-streaming skinny GEMM for the decoder's projections:
+//   Y[b, n] = sum_k X[b, k] * W[n, k]     (b < batch <= 32, W FP16 [n, k])
+// with the decoder layer's element-wise step fused into the epilogue.
+//
+// A decode step reads every weight once and multiplies it by 1..32 token
+// rows, so the kernel is an HBM stream of W.  Work is split "stream-K":
+// the (output tile, 64-wide k-block) pairs are laid end to end and CTA c
+// of G takes blocks [c*T/G, (c+1)*T/G), so every CTA streams the same number
+// of bytes whatever the shape.  A CTA stages its blocks through a 6-deep
+// shared-memory ring with tiled TMA (W box 32 rows x 128 B, 128-byte
+// swizzle; X box 8*NT rows), and its 4 warps run mma.sync m16n8k16 with
+// FP32 accumulators (warp w owns W rows 16w..16w+15 of the 64-row tile,
+// the batch rows are the n-tiles).  A tile split between CTAs is finished
+// by the last of them to arrive (an atomic counter per tile): it sums the
+// partial tiles in CTA order (deterministic) and applies the epilogue.
+//
+// Epilogues (the decoder layer body, transformers Mistral semantics):
+//   store     Y = f16(acc)
+//   residual  R = f16(R + f16(acc))                   (o_proj, down_proj)
+//   silu_mul  Y = f16(f16(silu(f16(acc_gate))) * f16(acc_up)); W rows
+//             [0, n/2) are gate rows and [n/2, n) up rows, a 64-row tile
+//             holds 32 gate rows and the matching 32 up rows.
+//
+// Programmatic dependent launch: a CTA requests its first weight stages
+// before griddepcontrol.wait (weights are never written by a predecessor),
+// and the activations only after it.
+#pragma once
+
+#include "pg_common.cuh"
+
+namespace pg {
+
+constexpr int kGemmTileRows = 64;  // W rows per output tile
+constexpr int kGemmBK = 64;        // k per stage: 128-byte rows
+constexpr int kGemmStages = 6;
+constexpr int kGemmWarps = 4;
+
+enum GemmMode { kGemmStore = 0, kGemmResidual = 1, kGemmSiluMul = 2 };
+
+struct GemmParams {
+  int32_t n, k, batch, mode;
+  int32_t tiles;     // output tiles (mode silu_mul: (n/2)/32, else n/64)
+  int32_t kblocks;   // k / 64
+  int32_t total;     // tiles * kblocks
+  int32_t grid;      // CTAs (<= total; total * grid < 2^31)
+  int32_t max_seg;   // tiles one CTA's range can touch
+  int32_t half_rows; // mode silu_mul: n / 2 (row offset of the up rows)
+  __half* y;
+  int64_t ldy;
+  __half* residual;
+  int64_t ldr;
+  float* partials;   // [grid * max_seg][64][8*NT]
+  int32_t* counters; // [tiles], zero between launches
+  int* error_flag;
+};
+
+__host__ __device__ constexpr int gemm_stage_bytes(int nt) {
+  return kGemmTileRows * 128 + 8 * nt * 128;
+}
+__host__ __device__ constexpr int gemm_smem_bytes(int nt) {
+  return kGemmStages * gemm_stage_bytes(nt) + kGemmStages * 8 + 1024;
+}
+
+__device__ __forceinline__ void ldsm_x4(const uint8_t* addr, uint32_t& r0, uint32_t& r1,
+                                        uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(smem_addr(addr)));
+}
+__device__ __forceinline__ void ldsm_x2(const uint8_t* addr, uint32_t& r0, uint32_t& r1) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];"
+               : "=r"(r0), "=r"(r1)
+               : "r"(smem_addr(addr)));
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3}], [%4];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_addr(bar))
+      : "memory");
+}
+
+constexpr int kGemmMaxContrib = 16;  // CTAs sharing one tile (host-checked)
+
+// The CTAs whose k-block ranges intersect tile t (ranges are
+// [floor(c*T/G), floor((c+1)*T/G))).
+__device__ __forceinline__ void gemm_contributors(const GemmParams& p, int t, int& c0, int& c1) {
+  c0 = ((t * p.kblocks + 1) * p.grid - 1) / p.total;
+  c1 = (((t + 1) * p.kblocks) * p.grid - 1) / p.total;
+}
+
+// Request the weight rows of k-block kb of tile `tile` (and expect the
+// whole stage, activations included, on the stage's barrier).
+template <int NT>
+__device__ __forceinline__ void gemm_issue_w(const CUtensorMap* tw, const GemmParams& p,
+                                             uint8_t* stage, uint64_t* bar, int tile, int kb) {
+  mbar_arrive_expect_tx(bar, gemm_stage_bytes(NT));
+  int r0, r1;
+  if (p.mode == kGemmSiluMul) {
+    r0 = tile * 32;
+    r1 = p.half_rows + tile * 32;
+  } else {
+    r0 = tile * kGemmTileRows;
+    r1 = r0 + 32;
+  }
+  tma_load_2d(stage, tw, kb * kGemmBK, r0, bar);
+  tma_load_2d(stage + 4096, tw, kb * kGemmBK, r1, bar);
+}
+
+template <int NT>
+__device__ __forceinline__ void gemm_issue_x(const CUtensorMap* tx, uint8_t* stage, uint64_t* bar,
+                                             int kb) {
+  tma_load_2d(stage + kGemmTileRows * 128, tx, kb * kGemmBK, 0, bar);
+}
+
+// Epilogue of one finished tile.  `src` gives the FP32 value of (tile row,
+// batch row): either this CTA's own accumulators (staged in shared memory)
+// or the ordered sum of the contributors' partial tiles.
+template <int NT, typename Src>
+__device__ __forceinline__ void gemm_epilogue(const GemmParams& p, int tile, Src src) {
+  const int rows = p.mode == kGemmSiluMul ? 32 : kGemmTileRows;
+  const int count = rows * p.batch;
+  for (int e = threadIdx.x; e < count; e += blockDim.x) {
+    const int b = e / rows, j = e % rows;
+    if (p.mode == kGemmStore) {
+      p.y[b * p.ldy + tile * kGemmTileRows + j] = __float2half_rn(src(j, b));
+    } else if (p.mode == kGemmResidual) {
+      __half* r = p.residual + b * p.ldr + tile * kGemmTileRows + j;
+      *r = __hadd(*r, __float2half_rn(src(j, b)));
+    } else {
+      const float g = __half2float(__float2half_rn(src(j, b)));
+      const __half u = __float2half_rn(src(j + 32, b));
+      const __half s = __float2half_rn(g / (1.f + expf(-g)));
+      p.y[b * p.ldy + tile * 32 + j] = __hmul(s, u);
+    }
+  }
+}
+
+// Finish this CTA's segment [kb0, kb1) of tile `tile`: the whole tile goes
+// straight to the epilogue; a part is written to the CTA's partial slot and
+// the last contributor to arrive sums the tile's slots in CTA order.
+template <int NT>
+__device__ __forceinline__ void gemm_flush(const GemmParams& p, const float (&acc)[NT][4], int tile,
+                                           int kb0, int kb1, int seg, float* s_tile, int* s_last,
+                                           int* s_seg) {
+  constexpr int XR = 8 * NT;
+  constexpr int ES = XR + 1;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  if (kb0 == 0 && kb1 == p.kblocks) {
+#pragma unroll
+    for (int i = 0; i < NT; ++i) {
+      const int row = 16 * warp + g, col = 8 * i + 2 * t;
+      s_tile[row * ES + col] = acc[i][0];
+      s_tile[row * ES + col + 1] = acc[i][1];
+      s_tile[(row + 8) * ES + col] = acc[i][2];
+      s_tile[(row + 8) * ES + col + 1] = acc[i][3];
+    }
+    __syncthreads();
+    gemm_epilogue<NT>(p, tile, [&](int j, int b) { return s_tile[j * ES + b]; });
+    __syncthreads();
+    return;
+  }
+  const int c = blockIdx.x;
+  float* slot = p.partials + (static_cast<int64_t>(c) * p.max_seg + seg) * (kGemmTileRows * XR);
+#pragma unroll
+  for (int i = 0; i < NT; ++i) {
+    const int row = 16 * warp + g, col = 8 * i + 2 * t;
+    *reinterpret_cast<float2*>(slot + row * XR + col) = make_float2(acc[i][0], acc[i][1]);
+    *reinterpret_cast<float2*>(slot + (row + 8) * XR + col) = make_float2(acc[i][2], acc[i][3]);
+  }
+  __threadfence();
+  __syncthreads();
+  int first, last;
+  gemm_contributors(p, tile, first, last);
+  if (threadIdx.x == 0) {
+    const int prev = atomicAdd(p.counters + tile, 1);
+    const int done = prev == last - first;
+    if (done) p.counters[tile] = 0;  // re-armed for the next launch
+    *s_last = done;
+  }
+  // Slot of tile `tile` in each contributor's partials (its segment index).
+  if (threadIdx.x <= last - first) {
+    const int cc = first + threadIdx.x;
+    s_seg[threadIdx.x] = (cc * p.max_seg + tile - (cc * p.total / p.grid) / p.kblocks);
+  }
+  __syncthreads();
+  if (*s_last) {
+    __threadfence();
+    const int n = last - first + 1;
+    gemm_epilogue<NT>(p, tile, [&](int j, int b) {
+      float v = 0.f;
+      for (int q = 0; q < n; ++q)
+        v += __ldcg(p.partials + static_cast<int64_t>(s_seg[q]) * (kGemmTileRows * XR) + j * XR + b);
+      return v;
+    });
+  }
+  __syncthreads();
+}
+
+template <int NT>
+__global__ void __launch_bounds__(kGemmWarps * 32)
+    pg_skinny_gemm_kernel(const __grid_constant__ CUtensorMap tm_w,
+                          const __grid_constant__ CUtensorMap tm_x,
+                          const __grid_constant__ GemmParams p) {
+  constexpr int XR = 8 * NT;            // padded batch rows
+  constexpr int SB = gemm_stage_bytes(NT);
+  constexpr int ES = XR + 1;            // padded row of the epilogue tile
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kGemmStages * SB);
+  __shared__ int s_last;
+  __shared__ int s_seg[kGemmMaxContrib];
+  __shared__ float s_tile[kGemmTileRows * ES];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c = blockIdx.x;
+  const int b0 = c * p.total / p.grid, b1 = (c + 1) * p.total / p.grid;
+  const int nblk = b1 - b0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kGemmStages; ++s) mbar_init(full + s, 1);
+    fence_barrier_init();
+    prefetch_tensormap(&tm_w);
+    prefetch_tensormap(&tm_x);
+  }
+  __syncthreads();
+  // Issue cursor (tile, k-block) of the next block to request.
+  int itile = b0 / p.kblocks, ikb = b0 % p.kblocks;
+  const int pro = nblk < kGemmStages ? nblk : kGemmStages;
+  if (threadIdx.x == 0) {
+    int t = itile, k = ikb;
+    for (int i = 0; i < pro; ++i) {
+      gemm_issue_w<NT>(&tm_w, p, smem + i * SB, full + i, t, k);
+      if (++k == p.kblocks) k = 0, ++t;
+    }
+  }
+  pdl_launch_dependents();
+  pdl_wait_primary();
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < pro; ++i) {
+      gemm_issue_x<NT>(&tm_x, smem + i * SB, full + i, ikb);
+      if (++ikb == p.kblocks) ikb = 0, ++itile;
+    }
+  }
+
+  // ldmatrix lane addresses (128-byte swizzle: chunk ^ (row & 7)).
+  const int mat = lane >> 3, rr = lane & 7;
+  const int arow = 16 * warp + rr + 8 * (mat & 1);
+  const int achunk = mat >> 1;
+  float acc[NT][4];
+#pragma unroll
+  for (int i = 0; i < NT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+
+  // Consumer cursor.
+  int cur = b0 / p.kblocks, ckb = b0 % p.kblocks;
+  int seg = 0;
+  int seg_kb0 = ckb;
+  bool ok = true;
+
+  int i = 0;
+  for (; i < nblk; ++i) {
+    if (ckb == p.kblocks) {
+      gemm_flush<NT>(p, acc, cur, seg_kb0, p.kblocks, seg, s_tile, &s_last, s_seg);
+#pragma unroll
+      for (int q = 0; q < NT; ++q) acc[q][0] = acc[q][1] = acc[q][2] = acc[q][3] = 0.f;
+      ++cur;
+      ckb = 0;
+      ++seg;
+      seg_kb0 = 0;
+    }
+    const int st = i % kGemmStages;
+    const bool waited = mbar_wait_bounded(full + st, static_cast<uint32_t>(i / kGemmStages) & 1u);
+    if (!__syncthreads_and(waited)) {
+      ok = false;
+      break;
+    }
+    const uint8_t* ws = smem + st * SB;
+    const uint8_t* xs = ws + kGemmTileRows * 128;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint32_t a[4];
+      ldsm_x4(ws + arow * 128 + (((2 * j + achunk) ^ rr) << 4), a[0], a[1], a[2], a[3]);
+#pragma unroll
+      for (int q = 0; q < NT; q += 2) {
+        if (q + 1 < NT) {
+          // Matrices: n-tile q k0-7, k8-15; n-tile q+1 k0-7, k8-15.
+          const int xrow = 8 * (q + (mat >> 1)) + rr;
+          uint32_t x0, x1, x2, x3;
+          ldsm_x4(xs + xrow * 128 + (((2 * j + (mat & 1)) ^ rr) << 4), x0, x1, x2, x3);
+          mma_16816(acc[q], a, x0, x1);
+          mma_16816(acc[q + 1], a, x2, x3);
+        } else {
+          const int xrow = 8 * q + rr;
+          uint32_t x0, x1;
+          ldsm_x2(xs + xrow * 128 + (((2 * j + (mat & 1)) ^ rr) << 4), x0, x1);
+          mma_16816(acc[q], a, x0, x1);
+        }
+      }
+    }
+    ++ckb;
+    __syncthreads();  // every warp is done with stage st
+    if (threadIdx.x == 0 && i + kGemmStages < nblk) {
+      gemm_issue_w<NT>(&tm_w, p, smem + st * SB, full + st, itile, ikb);
+      gemm_issue_x<NT>(&tm_x, smem + st * SB, full + st, ikb);
+      if (++ikb == p.kblocks) ikb = 0, ++itile;
+    }
+  }
+  if (!ok) {
+    if (threadIdx.x == 0) record_error(p.error_flag, kDevWaitTimeout);
+    // Drain this CTA's copies still in flight before exiting.
+    const int end = i + kGemmStages < nblk ? i + kGemmStages : nblk;
+    for (int v = i; v < end; ++v)
+      mbar_wait_bounded(full + v % kGemmStages, static_cast<uint32_t>(v / kGemmStages) & 1u);
+    return;
+  }
+  gemm_flush<NT>(p, acc, cur, seg_kb0, ckb, seg, s_tile, &s_last, s_seg);
+}
+
+}  // namespace pg

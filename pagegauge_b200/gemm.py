@@ -1,0 +1,73 @@
+"""Weight-streaming projections of the decoder (the C ABI's
+``pg_skinny_gemm``): ``y = x @ w.T`` for up to 32 token rows with the
+decoder layer's element-wise step fused into the epilogue.
+
+The reference runs these projections through cuBLAS (``F.linear`` in the
+decoder layer, scripts/benchmark_page_gauge_transformer.py:2754-2804).
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+STORE, RESIDUAL, SILU_MUL = 0, 1, 2
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+class SkinnyGemm:
+    """Launcher with caller-owned split-K scratch (partial tiles + per-tile
+    arrival counters), sized for the largest shape it is asked to run."""
+
+    def __init__(self, device, partial_floats: int = 1 << 20, counters: int = 1024):
+        self.device = torch.device(device)
+        self.sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+        self.partials = torch.empty(partial_floats, dtype=torch.float32, device=self.device)
+        self.counters = torch.zeros(counters, dtype=torch.int32, device=self.device)
+
+    def reserve(self, n: int, k: int, batch: int, mode: int = STORE) -> None:
+        """Grow the scratch for a shape (host-side; outside graph capture)."""
+        floats, tiles = ctypes.c_int64(0), ctypes.c_int32(0)
+        _lib.check(_lib.load().pg_skinny_gemm_workspace(n, k, batch, mode, 0, self.sms,
+                                                        ctypes.byref(floats), ctypes.byref(tiles)))
+        if floats.value > self.partials.numel():
+            self.partials = torch.empty(floats.value, dtype=torch.float32, device=self.device)
+        if tiles.value > self.counters.numel():
+            self.counters = torch.zeros(tiles.value, dtype=torch.int32, device=self.device)
+
+    def __call__(self, x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None,
+                 mode: int = STORE, residual: torch.Tensor | None = None, pdl: bool = True,
+                 grid: int = 0) -> torch.Tensor | None:
+        if x.dtype != torch.float16 or w.dtype != torch.float16 or x.dim() != 2 or w.dim() != 2:
+            raise ValueError("x [batch, k] and w [n, k] must be 2-D float16")
+        if x.stride(1) != 1 or w.stride(1) != 1:
+            raise ValueError("x and w need a contiguous last dimension")
+        batch, k = x.shape
+        n = w.shape[0]
+        if w.shape[1] != k:
+            raise ValueError("x and w disagree on k")
+        a = _lib.PgGemmArgs()
+        a.w, a.ldw = w.data_ptr(), w.stride(0)
+        a.x, a.ldx = x.data_ptr(), x.stride(0)
+        if mode == RESIDUAL:
+            if residual is None or residual.shape != (batch, n) or residual.stride(1) != 1:
+                raise ValueError("residual mode needs residual [batch, n]")
+            a.residual, a.ldr = residual.data_ptr(), residual.stride(0)
+        else:
+            cols = n // 2 if mode == SILU_MUL else n
+            if out is None:
+                out = torch.empty(batch, cols, dtype=torch.float16, device=x.device)
+            if out.shape != (batch, cols) or out.stride(1) != 1:
+                raise ValueError(f"out must be [batch, {cols}]")
+            a.y, a.ldy = out.data_ptr(), out.stride(0)
+        a.n, a.k, a.batch, a.mode, a.grid, a.pdl = n, k, batch, mode, grid, int(pdl)
+        a.partials, a.partial_floats = self.partials.data_ptr(), self.partials.numel()
+        a.counters, a.num_counters = self.counters.data_ptr(), self.counters.numel()
+        _lib.check(_lib.load().pg_skinny_gemm(ctypes.byref(a), _stream()))
+        return out if mode != RESIDUAL else residual
