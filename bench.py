@@ -61,6 +61,8 @@ def parse_args():
     p.add_argument("--decoder-batch", type=int, nargs="*", default=[32, 1],
                    help="decoder workload: batch sizes (the first is the headline)")
     p.add_argument("--decoder-steps", type=int, default=16)
+    p.add_argument("--decoder-gemm", choices=("auto", "pg", "cublas"), default="auto",
+                   help="decoder projections: weight-streaming kernels (pg), cuBLAS, or by batch")
     p.add_argument("--no-cpu-baseline", action="store_true")
     return p.parse_args()
 
@@ -650,7 +652,7 @@ def decoder_bytes(dec, batch: int) -> int:
 
 
 def measure_decoder(dist: Dist, batch: int, context: int = 16384, steps: int = 16,
-                    seed: int = 20261004) -> dict:
+                    seed: int = 20261004, gemm: str = "auto") -> dict:
     """Mistral-7B-shaped random-init FP16 decoder,
     prompt of ``context`` random tokens prefilled into PageGauge caches, one
     eager warm-up decode step, then ``steps`` greedy decode steps (CUDA
@@ -664,7 +666,8 @@ def measure_decoder(dist: Dist, batch: int, context: int = 16384, steps: int = 1
     cfg = DecoderConfig.mistral_7b_shaped()
     t0 = time.perf_counter()
     w = random_decoder_weights(cfg, seed, device="cuda", tp=TensorParallel.of(cfg, rank, world))
-    dec = PageGaugeDecoder(w, batch, max_context=context + 4 * steps + 32, process_group=pg)
+    dec = PageGaugeDecoder(w, batch, max_context=context + 4 * steps + 32, process_group=pg,
+                           gemm=gemm)
     prompt = torch.randint(0, cfg.vocab, (batch, context),
                            generator=torch.Generator().manual_seed(seed + batch))
     dec.prefill(prompt.cuda())
@@ -706,7 +709,7 @@ def measure_decoder(dist: Dist, batch: int, context: int = 16384, steps: int = 1
         "e2e_tokens_per_s": round(batch / e2e_s, 2),
         "hbm_bytes_per_step_per_rank": nbytes, "achieved_gbs_per_rank": round(achieved, 1),
         "roofline_frac": round(achieved / peak, 4), "prefill_s": round(prefill_s, 2),
-        "replans_in_timing": 0, "params": cfg.parameter_count(),
+        "replans_in_timing": 0, "params": cfg.parameter_count(), "gemm": dec.gemm_impl,
     }
     del dec, w
     torch.cuda.empty_cache()
@@ -719,9 +722,10 @@ def run_decoder(args, dist: Dist, local: int) -> None:
     batches = args.decoder_batch or [32]
     results = {}
     with clocks:
-        results[batches[0]] = measure_decoder(dist, batches[0], steps=args.decoder_steps)
+        results[batches[0]] = measure_decoder(dist, batches[0], steps=args.decoder_steps,
+                                              gemm=args.decoder_gemm)
     for b in batches[1:]:
-        results[b] = measure_decoder(dist, b, steps=args.decoder_steps)
+        results[b] = measure_decoder(dist, b, steps=args.decoder_steps, gemm=args.decoder_gemm)
     b32 = results[batches[0]]
     peak, peak_src = peak_hbm()
     if rank == 0:

@@ -269,6 +269,9 @@ int32_t pg_quantize_pages(const void* key, const void* value,
  *   mode 1  residual = f16(residual + f16(acc))         (o_proj, down_proj)
  *   mode 2  y[b, j] = f16(f16(silu(f16(acc[b, j]))) * f16(acc[b, n/2 + j]))
  *           for the packed gate|up projection (rows [0, n/2) gate, rest up).
+ * w is the weight in the packed layout pg_pack_weight writes (one 8 KB
+ * block per 64 rows x 64 k, 128-byte swizzled; ldw is ignored), so each
+ * pipeline stage's weights are one contiguous bulk copy.
  * The reference runs these through cuBLAS (F.linear in
  * scripts/benchmark_page_gauge_transformer.py:2754-2804).  partials and
  * counters are caller-owned scratch sized by pg_skinny_gemm_workspace;
@@ -293,6 +296,12 @@ typedef struct pg_gemm_args {
   int32_t num_counters;
 } pg_gemm_args;
 
+/* Pack W [n, k] (row stride ld, FP16) for pg_skinny_gemm with the same
+ * mode (silu_mul pairs gate row j with up row n/2 + j in one tile); out
+ * holds n * k halves.                                                     */
+int32_t pg_pack_weight(const void* w, int64_t ld, int32_t n, int32_t k, int32_t mode, void* out,
+                       void* stream);
+
 int32_t pg_skinny_gemm_workspace(int32_t n, int32_t k, int32_t batch, int32_t mode,
                                  int32_t grid, int32_t num_sms, int64_t* partial_floats,
                                  int32_t* counters);
@@ -309,6 +318,13 @@ int32_t pg_add_rmsnorm(void* residual, const void* delta, const void* weight, vo
  * out as gate | up (the packed gate_up projection).                        */
 int32_t pg_silu_mul(const void* gate_up, void* out, int32_t rows, int32_t features,
                     int64_t in_stride, int64_t out_stride, void* stream);
+
+/* Greedy token of each row of FP16 logits [rows, cols] (row stride ld):
+ * out_idx[r] = index_offset + argmax (ties to the lowest index), out_val
+ * (optional) the maximum as FP32.  index_offset places a vocabulary slice
+ * of a tensor-parallel LM head in the full vocabulary.                    */
+int32_t pg_argmax_rows(const void* logits, int64_t ld, int32_t rows, int32_t cols,
+                       int64_t index_offset, float* out_val, int64_t* out_idx, void* stream);
 
 /* positions[r] += advance; last_page_len[r] = positions[r] % 16 + 1 (NULL
  * last_page_len: positions only).  Keeps a captured decode step's device

@@ -94,6 +94,8 @@ _SIGNATURES = {
                                ctypes.c_float, c_vp]),
     "pg_silu_mul": (c_i32, [c_vp, c_vp, c_i32, c_i32, c_i64, c_i64, c_vp]),
     "pg_step_positions": (c_i32, [c_vp, c_vp, c_i32, c_i32, c_vp]),
+    "pg_argmax_rows": (c_i32, [c_vp, c_i64, c_i32, c_i32, c_i64, c_vp, c_vp, c_vp]),
+    "pg_pack_weight": (c_i32, [c_vp, c_i64, c_i32, c_i32, c_i32, c_vp, c_vp]),
     "pg_skinny_gemm_workspace": (c_i32, [c_i32, c_i32, c_i32, c_i32, c_i32, c_i32,
                                          ctypes.POINTER(c_i64), c_i32p]),
     "pg_skinny_gemm": (c_i32, [ctypes.POINTER(PgGemmArgs), c_vp]),

@@ -207,8 +207,10 @@ __device__ __forceinline__ void rotate_query_heads(const AppendParams& p, int r,
 __global__ void __launch_bounds__(kAppendThreads)
     pg_rope_append_fp16_kernel(const __grid_constant__ AppendParams p) {
   // A dependent decode launch may start streaming completed INT8 pages now
-  // (it waits for this grid before reading anything written here).
+  // (it waits for this grid before reading anything written here); this
+  // grid waits for its own predecessor (which produced q, k, v).
   pdl_launch_dependents();
+  pdl_wait_primary();
   const int r = blockIdx.x / p.hkv;
   const int h = blockIdx.x % p.hkv;
   const int g = threadIdx.x >> 6, j = threadIdx.x & 63;
@@ -298,8 +300,10 @@ __global__ void __launch_bounds__(kAppendThreads)
   // A dependent decode launch may start streaming completed INT8 pages now:
   // the page this launch may close is still in the exact window, so the
   // decode reads it from the ring, and the decode waits for this grid
-  // before reading q or the ring.
+  // before reading q or the ring.  This grid waits for its own predecessor
+  // (which produced q, k, v) before reading anything.
   pdl_launch_dependents();
+  pdl_wait_primary();
   __shared__ __align__(16) uint32_t newest[2][kHeadDim / 2];
   const int r = blockIdx.x / p.hkv;
   const int h = blockIdx.x % p.hkv;

@@ -10,6 +10,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include "pagegauge_b200.h"
@@ -173,6 +174,26 @@ int32_t launch_decode(const pg::DecodeParams& p, const CUtensorMap& k8,
                     "decode kernel launch");
 }
 
+// Launch as a programmatic dependent of the previous kernel in the stream:
+// the grid may be scheduled while that kernel finishes (hiding the launch
+// latency); the kernel itself waits (griddepcontrol.wait) before touching
+// anything the predecessor writes.
+template <typename... KArgs, typename... Args>
+int32_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                   cudaStream_t stream, const char* what, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_check(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...), what);
+}
+
 // Resident CTAs of the decode kernel per SM at `warps` warps per CTA
 // (shared-memory bound: 228 KB per SM, 1 KB reserved per CTA; at most
 // 2048 threads and 64 K registers at up to 168 registers per thread).
@@ -262,9 +283,9 @@ static int32_t append_fp16_impl(const void* query, const void* key,
   p.hkv = kv_heads;
   p.exact_pages_per_request = ppr;
   p.error_flag = device_error_ptr();
-  pg::pg_rope_append_fp16_kernel<<<batch * kv_heads, pg::kAppendThreads, 0,
-                                   static_cast<cudaStream_t>(stream)>>>(p);
-  return cuda_check(cudaGetLastError(), "rope_append_fp16 launch");
+  return launch_pdl(pg::pg_rope_append_fp16_kernel, dim3(batch * kv_heads),
+                    dim3(pg::kAppendThreads), 0, static_cast<cudaStream_t>(stream),
+                    "rope_append_fp16 launch", p);
 }
 
 int32_t pg_rope_append_fp16(const void* query, const void* key,
@@ -380,9 +401,9 @@ static int32_t append_page_gauge_impl(
   p.exact_sink_pages = exact_sink_pages;
   p.code_pages_per_request = code_ppr;
   p.error_flag = device_error_ptr();
-  pg::pg_rope_append_page_gauge_kernel<<<batch * kv_heads, pg::kAppendThreads, 0,
-                                         static_cast<cudaStream_t>(stream)>>>(p);
-  return cuda_check(cudaGetLastError(), "rope_append_page_gauge launch");
+  return launch_pdl(pg::pg_rope_append_page_gauge_kernel, dim3(batch * kv_heads),
+                    dim3(pg::kAppendThreads), 0, static_cast<cudaStream_t>(stream),
+                    "rope_append_page_gauge launch", p);
 }
 
 int32_t pg_rope_append_page_gauge(
@@ -773,8 +794,8 @@ int32_t pg_add_rmsnorm(void* residual, const void* delta, const void* weight, vo
   p.out_stride = out_stride;
   p.hidden = hidden;
   p.eps = eps;
-  pg::pg_add_rmsnorm_kernel<<<rows, pg::kNormThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
-  return cuda_check(cudaGetLastError(), "add_rmsnorm launch");
+  return launch_pdl(pg::pg_add_rmsnorm_kernel, dim3(rows), dim3(pg::kNormThreads), 0,
+                    static_cast<cudaStream_t>(stream), "add_rmsnorm launch", p);
 }
 
 int32_t pg_silu_mul(const void* gate_up, void* out, int32_t rows, int32_t features,
@@ -793,16 +814,26 @@ int32_t pg_silu_mul(const void* gate_up, void* out, int32_t rows, int32_t featur
   p.features = features;
   const int64_t chunks = static_cast<int64_t>(rows) * (features / 8);
   const int blocks = static_cast<int>(std::min<int64_t>((chunks + 255) / 256, 148 * 8));
-  pg::pg_silu_mul_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
-  return cuda_check(cudaGetLastError(), "silu_mul launch");
+  return launch_pdl(pg::pg_silu_mul_kernel, dim3(blocks), dim3(256), 0,
+                    static_cast<cudaStream_t>(stream), "silu_mul launch", p);
 }
 
 int32_t pg_step_positions(int32_t* positions, int32_t* last_page_len, int32_t batch,
                           int32_t advance, void* stream) {
   PG_REQUIRE(positions != nullptr && batch > 0, "positions must be a device int32 [B] tensor");
-  pg::pg_step_positions_kernel<<<(batch + 127) / 128, 128, 0, static_cast<cudaStream_t>(stream)>>>(
-      positions, last_page_len, batch, advance);
-  return cuda_check(cudaGetLastError(), "step_positions launch");
+  return launch_pdl(pg::pg_step_positions_kernel, dim3((batch + 127) / 128), dim3(128), 0,
+                    static_cast<cudaStream_t>(stream), "step_positions launch", positions,
+                    last_page_len, batch, advance);
+}
+
+int32_t pg_argmax_rows(const void* logits, int64_t ld, int32_t rows, int32_t cols,
+                       int64_t index_offset, float* out_val, int64_t* out_idx, void* stream) {
+  PG_REQUIRE(rows > 0 && cols > 0 && cols % 8 == 0, "rows must be positive and cols a positive multiple of 8");
+  PG_REQUIRE(ld % 8 == 0 && ld >= cols && aligned(logits, 16), "logit rows must be 16-byte aligned");
+  PG_REQUIRE(out_idx != nullptr, "out_idx is required");
+  return launch_pdl(pg::pg_argmax_rows_kernel, dim3(rows), dim3(pg::kArgmaxThreads), 0,
+                    static_cast<cudaStream_t>(stream), "argmax launch",
+                    static_cast<const __half*>(logits), ld, cols, index_offset, out_val, out_idx);
 }
 
 // ------------------------------------------------------- skinny GEMM
@@ -911,6 +942,20 @@ int32_t pg_skinny_gemm_workspace(int32_t n, int32_t k, int32_t batch, int32_t mo
   return PG_OK;
 }
 
+int32_t pg_pack_weight(const void* w, int64_t ld, int32_t n, int32_t k, int32_t mode, void* out,
+                       void* stream) {
+  PG_REQUIRE(k > 0 && k % pg::kGemmBK == 0 && n > 0 && n % 64 == 0,
+             "n and k must be positive multiples of 64");
+  PG_REQUIRE(mode >= 0 && mode <= 2, "mode must be 0, 1 or 2");
+  PG_REQUIRE(ld >= k && ld % 8 == 0 && aligned(w, 16) && aligned(out, 16),
+             "w rows must be 16-byte aligned and cover k");
+  const int64_t chunks = static_cast<int64_t>(n) * (k / 8);
+  const int blocks = static_cast<int>(std::min<int64_t>((chunks + 255) / 256, 148 * 16));
+  pg::pg_pack_weight_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __half*>(w), ld, n, k, mode, static_cast<__half*>(out));
+  return cuda_check(cudaGetLastError(), "pack_weight launch");
+}
+
 int32_t pg_skinny_gemm(const pg_gemm_args* a, void* stream) {
   PG_REQUIRE(a != nullptr, "null arguments");
   GemmShape g;
@@ -919,8 +964,8 @@ int32_t pg_skinny_gemm(const pg_gemm_args* a, void* stream) {
   const int nt = gemm_nt(a->batch);
   PG_REQUIRE(a->w != nullptr && a->x != nullptr, "w and x are required");
   PG_REQUIRE(aligned(a->w, 16) && aligned(a->x, 16), "w and x must be 16-byte aligned");
-  PG_REQUIRE(a->ldw >= a->k && a->ldw % 8 == 0 && a->ldx >= a->k && a->ldx % 8 == 0,
-             "row strides must cover k and be multiples of 8 elements");
+  PG_REQUIRE(a->ldx >= a->k && a->ldx % 8 == 0,
+             "the x row stride must cover k and be a multiple of 8 elements");
   if (a->mode == pg::kGemmResidual)
     PG_REQUIRE(a->residual != nullptr && a->ldr >= a->n, "residual mode needs residual [batch, n]");
   else
@@ -932,9 +977,7 @@ int32_t pg_skinny_gemm(const pg_gemm_args* a, void* stream) {
              "split-K workspace too small (query pg_skinny_gemm_workspace)");
   rc = ensure_gemm_smem();
   if (rc != PG_OK) return rc;
-  CUtensorMap tw, tx;
-  rc = make_2d_map(&tw, a->w, a->k, a->n, a->ldw, 32);
-  if (rc != PG_OK) return rc;
+  CUtensorMap tx;
   rc = make_2d_map(&tx, a->x, a->k, a->batch, a->ldx, 8 * nt);
   if (rc != PG_OK) return rc;
   pg::GemmParams p{};
@@ -967,11 +1010,14 @@ int32_t pg_skinny_gemm(const pg_gemm_args* a, void* stream) {
   cfg.numAttrs = a->pdl ? 1 : 0;
   cudaError_t e;
   if (nt == 1)
-    e = cudaLaunchKernelEx(&cfg, pg::pg_skinny_gemm_kernel<1>, tw, tx, p);
+    e = cudaLaunchKernelEx(&cfg, pg::pg_skinny_gemm_kernel<1>,
+                           static_cast<const __half*>(a->w), tx, p);
   else if (nt == 2)
-    e = cudaLaunchKernelEx(&cfg, pg::pg_skinny_gemm_kernel<2>, tw, tx, p);
+    e = cudaLaunchKernelEx(&cfg, pg::pg_skinny_gemm_kernel<2>,
+                           static_cast<const __half*>(a->w), tx, p);
   else
-    e = cudaLaunchKernelEx(&cfg, pg::pg_skinny_gemm_kernel<4>, tw, tx, p);
+    e = cudaLaunchKernelEx(&cfg, pg::pg_skinny_gemm_kernel<4>,
+                           static_cast<const __half*>(a->w), tx, p);
   return cuda_check(e, "skinny gemm launch");
 }
 

@@ -29,6 +29,8 @@ struct NormParams {
 __global__ void __launch_bounds__(kNormThreads)
     pg_add_rmsnorm_kernel(const __grid_constant__ NormParams p) {
   __shared__ float part[kNormThreads / 32];
+  pdl_launch_dependents();
+  pdl_wait_primary();
   const int row = blockIdx.x;
   __half* res = p.residual + row * p.residual_stride;
   const __half* del = p.delta ? p.delta + row * p.delta_stride : nullptr;
@@ -98,6 +100,8 @@ struct SiluMulParams {
 
 __global__ void __launch_bounds__(256)
     pg_silu_mul_kernel(const __grid_constant__ SiluMulParams p) {
+  pdl_launch_dependents();
+  pdl_wait_primary();
   const int chunks = p.features / 8;
   const int64_t total = static_cast<int64_t>(p.rows) * chunks;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
@@ -125,11 +129,66 @@ __global__ void __launch_bounds__(256)
 // positions[r] += advance; last_len[r] = positions[r] % 16 + 1.
 __global__ void pg_step_positions_kernel(int32_t* positions, int32_t* last_len, int32_t batch,
                                          int32_t advance) {
+  pdl_launch_dependents();
+  pdl_wait_primary();
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= batch) return;
   const int32_t pos = positions[r] + advance;
   positions[r] = pos;
   if (last_len != nullptr) last_len[r] = pos % kPage + 1;
+}
+
+// Greedy token per row: the largest logit of a row of FP16 logits and its
+// index (ties to the lowest index), one CTA of 1024 threads per row.
+constexpr int kArgmaxThreads = 1024;
+
+__global__ void __launch_bounds__(kArgmaxThreads)
+    pg_argmax_rows_kernel(const __half* logits, int64_t ld, int32_t cols, int64_t index_offset,
+                          float* out_val, int64_t* out_idx) {
+  __shared__ float sv[kArgmaxThreads / 32];
+  __shared__ int si[kArgmaxThreads / 32];
+  pdl_launch_dependents();
+  pdl_wait_primary();
+  const __half* row = logits + blockIdx.x * ld;
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int c = threadIdx.x * 8; c < cols; c += kArgmaxThreads * 8) {
+    const uint4 v = *reinterpret_cast<const uint4*>(row + c);
+    const __half* h = reinterpret_cast<const __half*>(&v);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float f = __half2float(h[e]);
+      if (f > best) {  // columns grow within a thread: the first maximum stays
+        best = f;
+        bi = c + e;
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > best || (ov == best && oi < bi)) {
+      best = ov;
+      bi = oi;
+    }
+  }
+  if ((threadIdx.x & 31) == 0) {
+    sv[threadIdx.x >> 5] = best;
+    si[threadIdx.x >> 5] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < kArgmaxThreads / 32; ++w)
+      if (sv[w] > best || (sv[w] == best && si[w] < bi)) {
+        best = sv[w];
+        bi = si[w];
+      }
+    // A row of NaN or -inf only: index 0.
+    if (bi == 0x7fffffff) bi = 0;
+    if (out_val != nullptr) out_val[blockIdx.x] = best;
+    out_idx[blockIdx.x] = index_offset + bi;
+  }
 }
 
 }  // namespace pg

@@ -6,9 +6,13 @@
 // rows, so the kernel is an HBM stream of W.  Work is split "stream-K":
 // the (output tile, 64-wide k-block) pairs are laid end to end and CTA c
 // of G takes blocks [c*T/G, (c+1)*T/G), so every CTA streams the same number
-// of bytes whatever the shape.  A CTA stages its blocks through a 6-deep
-// shared-memory ring with tiled TMA (W box 32 rows x 128 B, 128-byte
-// swizzle; X box 8*NT rows), and its 4 warps run mma.sync m16n8k16 with
+// of bytes whatever the shape.  The weights are stored pre-tiled (one-time
+// packing, pg_pack_weight): every (tile, k-block) is a contiguous 8 KB block
+// of 64 rows x 64 halves already in the 128-byte-swizzled order ldmatrix
+// reads, so a stage's weights are one 8 KB bulk copy (cp.async.bulk) from
+// a sequential HBM stream.  A CTA stages its blocks through a 6-deep
+// shared-memory ring (activations: tiled TMA, X box 8*NT rows, 128-byte
+// swizzle), and its 4 warps run mma.sync m16n8k16 with
 // FP32 accumulators (warp w owns W rows 16w..16w+15 of the 64-row tile,
 // the batch rows are the n-tiles).  A tile split between CTAs is finished
 // by the last of them to arrive (an atomic counter per tile): it sums the
@@ -32,7 +36,9 @@ namespace pg {
 
 constexpr int kGemmTileRows = 64;  // W rows per output tile
 constexpr int kGemmBK = 64;        // k per stage: 128-byte rows
-constexpr int kGemmStages = 6;
+// Ring depth: enough weight bytes in flight per SM at the CTAs per SM the
+// shared memory allows (3 at 9 KB stages, 2 at 10-12 KB stages).
+__host__ __device__ constexpr int gemm_stages(int nt) { return nt == 1 ? 6 : 8; }
 constexpr int kGemmWarps = 4;
 
 enum GemmMode { kGemmStore = 0, kGemmResidual = 1, kGemmSiluMul = 2 };
@@ -58,7 +64,7 @@ __host__ __device__ constexpr int gemm_stage_bytes(int nt) {
   return kGemmTileRows * 128 + 8 * nt * 128;
 }
 __host__ __device__ constexpr int gemm_smem_bytes(int nt) {
-  return kGemmStages * gemm_stage_bytes(nt) + kGemmStages * 8 + 1024;
+  return gemm_stages(nt) * gemm_stage_bytes(nt) + gemm_stages(nt) * 8 + 1024;
 }
 
 __device__ __forceinline__ void ldsm_x4(const uint8_t* addr, uint32_t& r0, uint32_t& r1,
@@ -91,22 +97,23 @@ __device__ __forceinline__ void gemm_contributors(const GemmParams& p, int t, in
   c1 = (((t + 1) * p.kblocks) * p.grid - 1) / p.total;
 }
 
-// Request the weight rows of k-block kb of tile `tile` (and expect the
-// whole stage, activations included, on the stage's barrier).
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// Request the packed weight block (tile, kb) and expect the whole stage,
+// activations included, on the stage's barrier.
 template <int NT>
-__device__ __forceinline__ void gemm_issue_w(const CUtensorMap* tw, const GemmParams& p,
+__device__ __forceinline__ void gemm_issue_w(const __half* wp, const GemmParams& p,
                                              uint8_t* stage, uint64_t* bar, int tile, int kb) {
   mbar_arrive_expect_tx(bar, gemm_stage_bytes(NT));
-  int r0, r1;
-  if (p.mode == kGemmSiluMul) {
-    r0 = tile * 32;
-    r1 = p.half_rows + tile * 32;
-  } else {
-    r0 = tile * kGemmTileRows;
-    r1 = r0 + 32;
-  }
-  tma_load_2d(stage, tw, kb * kGemmBK, r0, bar);
-  tma_load_2d(stage + 4096, tw, kb * kGemmBK, r1, bar);
+  const __half* src = wp + (static_cast<int64_t>(tile) * p.kblocks + kb) * (kGemmTileRows * kGemmBK);
+  bulk_load(stage, src, kGemmTileRows * 128, bar);
 }
 
 template <int NT>
@@ -189,24 +196,48 @@ __device__ __forceinline__ void gemm_flush(const GemmParams& p, const float (&ac
   __syncthreads();
   if (*s_last) {
     __threadfence();
+    // Sum the contributors' tiles in CTA order (deterministic): each thread
+    // owns float4 chunks of the 64 x XR tile, all contributors' loads of a
+    // chunk in flight together, then the sums go through shared memory.
     const int n = last - first + 1;
-    gemm_epilogue<NT>(p, tile, [&](int j, int b) {
-      float v = 0.f;
-      for (int q = 0; q < n; ++q)
-        v += __ldcg(p.partials + static_cast<int64_t>(s_seg[q]) * (kGemmTileRows * XR) + j * XR + b);
-      return v;
-    });
+    constexpr int CH = kGemmTileRows * XR / 4;  // float4 chunks per tile
+    for (int ch = threadIdx.x; ch < CH; ch += blockDim.x) {
+      float4 v[kGemmMaxContrib];
+#pragma unroll
+      for (int q = 0; q < kGemmMaxContrib; ++q)
+        if (q < n)
+          v[q] = __ldcg(reinterpret_cast<const float4*>(
+                            p.partials + static_cast<int64_t>(s_seg[q]) * (kGemmTileRows * XR)) +
+                        ch);
+      float4 acc4 = v[0];
+#pragma unroll
+      for (int q = 1; q < kGemmMaxContrib; ++q)
+        if (q < n) {
+          acc4.x += v[q].x;
+          acc4.y += v[q].y;
+          acc4.z += v[q].z;
+          acc4.w += v[q].w;
+        }
+      const int row = (4 * ch) / XR, col = (4 * ch) % XR;
+      s_tile[row * ES + col] = acc4.x;
+      s_tile[row * ES + col + 1] = acc4.y;
+      s_tile[row * ES + col + 2] = acc4.z;
+      s_tile[row * ES + col + 3] = acc4.w;
+    }
+    __syncthreads();
+    gemm_epilogue<NT>(p, tile, [&](int j, int b) { return s_tile[j * ES + b]; });
   }
   __syncthreads();
 }
 
 template <int NT>
 __global__ void __launch_bounds__(kGemmWarps * 32)
-    pg_skinny_gemm_kernel(const __grid_constant__ CUtensorMap tm_w,
+    pg_skinny_gemm_kernel(const __half* __restrict__ w_packed,
                           const __grid_constant__ CUtensorMap tm_x,
                           const __grid_constant__ GemmParams p) {
   constexpr int XR = 8 * NT;            // padded batch rows
   constexpr int SB = gemm_stage_bytes(NT);
+  constexpr int kGemmStages = gemm_stages(NT);
   constexpr int ES = XR + 1;            // padded row of the epilogue tile
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
@@ -222,7 +253,6 @@ __global__ void __launch_bounds__(kGemmWarps * 32)
   if (threadIdx.x == 0) {
     for (int s = 0; s < kGemmStages; ++s) mbar_init(full + s, 1);
     fence_barrier_init();
-    prefetch_tensormap(&tm_w);
     prefetch_tensormap(&tm_x);
   }
   __syncthreads();
@@ -232,7 +262,7 @@ __global__ void __launch_bounds__(kGemmWarps * 32)
   if (threadIdx.x == 0) {
     int t = itile, k = ikb;
     for (int i = 0; i < pro; ++i) {
-      gemm_issue_w<NT>(&tm_w, p, smem + i * SB, full + i, t, k);
+      gemm_issue_w<NT>(w_packed, p, smem + i * SB, full + i, t, k);
       if (++k == p.kblocks) k = 0, ++t;
     }
   }
@@ -302,7 +332,7 @@ __global__ void __launch_bounds__(kGemmWarps * 32)
     ++ckb;
     __syncthreads();  // every warp is done with stage st
     if (threadIdx.x == 0 && i + kGemmStages < nblk) {
-      gemm_issue_w<NT>(&tm_w, p, smem + st * SB, full + st, itile, ikb);
+      gemm_issue_w<NT>(w_packed, p, smem + st * SB, full + st, itile, ikb);
       gemm_issue_x<NT>(&tm_x, smem + st * SB, full + st, ikb);
       if (++ikb == p.kblocks) ikb = 0, ++itile;
     }
@@ -316,6 +346,32 @@ __global__ void __launch_bounds__(kGemmWarps * 32)
     return;
   }
   gemm_flush<NT>(p, acc, cur, seg_kb0, ckb, seg, s_tile, &s_last, s_seg);
+}
+
+// Weight packing: W [n, k] (row stride ld) -> [tiles][k/64][64][64] with the
+// 16-byte chunk c of row r stored at chunk c ^ (r & 7).  Tile t holds rows
+// 64t..64t+63, or in silu_mul mode gate rows 32t..32t+31 then the up rows
+// n/2 + 32t.. .  One thread per 16-byte chunk.
+__global__ void pg_pack_weight_kernel(const __half* __restrict__ w, int64_t ld, int32_t n,
+                                      int32_t k, int32_t mode, __half* __restrict__ out) {
+  const int kb_count = k / kGemmBK;
+  const int64_t chunks = static_cast<int64_t>(n) * (k / 8);
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < chunks;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int c = static_cast<int>(i & 7);
+    const int64_t rest = i >> 3;
+    const int r = static_cast<int>(rest % kGemmTileRows);
+    const int64_t tk = rest / kGemmTileRows;
+    const int kb = static_cast<int>(tk % kb_count);
+    const int tile = static_cast<int>(tk / kb_count);
+    int64_t src_row;
+    if (mode == kGemmSiluMul)
+      src_row = r < 32 ? tile * 32 + r : n / 2 + tile * 32 + (r - 32);
+    else
+      src_row = static_cast<int64_t>(tile) * kGemmTileRows + r;
+    const uint4 v = *reinterpret_cast<const uint4*>(w + src_row * ld + kb * kGemmBK + c * 8);
+    *reinterpret_cast<uint4*>(out + (tk * kGemmTileRows + r) * kGemmBK + ((c ^ (r & 7)) * 8)) = v;
+  }
 }
 
 }  // namespace pg

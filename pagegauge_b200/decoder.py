@@ -44,6 +44,7 @@ import torch
 from . import _lib, scheduler
 from .cache import GaugeCache, apply_rope_fp16, rope_tables
 from .decode import PageGaugeDecode
+from .gemm import RESIDUAL, SILU_MUL, STORE, PackedWeight, SkinnyGemm
 from .quantize import quantize_pages_into
 from .runtime import load_append_extension
 
@@ -235,7 +236,8 @@ class PageGaugeDecoder:
     """
 
     def __init__(self, weights: DecoderWeights, batch: int, max_context: int,
-                 process_group=None, ring_pages: int = 16, workspace_mb: int = 32):
+                 process_group=None, ring_pages: int = 16, workspace_mb: int = 32,
+                 gemm: str = "auto"):
         cfg, tp = weights.cfg, weights.tp
         if cfg.head_dim != HEAD_DIM:
             raise ValueError("head_dim must be 128")
@@ -276,6 +278,31 @@ class PageGaugeDecoder:
         self.act = torch.zeros(B, self.inter, **h16)
         self.down = torch.zeros(B, cfg.hidden, **h16)
         self.logits = torch.zeros(B, self.vocab_local, **h16)
+        self.best_val = torch.zeros(B, dtype=torch.float32, **z)
+        self.best_idx = torch.zeros(B, dtype=torch.int64, **z)
+        if gemm not in ("auto", "pg", "cublas"):
+            raise ValueError("gemm must be 'auto', 'pg' (weight-streaming kernels) or 'cublas'")
+        # Measured on B200: the weight-streaming kernels (fused epilogues,
+        # PDL) win at up to 8 token rows; cuBLAS's tensor-core GEMMs win at 32.
+        if gemm == "auto":
+            gemm = "pg" if batch <= 8 else "cublas"
+        self.gemm_impl = gemm
+        self.sk = SkinnyGemm(dev)
+        self.packed = []
+        if gemm == "pg":
+            # Weights in the streaming kernels' tiled layout (the row-major
+            # copies stay for the dense prefill).
+            for lw in weights.layers:
+                self.packed.append({"qkv": PackedWeight(lw.qkv), "o": PackedWeight(lw.o),
+                                    "gate_up": PackedWeight(lw.gate_up, SILU_MUL),
+                                    "down": PackedWeight(lw.down)})
+            self.lm_head_packed = PackedWeight(weights.lm_head)
+            fused = process_group is None
+            self.sk.reserve(qkv_w, cfg.hidden, B, STORE)
+            self.sk.reserve(cfg.hidden, self.hq * HEAD_DIM, B, RESIDUAL if fused else STORE)
+            self.sk.reserve(2 * self.inter, cfg.hidden, B, SILU_MUL)
+            self.sk.reserve(cfg.hidden, self.inter, B, RESIDUAL if fused else STORE)
+            self.sk.reserve(self.vocab_local, cfg.hidden, B, STORE)
         self.tokens = torch.zeros(B, dtype=torch.int64, **z)
         self.positions = torch.zeros(B, dtype=torch.int32, **z)
         self.last_len = torch.ones(B, dtype=torch.int32, **z)
@@ -307,8 +334,10 @@ class PageGaugeDecoder:
     def _greedy(self, logits: torch.Tensor) -> torch.Tensor:
         """Argmax over the full vocabulary of vocabulary-parallel logits
         (ties to the lowest index, as torch.argmax on the full row)."""
-        vals, idx = torch.max(logits.float(), dim=-1)
-        idx = idx + self.tp.vocab[0]
+        B = logits.shape[0]
+        _call("pg_argmax_rows", logits.data_ptr(), logits.stride(0), B, logits.shape[1],
+              self.tp.vocab[0], self.best_val.data_ptr(), self.best_idx.data_ptr(), _stream())
+        vals, idx = self.best_val[:B], self.best_idx[:B]
         if self.pg is None:
             return idx
         pair = torch.stack((vals, idx.to(torch.float32)), dim=-1)  # [B, 2]; V < 2^24
@@ -430,12 +459,14 @@ class PageGaugeDecoder:
         d = HEAD_DIM
         B = self.batch
         torch.index_select(self.w.embed, 0, self.tokens, out=self.residual)
-        delta = None
         q_w, kv_w = self.hq * d, self.hkv * d
+        fused = self.gemm_impl == "pg" and self.pg is None
+        delta = None
         for l, lw in enumerate(self.w.layers):
             c = self.caches[l]
+            pk = self.packed[l] if self.packed else {}
             self._norm(self.residual, delta, lw.attn_norm, self.normed)
-            torch.matmul(self.normed, lw.qkv.t(), out=self.qkv)
+            self._linear(self.normed, lw.qkv, self.qkv, pk.get("qkv"))
             q = self.qkv[:, :q_w].view(B, self.hq, d)
             k = self.qkv[:, q_w:q_w + kv_w].view(B, self.hkv, d)
             v = self.qkv[:, q_w + kv_w:].view(B, self.hkv, d)
@@ -445,30 +476,53 @@ class PageGaugeDecoder:
                 c.value_scales, 0)
             dec.run(self.rq, c.key_codes, c.value_codes, c.key_scales, c.value_scales,
                     c.exact_key, c.exact_value, c.value_center, out=self.attn)
-            torch.matmul(self.attn.view(B, -1), lw.o.t(), out=self.o)
+            if fused:
+                # residual += attn @ Wo^T (fused epilogue), then the MLP with
+                # SiLU(gate) * up fused into the gate/up projection and the
+                # down projection added into the residual.
+                self.sk(self.attn.view(B, -1), pk["o"], mode=RESIDUAL, residual=self.residual)
+                self._norm(self.residual, None, lw.mlp_norm, self.normed)
+                self.sk(self.normed, pk["gate_up"], out=self.act, mode=SILU_MUL)
+                self.sk(self.act, pk["down"], mode=RESIDUAL, residual=self.residual)
+                delta = None
+                continue
+            self._linear(self.attn.view(B, -1), lw.o, self.o, pk.get("o"))
             self._all_reduce(self.o)
             self._norm(self.residual, self.o, lw.mlp_norm, self.normed)
-            torch.matmul(self.normed, lw.gate_up.t(), out=self.gate_up)
-            self._silu_mul(self.gate_up, self.act)
-            torch.matmul(self.act, lw.down.t(), out=self.down)
+            if self.gemm_impl == "pg":
+                self.sk(self.normed, pk["gate_up"], out=self.act, mode=SILU_MUL)
+            else:
+                torch.matmul(self.normed, lw.gate_up.t(), out=self.gate_up)
+                self._silu_mul(self.gate_up, self.act)
+            self._linear(self.act, lw.down, self.down, pk.get("down"))
             self._all_reduce(self.down)
             delta = self.down
         self._norm(self.residual, delta, self.w.final_norm, self.normed)
-        torch.matmul(self.normed, self.w.lm_head.t(), out=self.logits)
+        self._linear(self.normed, self.w.lm_head, self.logits,
+                     self.lm_head_packed if self.packed else None)
         self.tokens.copy_(self._greedy(self.logits))
         _call("pg_step_positions", self.positions.data_ptr(), self.last_len.data_ptr(), B, 1,
               _stream())
 
+    def _linear(self, x: torch.Tensor, w: torch.Tensor, out: torch.Tensor,
+                packed: PackedWeight | None = None) -> None:
+        if packed is not None:
+            self.sk(x, packed, out=out)
+        else:
+            torch.matmul(x, w.t(), out=out)
+
     def launches_per_step(self) -> int:
-        """Kernel launches of this library in one decode step (append,
-        split decode, merge, two norms and SiLU*up per layer; the final norm
-        and the position update)."""
+        """Kernel launches of this library in one decode step."""
         entry = next(iter(self._bank.values()), None)
         attn = 2
         if entry is not None:
             plan = entry["dec"].work_plan
             attn = 1 if (plan.single and plan.num_items) else 2
-        return self.cfg.layers * (4 + attn) + 2
+        if self.gemm_impl == "pg":
+            # norm, qkv, append, o, norm, gate_up(+SiLU), down per layer; the
+            # final norm, LM head, argmax and position update.
+            return self.cfg.layers * (7 + attn) + 4
+        return self.cfg.layers * (4 + attn) + 3
 
     def _capture(self, entry: dict) -> None:
         graph = torch.cuda.CUDAGraph()

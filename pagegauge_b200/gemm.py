@@ -21,6 +21,25 @@ def _stream() -> int:
     return torch.cuda.current_stream().cuda_stream
 
 
+class PackedWeight:
+    """W [n, k] FP16 in the kernel's tiled layout (one contiguous 8 KB block
+    per 64 rows x 64 k, 128-byte swizzled; in silu_mul mode each tile holds
+    32 gate rows and the matching 32 up rows)."""
+
+    def __init__(self, w: torch.Tensor, mode: int = STORE):
+        if w.dtype != torch.float16 or w.dim() != 2 or not w.is_cuda or w.stride(1) != 1:
+            raise ValueError("w must be a CUDA float16 [n, k] tensor with contiguous rows")
+        self.n, self.k = w.shape
+        self.mode = mode
+        self.data = torch.empty(self.n * self.k, dtype=torch.float16, device=w.device)
+        _lib.check(_lib.load().pg_pack_weight(w.data_ptr(), w.stride(0), self.n, self.k, mode,
+                                              self.data.data_ptr(), _stream()))
+
+    @property
+    def shape(self):
+        return (self.n, self.k)
+
+
 class SkinnyGemm:
     """Launcher with caller-owned split-K scratch (partial tiles + per-tile
     arrival counters), sized for the largest shape it is asked to run."""
@@ -41,19 +60,21 @@ class SkinnyGemm:
         if tiles.value > self.counters.numel():
             self.counters = torch.zeros(tiles.value, dtype=torch.int32, device=self.device)
 
-    def __call__(self, x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None,
+    def __call__(self, x: torch.Tensor, w: PackedWeight, out: torch.Tensor | None = None,
                  mode: int = STORE, residual: torch.Tensor | None = None, pdl: bool = True,
                  grid: int = 0) -> torch.Tensor | None:
-        if x.dtype != torch.float16 or w.dtype != torch.float16 or x.dim() != 2 or w.dim() != 2:
-            raise ValueError("x [batch, k] and w [n, k] must be 2-D float16")
-        if x.stride(1) != 1 or w.stride(1) != 1:
-            raise ValueError("x and w need a contiguous last dimension")
+        """y = x @ W^T with W packed for this ``mode`` (silu_mul needs the
+        silu_mul packing; store and residual share theirs)."""
+        if x.dtype != torch.float16 or x.dim() != 2 or x.stride(1) != 1:
+            raise ValueError("x must be a float16 [batch, k] tensor with contiguous rows")
+        if (w.mode == SILU_MUL) != (mode == SILU_MUL):
+            raise ValueError("the weight was packed for another epilogue")
         batch, k = x.shape
-        n = w.shape[0]
-        if w.shape[1] != k:
+        n = w.n
+        if w.k != k:
             raise ValueError("x and w disagree on k")
         a = _lib.PgGemmArgs()
-        a.w, a.ldw = w.data_ptr(), w.stride(0)
+        a.w, a.ldw = w.data.data_ptr(), w.k
         a.x, a.ldx = x.data_ptr(), x.stride(0)
         if mode == RESIDUAL:
             if residual is None or residual.shape != (batch, n) or residual.stride(1) != 1:

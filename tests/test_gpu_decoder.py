@@ -42,10 +42,11 @@ def _oracle_caches(dec):
     return out
 
 
-@pytest.mark.parametrize("batch,prompt_len", [(2, 300), (1, 256)])
-def test_decoder_prefill_and_decode_match_oracle(cuda_lib, batch, prompt_len):
+@pytest.mark.parametrize("batch,prompt_len,gemm", [(2, 300, "pg"), (1, 256, "pg"),
+                                                   (2, 300, "cublas")])
+def test_decoder_prefill_and_decode_match_oracle(cuda_lib, batch, prompt_len, gemm):
     weights = random_decoder_weights(CFG, SEED, device="cuda", gen_device="cpu")
-    dec = PageGaugeDecoder(weights, batch=batch, max_context=512)
+    dec = PageGaugeDecoder(weights, batch=batch, max_context=512, gemm=gemm)
     g = torch.Generator().manual_seed(8)
     prompt = torch.randint(0, CFG.vocab, (batch, prompt_len), generator=g)
     logits = dec.prefill(prompt.cuda()).float().cpu().numpy()

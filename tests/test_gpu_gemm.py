@@ -10,7 +10,7 @@ from __future__ import annotations
 import pytest
 import torch
 
-from pagegauge_b200.gemm import RESIDUAL, SILU_MUL, STORE, SkinnyGemm
+from pagegauge_b200.gemm import RESIDUAL, SILU_MUL, STORE, PackedWeight, SkinnyGemm
 from pagegauge_b200.runtime import read_device_error
 
 pytestmark = pytest.mark.gpu
@@ -50,8 +50,9 @@ def test_store_matches_torch(cuda_lib, n, k, batch, grid):
     w, x = _data(n, k, batch, n + k + batch)
     gemm = SkinnyGemm("cuda")
     gemm.reserve(n, k, batch)
-    out = gemm(x, w, grid=grid)
-    again = gemm(x, w, grid=grid)
+    pw = PackedWeight(w)
+    out = gemm(x, pw, grid=grid)
+    again = gemm(x, pw, grid=grid)
     torch.cuda.synchronize()
     assert read_device_error() == 0
     _assert_f16_close(out, _ref(x, w), k)
@@ -71,8 +72,9 @@ def test_residual_epilogue(cuda_lib, batch):
     r = r0.clone()
     gemm = SkinnyGemm("cuda")
     gemm.reserve(n, k, batch, RESIDUAL)
-    gemm(x, w, mode=RESIDUAL, residual=r)
-    y = gemm(x, w)
+    pw = PackedWeight(w)
+    gemm(x, pw, mode=RESIDUAL, residual=r)
+    y = gemm(x, pw)
     torch.cuda.synchronize()
     _assert_f16_close(y, _ref(x, w), k)
     assert torch.equal(r, r0 + y)
@@ -84,7 +86,7 @@ def test_silu_mul_epilogue(cuda_lib, batch, grid):
     w, x = _data(2 * f, k, batch, 7 + batch)
     gemm = SkinnyGemm("cuda")
     gemm.reserve(2 * f, k, batch, SILU_MUL)
-    out = gemm(x, w, mode=SILU_MUL, grid=grid)
+    out = gemm(x, PackedWeight(w, SILU_MUL), mode=SILU_MUL, grid=grid)
     torch.cuda.synchronize()
     acc = _ref(x, w)
     gate = acc[:, :f].half().float()
@@ -114,13 +116,14 @@ def test_strided_operands_and_graph_replay(cuda_lib):
     out = out_big[:, :n]
     gemm = SkinnyGemm("cuda")
     gemm.reserve(n, k, batch)
+    pw = PackedWeight(w)
     s = torch.cuda.Stream()
     with torch.cuda.stream(s):
-        gemm(x, w, out=out)
+        gemm(x, pw, out=out)
         torch.cuda.synchronize()
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=s):
-            gemm(x, w, out=out)
+            gemm(x, pw, out=out)
         out.zero_()
         graph.replay()
         graph.replay()
@@ -133,7 +136,25 @@ def test_strided_operands_and_graph_replay(cuda_lib):
 def test_rejects_bad_shapes(cuda_lib):
     gemm = SkinnyGemm("cuda")
     w, x = _data(256, 512, 2, 1)
-    with pytest.raises(RuntimeError, match="multiple of 64"):
-        gemm(x[:, :500], w[:, :500].contiguous())
+    with pytest.raises(RuntimeError, match="multiples of 64"):
+        PackedWeight(w[:, :500].contiguous())
+    pw = PackedWeight(w)
     with pytest.raises(RuntimeError, match="batch must be 1..32"):
-        gemm(torch.zeros(33, 512, dtype=torch.float16, device="cuda"), w)
+        gemm(torch.zeros(33, 512, dtype=torch.float16, device="cuda"), pw)
+    with pytest.raises(ValueError, match="another epilogue"):
+        gemm(x, pw, mode=SILU_MUL)
+
+
+def test_packed_layout(cuda_lib):
+    """Tile t, k-block kb, row r, 16-byte chunk c ^ (r & 7) holds
+    W[64t + r, 64kb + 8c .. +8]; silu_mul tiles take 32 gate + 32 up rows."""
+    n, k = 128, 192
+    w = torch.arange(n * k, device="cuda").remainder(2039).half().view(n, k)
+    for mode in (STORE, SILU_MUL):
+        pw = PackedWeight(w, mode).data.view(-1, k // 64, 64, 8, 8)
+        for t, kb, r, c in ((0, 0, 0, 0), (1, 2, 13, 5), (0, 1, 40, 7), (1, 0, 63, 3)):
+            if mode == STORE:
+                row = 64 * t + r
+            else:
+                row = 32 * t + r if r < 32 else n // 2 + 32 * t + (r - 32)
+            assert torch.equal(pw[t, kb, r, c ^ (r & 7)], w[row, 64 * kb + 8 * c:64 * kb + 8 * c + 8])
