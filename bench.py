@@ -61,6 +61,8 @@ def parse_args():
     p.add_argument("--decoder-batch", type=int, nargs="*", default=[32, 1],
                    help="decoder workload: batch sizes (the first is the headline)")
     p.add_argument("--decoder-steps", type=int, default=16)
+    p.add_argument("--decoder-policy", default="S0/A0/T256",
+                   help="exact pages: S<sink pages>/A<static suffix pages>/T<tail tokens>")
     p.add_argument("--decoder-gemm", choices=("auto", "pg", "cublas"), default="auto",
                    help="decoder projections: weight-streaming kernels (pg), cuBLAS, or by batch")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -644,15 +646,26 @@ def decoder_bytes(dec, batch: int) -> int:
                 for t in (lw.attn_norm, lw.qkv, lw.o, lw.mlp_norm, lw.gate_up, lw.down))
     total += w.lm_head.numel() * 2 + w.final_norm.numel() * 2 + batch * w.embed.shape[1] * 2
     old, exact = [], []
-    for p in dec.host_positions:
-        first = max(0, int(p) // PAGE - 15)
-        old.append(first * PAGE)
-        exact.append(int(p) + 1 - first * PAGE)
+    from pagegauge_b200.decoder import page_tables
+    o_ptr, _, _, _ = page_tables(dec.host_positions, dec.capacity_pages, dec.ring_pages,
+                                 dec.sink_pages, dec.suffix_pages, dec.initial_pages)
+    for r, p in enumerate(dec.host_positions):
+        n_old = int(o_ptr[r + 1] - o_ptr[r])
+        old.append(n_old * PAGE)
+        exact.append(int(p) + 1 - n_old * PAGE)
     return total + dec.cfg.layers * algorithmic_bytes(old, exact, hkv=dec.hkv)
 
 
+def parse_policy(text: str) -> tuple[int, int, int]:
+    """'S4/A0/T768' -> (sink pages, suffix pages, ring pages)."""
+    parts = dict((p[0].upper(), int(p[1:])) for p in text.split("/"))
+    if parts.get("T", 256) % PAGE:
+        raise ValueError("the tail must be whole pages")
+    return parts.get("S", 0), parts.get("A", 0), parts.get("T", 256) // PAGE
+
+
 def measure_decoder(dist: Dist, batch: int, context: int = 16384, steps: int = 16,
-                    seed: int = 20261004, gemm: str = "auto") -> dict:
+                    seed: int = 20261004, gemm: str = "auto", policy: str = "S0/A0/T256") -> dict:
     """Mistral-7B-shaped random-init FP16 decoder,
     prompt of ``context`` random tokens prefilled into PageGauge caches, one
     eager warm-up decode step, then ``steps`` greedy decode steps (CUDA
@@ -666,8 +679,9 @@ def measure_decoder(dist: Dist, batch: int, context: int = 16384, steps: int = 1
     cfg = DecoderConfig.mistral_7b_shaped()
     t0 = time.perf_counter()
     w = random_decoder_weights(cfg, seed, device="cuda", tp=TensorParallel.of(cfg, rank, world))
+    sink, suffix, ring = parse_policy(policy)
     dec = PageGaugeDecoder(w, batch, max_context=context + 4 * steps + 32, process_group=pg,
-                           gemm=gemm)
+                           gemm=gemm, ring_pages=ring, sink_pages=sink, suffix_pages=suffix)
     prompt = torch.randint(0, cfg.vocab, (batch, context),
                            generator=torch.Generator().manual_seed(seed + batch))
     dec.prefill(prompt.cuda())
@@ -710,6 +724,7 @@ def measure_decoder(dist: Dist, batch: int, context: int = 16384, steps: int = 1
         "hbm_bytes_per_step_per_rank": nbytes, "achieved_gbs_per_rank": round(achieved, 1),
         "roofline_frac": round(achieved / peak, 4), "prefill_s": round(prefill_s, 2),
         "replans_in_timing": 0, "params": cfg.parameter_count(), "gemm": dec.gemm_impl,
+        "exact_policy": policy,
     }
     del dec, w
     torch.cuda.empty_cache()
@@ -723,9 +738,10 @@ def run_decoder(args, dist: Dist, local: int) -> None:
     results = {}
     with clocks:
         results[batches[0]] = measure_decoder(dist, batches[0], steps=args.decoder_steps,
-                                              gemm=args.decoder_gemm)
+                                              gemm=args.decoder_gemm, policy=args.decoder_policy)
     for b in batches[1:]:
-        results[b] = measure_decoder(dist, b, steps=args.decoder_steps, gemm=args.decoder_gemm)
+        results[b] = measure_decoder(dist, b, steps=args.decoder_steps, gemm=args.decoder_gemm,
+                                     policy=args.decoder_policy)
     b32 = results[batches[0]]
     peak, peak_src = peak_hbm()
     if rank == 0:

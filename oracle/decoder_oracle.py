@@ -129,23 +129,37 @@ def dense_forward(w, cfg, tokens, reduce=None, round16=True, rope_cache=None):
     return linear(x, w["lm_head"], round16)[0].astype(np.float32), kvs
 
 
-def page_tables(positions, capacity_pages, ring_pages=16):
-    """Old/exact page ids per request for a step appending at positions[r]:
-    the exact window is the current page and the ring_pages - 1 pages before
-    it (ring slot page % ring_pages), older pages are INT8
-    (page_gauge_logical_partition, benchmark_page_gauge_transformer.py:536-599,
-    with no fixed prefix)."""
+def page_tables(positions, capacity_pages, ring_pages=16, sink_pages=0, suffix_pages=0,
+                initial_pages=None):
+    """Old/exact page ids per request for a step appending at positions[r]
+    (page_gauge_logical_partition and exact_physical_page_index,
+    benchmark_page_gauge_transformer.py:460-599): exact pages are the first
+    sink_pages, the suffix_pages that ended an ``initial_pages`` prompt, and
+    the current page with the ring_pages - 1 before it; the exact storage of
+    a request is sink, suffix, then a ring slot ``fixed + page % ring``."""
+    fixed = sink_pages + suffix_pages
+    storage = fixed + ring_pages
+    sbeg = initial_pages - suffix_pages if suffix_pages else None
     tables = []
     for r, p in enumerate(positions):
         cur = p // PAGE
-        first = max(0, cur - ring_pages + 1)
-        tables.append(([r * capacity_pages + lp for lp in range(first)],
-                       [r * ring_pages + lp % ring_pages for lp in range(first, cur + 1)],
-                       first * PAGE, p + 1 - first * PAGE))
+        tail0 = max(0, cur - ring_pages + 1)
+        old, exact = [], []
+        for lp in range(cur + 1):
+            if lp < sink_pages:
+                exact.append(r * storage + lp)
+            elif sbeg is not None and sbeg <= lp < initial_pages:
+                exact.append(r * storage + sink_pages + lp - sbeg)
+            elif lp >= tail0:
+                exact.append(r * storage + fixed + lp % ring_pages)
+            else:
+                old.append(r * capacity_pages + lp)
+        tables.append((old, exact, len(old) * PAGE, p + 1 - len(old) * PAGE))
     return tables
 
 
-def decode_step(w, cfg, caches, tokens, positions, capacity_pages, ring_pages=16):
+def decode_step(w, cfg, caches, tokens, positions, capacity_pages, ring_pages=16, sink_pages=0,
+                suffix_pages=0, initial_pages=None):
     """One greedy decode step of the batch from the page-gauge caches
     (``caches[l]`` = dict with GaugeState ``state`` and FP16 ``key_center`` /
     ``value_center`` [B, hkv, 128]); mutates the caches with the fused append
@@ -155,7 +169,8 @@ def decode_step(w, cfg, caches, tokens, positions, capacity_pages, ring_pages=16
     cos32, sin32 = cfg["rope"]
     cos, sin = _f16(cos32), _f16(sin32)
     h = np.asarray(w["embed"][np.asarray(tokens)], np.float16)
-    tables = page_tables(positions, capacity_pages, ring_pages)
+    tables = page_tables(positions, capacity_pages, ring_pages, sink_pages, suffix_pages,
+                         initial_pages)
     for lw, c in zip(w["layers"], caches):
         x = rms_norm(h, lw["attn_norm"], cfg["eps"])
         qkv = linear(x, lw["qkv"])
@@ -164,7 +179,8 @@ def decode_step(w, cfg, caches, tokens, positions, capacity_pages, ring_pages=16
         v = qkv[:, (hq + hkv) * DIM:].reshape(B, hkv, DIM)
         st = c["state"]
         rq = O.rope_append_page_gauge_batched(st, q, k, v, cos, sin, c["key_center"],
-                                              c["value_center"], 0, positions)
+                                              c["value_center"], sink_pages + suffix_pages,
+                                              positions)
         att = np.empty((B, hq, DIM), np.float16)
         for r in range(B):
             old, exact, old_tok, ex_tok = tables[r]

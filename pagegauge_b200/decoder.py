@@ -193,21 +193,39 @@ def random_decoder_weights(cfg: DecoderConfig, seed: int = 20261004, device="cud
     return w
 
 
-def page_tables(positions, capacity_pages: int, ring_pages: int = 16):
+def page_tables(positions, capacity_pages: int, ring_pages: int = 16, sink_pages: int = 0,
+                suffix_pages: int = 0, initial_pages: int | None = None):
     """Per-request old/exact page lists for a decode step appending at
-    ``positions[r]`` (the logical partition of page_gauge_logical_partition,
-    scripts/benchmark_page_gauge_transformer.py:536-599, with no fixed
-    prefix): the exact window is the current page and the ring_pages - 1
-    before it (ring slot = page % ring_pages); older pages are INT8.
-    Returns CSR (old_indptr, old_indices, exact_indptr, exact_indices)."""
+    ``positions[r]`` (the exact-once partition of
+    page_gauge_logical_partition, scripts/benchmark_page_gauge_transformer.py:536-599):
+    exact = the first ``sink_pages`` pages, the ``suffix_pages`` pages that
+    ended the prompt (``initial_pages`` pages long), and the current page
+    with the ``ring_pages - 1`` before it; every other page is INT8.  Exact
+    pages map to exact_physical_page_index's slots (fixed slots, then the
+    tail ring at ``fixed + page % ring_pages``), INT8 page p of request r to
+    ``r * capacity_pages + p``.  Exact pages are listed in logical order, so
+    the current (partial) page is last.  Returns CSR (old_indptr,
+    old_indices, exact_indptr, exact_indices)."""
+    from .page_table import exact_physical_page_index
+
+    suffix_begin = (initial_pages - suffix_pages) if suffix_pages else None
     old_idx, ex_idx, old_cnt, ex_cnt = [], [], [0], [0]
     for r, p in enumerate(positions):
-        cur = int(p) // PAGE
-        first = max(0, cur - (ring_pages - 1))
-        old_idx.extend(r * capacity_pages + lp for lp in range(first))
-        ex_idx.extend(r * ring_pages + lp % ring_pages for lp in range(first, cur + 1))
-        old_cnt.append(old_cnt[-1] + first)
-        ex_cnt.append(ex_cnt[-1] + cur + 1 - first)
+        total = int(p) // PAGE + 1
+        tail_begin = max(0, total - ring_pages)
+        n_old = n_ex = 0
+        for lp in range(total):
+            exact = (lp < sink_pages or lp >= tail_begin
+                     or (suffix_begin is not None and suffix_begin <= lp < initial_pages))
+            if exact:
+                ex_idx.append(exact_physical_page_index(r, lp, ring_pages, sink_pages, suffix_pages,
+                                                        initial_pages))
+                n_ex += 1
+            else:
+                old_idx.append(r * capacity_pages + lp)
+                n_old += 1
+        old_cnt.append(old_cnt[-1] + n_old)
+        ex_cnt.append(ex_cnt[-1] + n_ex)
     as32 = lambda x: np.asarray(x if len(x) else [0], dtype=np.int32)
     return (np.asarray(old_cnt, np.int32), as32(old_idx), np.asarray(ex_cnt, np.int32),
             as32(ex_idx))
@@ -237,7 +255,7 @@ class PageGaugeDecoder:
 
     def __init__(self, weights: DecoderWeights, batch: int, max_context: int,
                  process_group=None, ring_pages: int = 16, workspace_mb: int = 32,
-                 gemm: str = "auto"):
+                 gemm: str = "auto", sink_pages: int = 0, suffix_pages: int = 0):
         cfg, tp = weights.cfg, weights.tp
         if cfg.head_dim != HEAD_DIM:
             raise ValueError("head_dim must be 128")
@@ -250,7 +268,19 @@ class PageGaugeDecoder:
         self.hkv = tp.kv_heads[1] - tp.kv_heads[0]
         self.inter = tp.intermediate[1] - tp.intermediate[0]
         self.vocab_local = tp.vocab[1] - tp.vocab[0]
+        # Exact-page policy (the paper's S<sink>/A<suffix>/T<ring*16>): the
+        # exact storage of a request is sink_pages fixed prefix slots,
+        # suffix_pages slots for the pages that ended the prompt, then the
+        # tail ring (page_table.exact_physical_page_index).
+        from .page_table import validate_exact_prefix_pages
         self.ring_pages = ring_pages
+        self.sink_pages = validate_exact_prefix_pages(sink_pages)
+        self.suffix_pages = int(suffix_pages)
+        if self.suffix_pages < 0 or ring_pages <= 0:
+            raise ValueError("suffix pages must be non-negative and the ring positive")
+        self.initial_pages = None
+        self.fixed_pages = self.sink_pages + self.suffix_pages
+        storage = self.fixed_pages + ring_pages
         self.capacity_pages = math.ceil(max_context / PAGE)
         self.max_context = self.capacity_pages * PAGE
         # FP32 accumulation in every cuBLAS reduction (no FP16 split-K sums).
@@ -261,10 +291,10 @@ class PageGaugeDecoder:
         for _ in range(cfg.layers):
             codes = lambda: torch.zeros(B * cap, PAGE, hkv, HEAD_DIM, dtype=torch.int8, **z)
             scales = lambda: torch.zeros(B * cap, hkv, dtype=torch.float16, **z)
-            ring = lambda: torch.zeros(B * ring_pages, PAGE, hkv, HEAD_DIM, dtype=torch.float16, **z)
+            ring = lambda: torch.zeros(B * storage, PAGE, hkv, HEAD_DIM, dtype=torch.float16, **z)
             cen = lambda: torch.zeros(B, hkv, HEAD_DIM, dtype=torch.float16, **z)
             self.caches.append(GaugeCache(ring(), ring(), codes(), codes(), scales(), scales(),
-                                          cen(), cen(), ring_pages, 0))
+                                          cen(), cen(), ring_pages, self.fixed_pages))
         self.cos, self.sin = rope_tables(self.max_context, cfg.rope_theta, device=dev)
         qkv_w = (self.hq + 2 * hkv) * HEAD_DIM
         h16 = dict(dtype=torch.float16, **z)
@@ -355,6 +385,14 @@ class PageGaugeDecoder:
         B, T = prompt.shape
         if B != self.batch or not 0 < T < self.max_context:
             raise ValueError("prompt must be [batch, T] with T below the cache capacity")
+        pages = -(-T // PAGE)
+        if self.suffix_pages:
+            from .page_table import validate_exact_static_suffix_pages
+            if T % PAGE:
+                raise ValueError("a static exact suffix needs a page-aligned prompt")
+            validate_exact_static_suffix_pages(self.suffix_pages, exact_prefix_pages=self.sink_pages,
+                                               initial_context_pages=pages)
+        self.initial_pages = pages
         out = torch.empty(B, self.vocab_local, dtype=torch.float16, device=self.device)
         for r in range(B):
             out[r] = self._prefill_request(r, prompt[r].to(self.device))
@@ -418,8 +456,14 @@ class PageGaugeDecoder:
                             c.key_codes[base:base + pages], c.value_codes[base:base + pages],
                             c.key_scales[base:base + pages], c.value_scales[base:base + pages],
                             0, "half_away")
-        for lp in range(max(0, pages - self.ring_pages), pages):
-            slot = r * self.ring_pages + lp % self.ring_pages
+        from .page_table import exact_physical_page_index
+        suffix_begin = pages - self.suffix_pages
+        for lp in range(pages):
+            if not (lp < self.sink_pages or lp >= max(0, pages - self.ring_pages)
+                    or (self.suffix_pages and lp >= suffix_begin)):
+                continue
+            slot = exact_physical_page_index(r, lp, self.ring_pages, self.sink_pages,
+                                             self.suffix_pages, pages)
             c.exact_key[slot] = (dk[lp].float() - c.key_center[r].float()).half()
             c.exact_value[slot] = (dv[lp].float() - c.value_center[r].float()).half()
 
@@ -437,7 +481,9 @@ class PageGaugeDecoder:
             return entry
         if max(int(p) for p in positions) >= self.max_context:
             raise RuntimeError("decode position exceeds the cache capacity")
-        o_ptr, o_idx, e_ptr, e_idx = page_tables(positions, self.capacity_pages, self.ring_pages)
+        o_ptr, o_idx, e_ptr, e_idx = page_tables(positions, self.capacity_pages, self.ring_pages,
+                                                 self.sink_pages, self.suffix_pages,
+                                                 self.initial_pages)
         dev = self.device
         dec = PageGaugeDecode(torch.empty(self._ws_bytes, dtype=torch.uint8, device=dev))
         old_idx = torch.from_numpy(o_idx).to(dev)
@@ -473,7 +519,7 @@ class PageGaugeDecoder:
             self.ext.rope_append_page_gauge_batched(
                 q, k, v, self.cos, self.sin, self.positions, c.key_center, c.value_center,
                 self.rq, c.exact_key, c.exact_value, c.key_codes, c.value_codes, c.key_scales,
-                c.value_scales, 0)
+                c.value_scales, self.fixed_pages)
             dec.run(self.rq, c.key_codes, c.value_codes, c.key_scales, c.value_scales,
                     c.exact_key, c.exact_value, c.value_center, out=self.attn)
             if fused:

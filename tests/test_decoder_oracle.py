@@ -101,6 +101,21 @@ def test_product_page_tables_match_oracle():
         assert list(e_idx[e_ptr[r]:e_ptr[r + 1]]) == exact
 
 
+@pytest.mark.parametrize("sink,suffix,ring", [(1, 0, 4), (4, 0, 48), (1, 2, 4), (0, 3, 2)])
+def test_product_page_tables_with_exact_policies_match_oracle(sink, suffix, ring):
+    from pagegauge_b200.decoder import page_tables
+
+    initial = 20
+    pos = [initial * 16 + d for d in (0, 5, 16, 40, 77, 400)]
+    o_ptr, o_idx, e_ptr, e_idx = page_tables(pos, 64, ring, sink, suffix, initial)
+    for r, (old, exact, ot, et) in enumerate(D.page_tables(pos, 64, ring, sink, suffix, initial)):
+        assert list(o_idx[o_ptr[r]:o_ptr[r + 1]]) == old
+        assert list(e_idx[e_ptr[r]:e_ptr[r + 1]]) == exact
+        # Exact-once cover of the context, current page last.
+        assert ot + et == pos[r] + 1
+        assert exact[-1] == r * (sink + suffix + ring) + sink + suffix + (pos[r] // 16) % ring
+
+
 def test_pick_greedy_ties_and_order():
     # [world, B, (value, index)]; rank slices are ascending vocabulary ranges.
     pairs = torch.tensor([[[1.0, 3.0], [5.0, 1.0]],

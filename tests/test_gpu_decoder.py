@@ -83,6 +83,33 @@ def test_decoder_prefill_and_decode_match_oracle(cuda_lib, batch, prompt_len, ge
     assert read_device_error() == 0
 
 
+@pytest.mark.parametrize("sink,suffix,ring", [(1, 2, 4), (4, 0, 6)])
+def test_decoder_exact_page_policies_match_oracle(cuda_lib, sink, suffix, ring):
+    """Exact prefix (sink) pages, a static exact suffix of the prompt and a
+    tail ring of `ring` pages (the paper's S/A/T policies)."""
+    batch, prompt_len = 2, 256
+    weights = random_decoder_weights(CFG, SEED, device="cuda", gen_device="cpu")
+    dec = PageGaugeDecoder(weights, batch=batch, max_context=512, ring_pages=ring,
+                           sink_pages=sink, suffix_pages=suffix)
+    prompt = torch.randint(0, CFG.vocab, (batch, prompt_len),
+                           generator=torch.Generator().manual_seed(17))
+    dec.prefill(prompt.cuda())
+    w, cfg = oracle_weights(CFG), oracle_cfg(CFG)
+    cfg["rope"] = (dec.cos.cpu().numpy(), dec.sin.cpu().numpy())
+    caches = _oracle_caches(dec)
+    tokens = dec.tokens.cpu().numpy().copy()
+    for i in range(21):
+        exp = D.decode_step(w, cfg, caches, tokens, [prompt_len + i] * batch, dec.capacity_pages,
+                            ring, sink, suffix, prompt_len // 16)
+        dec.step(use_graph=True)
+        got = dec.logits.float().cpu().numpy()
+        for r in range(batch):
+            _close(got[r], exp[r])
+        tokens = dec.tokens.cpu().numpy().copy()
+    from pagegauge_b200.runtime import read_device_error
+    assert read_device_error() == 0
+
+
 def test_decoder_graph_and_eager_steps_agree(cuda_lib):
     weights = random_decoder_weights(CFG, SEED + 1, device="cuda", gen_device="cpu")
     prompt = torch.randint(0, CFG.vocab, (2, 200), generator=torch.Generator().manual_seed(3))
