@@ -55,8 +55,10 @@ def parse_args():
                    help="pages per work item (-1: measured scheduler table, 0: heuristic)")
     p.add_argument("--layers", type=int, default=4)
     p.add_argument("--warps", type=int, default=4, help="warps per split-KV CTA")
-    p.add_argument("--merge", choices=("kernel", "fused"), default="kernel",
-                   help="cross-CTA merge: separate merge kernel or last-CTA merge in the split kernel")
+    p.add_argument("--merge", choices=("kernel", "fused", "cluster"), default="kernel",
+                   help="cross-CTA merge: separate merge kernel, last-CTA merge, or a single "
+                        "launch merging in thread-block clusters")
+    p.add_argument("--cluster", type=int, default=4, help="cluster size for --merge cluster")
     p.add_argument("--only", action="store_true", help="skip the secondary workloads")
     p.add_argument("--decoder-batch", type=int, nargs="*", default=[32, 1],
                    help="decoder workload: batch sizes (the first is the headline)")
@@ -315,7 +317,7 @@ class AttentionBench:
     of the public-API decode step."""
 
     def __init__(self, lengths, layers: int, split: int, fused_merge: bool, seed: int,
-                 warps: int = 4):
+                 warps: int = 4, cluster: int = 0):
         from pagegauge_b200 import scheduler
         from pagegauge_b200.cache import build_gauge_cache, rope_tables, synthetic_dense_cache
         from pagegauge_b200.decode import PageGaugeDecode
@@ -323,6 +325,7 @@ class AttentionBench:
         self.lengths = lengths
         self.layers = max(1, layers)
         self.fused = fused_merge
+        self.cluster = cluster
         cap = max(-(-n // PAGE) for n in lengths)
         self.caches = []
         self.q = self.tables = None
@@ -345,7 +348,8 @@ class AttentionBench:
         self.plan = self.dec.work_plan
         self.out = torch.empty_like(self.q)
         self.nbytes = algorithmic_bytes(t.old_tokens, t.exact_tokens)
-        self.launches_per_step = 1 if (self.plan.single and self.plan.num_items) else 2
+        self.launches_per_step = 1 if ((self.plan.single and self.plan.num_items)
+                                       or fused_merge or cluster > 1) else 2
         self.rope = rope_tables(cap * PAGE, device="cuda")
         self.stream = torch.cuda.Stream()
         self.chunk = 8 * self.layers
@@ -354,7 +358,8 @@ class AttentionBench:
         c = self.caches[layer]
         self.dec.run(self.q if q is None else q, c.key_codes, c.value_codes, c.key_scales,
                      c.value_scales, c.exact_key, c.exact_value, c.value_center,
-                     out=self.out if out is None else out, fused_merge=self.fused)
+                     out=self.out if out is None else out, fused_merge=self.fused,
+                     cluster=self.cluster)
 
     def capture(self):
         with torch.cuda.stream(self.stream):
@@ -795,7 +800,8 @@ def main() -> None:
     peak, peak_src = peak_hbm()
     lengths, glob, shards = workload_lengths(args.workload, world, rank)
     bench = AttentionBench(lengths, args.layers, args.split, args.merge == "fused",
-                           seed=SEED + 1000 * rank, warps=args.warps)
+                           seed=SEED + 1000 * rank, warps=args.warps,
+                           cluster=args.cluster if args.merge == "cluster" else 0)
     bench.capture()
     clocks = ClockSampler(local)
     ms = bench.time_steps(args.steps, args.warmup, dist, clocks)

@@ -215,9 +215,20 @@ typedef struct pg_decode_args {
                          merges each head in its last CTA (one launch, no
                          merge kernel).  Launches sharing it must not run
                          concurrently. */
+  int32_t cluster;    /* with merge_sem: 2..8 groups the CTAs in thread-block
+                         clusters of this many consecutive work items that
+                         merge through distributed shared memory (the single
+                         launch of the heterogeneous run_decode ABI,
+                         scripts/page_gauge_heterogeneous_fa2.py:286-379);
+                         0 or 1: last-CTA merge */
 } pg_decode_args;
 
 int32_t pg_decode_run(const pg_decode_args* args, void* stream);
+
+/* Clusters of `cluster` decode CTAs (of `warps` warps) the current GPU can
+ * hold at once: the single-launch plan fits one wave when its padded item
+ * count is at most cluster * *out.                                        */
+int32_t pg_decode_max_clusters(int32_t warps, int32_t cluster, int32_t* out);
 
 /* Allocation-free variant of pg_decode_plan + pg_decode_run (no counterpart
  * in the reference).  For callers that cannot allocate device memory - a

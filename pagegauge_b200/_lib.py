@@ -48,7 +48,7 @@ class PgDecodeArgs(ctypes.Structure):
         ("out", c_vp), ("out_stride_b", c_i64), ("out_stride_h", c_i64), ("lse_out", c_vp),
         ("extra_o", c_vp), ("extra_stride_b", c_i64), ("extra_stride_h", c_i64), ("extra_lse", c_vp),
         ("value_center", c_vp), ("vc_stride_b", c_i64), ("stage_mask", c_i32),
-        ("merge_sem", c_vp),
+        ("merge_sem", c_vp), ("cluster", c_i32),
     ]
 
 
@@ -88,6 +88,7 @@ _SIGNATURES = {
          ctypes.POINTER(PgPlanInfo)],
     ),
     "pg_decode_run": (c_i32, [ctypes.POINTER(PgDecodeArgs), c_vp]),
+    "pg_decode_max_clusters": (c_i32, [c_i32, c_i32, c_i32p]),
     "pg_decode_static": (c_i32, [ctypes.POINTER(PgDecodeArgs), c_vp, c_vp, c_i32, c_i32, c_i32, c_vp]),
     "pg_merge_state_in_place": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp]),
     "pg_add_rmsnorm": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_i32, c_i32, c_i64, c_i64, c_i64,

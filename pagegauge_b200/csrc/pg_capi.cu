@@ -153,7 +153,7 @@ int32_t ensure_decode_smem() {
 int32_t launch_decode(const pg::DecodeParams& p, const CUtensorMap& k8,
                       const CUtensorMap& v8, const CUtensorMap& k16,
                       const CUtensorMap& v16, int num_ctas, int warps,
-                      cudaStream_t stream) {
+                      cudaStream_t stream, int cluster = 1) {
   int32_t rc = ensure_decode_smem();
   if (rc != PG_OK) return rc;
   // Programmatic dependent launch: the kernel's prologue (work item, page
@@ -165,11 +165,15 @@ int32_t launch_decode(const pg::DecodeParams& p, const CUtensorMap& k8,
   cfg.blockDim = dim3(warps * 32);
   cfg.dynamicSmemBytes = pg::decode_smem_bytes(warps);
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = static_cast<unsigned>(cluster);
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = cluster > 1 ? 2 : 1;
   return cuda_check(cudaLaunchKernelEx(&cfg, pg::pg_decode_split_kernel, k8, v8, k16, v16, p),
                     "decode kernel launch");
 }
@@ -210,7 +214,7 @@ extern "C" {
 
 const char* pg_last_error(void) { return g_last_error.c_str(); }
 
-int32_t pg_abi_version(void) { return 100; }
+int32_t pg_abi_version(void) { return 101; }
 
 int32_t pg_read_device_error(int32_t* code_out) {
   int* p = device_error_ptr();
@@ -678,6 +682,12 @@ int32_t pg_decode_run(const pg_decode_args* a, void* stream) {
   p.sem = fused ? a->merge_sem : nullptr;
   p.item_off = a->item_off;
   if (fused) PG_REQUIRE(a->item_off != nullptr, "the fused merge needs item offsets");
+  PG_REQUIRE(a->cluster >= 0 && a->cluster <= 8, "cluster size must be 0..8");
+  const int cluster = (fused && a->cluster > 1) ? a->cluster : 1;
+  p.cluster = cluster;
+  if (cluster > 1) {
+    PG_REQUIRE(W >= 2, "the cluster merge needs at least 2 warps per CTA");
+  }
   if (a->extra_o != nullptr) PG_REQUIRE(a->extra_lse != nullptr, "extra state needs its lse");
 
   const int mask = (a->stage_mask & 3) == 0 ? 3 : (a->stage_mask & 3);
@@ -686,7 +696,8 @@ int32_t pg_decode_run(const pg_decode_args* a, void* stream) {
     if (!a->final_mode)
       PG_REQUIRE(a->part_o != nullptr && a->part_lse != nullptr,
                  "split decode needs a partial-state workspace");
-    int32_t rc = launch_decode(p, maps[0], maps[1], maps[2], maps[3], a->num_items, W, st);
+    const int ctas = (a->num_items + cluster - 1) / cluster * cluster;
+    int32_t rc = launch_decode(p, maps[0], maps[1], maps[2], maps[3], ctas, W, st, cluster);
     if (rc != PG_OK) return rc;
   }
   if (a->final_mode && a->num_items > 0) return PG_OK;
@@ -723,6 +734,30 @@ int32_t pg_decode_run(const pg_decode_args* a, void* stream) {
   cfg.numAttrs = 1;
   return cuda_check(cudaLaunchKernelEx(&cfg, pg::pg_merge_partials_kernel, m),
                     "merge kernel launch");
+}
+
+int32_t pg_decode_max_clusters(int32_t warps, int32_t cluster, int32_t* out) {
+  PG_REQUIRE(out != nullptr && warps >= 1 && warps <= pg::kMaxWarps && cluster >= 1 && cluster <= 8,
+             "bad arguments");
+  int32_t rc = ensure_decode_smem();
+  if (rc != PG_OK) return rc;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(cluster * 64);
+  cfg.blockDim = dim3(warps * 32);
+  cfg.dynamicSmemBytes = pg::decode_smem_bytes(warps);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(cluster);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  rc = cuda_check(cudaOccupancyMaxActiveClusters(&n, pg::pg_decode_split_kernel, &cfg),
+                  "cudaOccupancyMaxActiveClusters");
+  if (rc != PG_OK) return rc;
+  *out = n;
+  return PG_OK;
 }
 
 int32_t pg_merge_state_in_place(void* v_a, float* s_a, const void* v_b,

@@ -22,6 +22,8 @@
 // sum-exp written for a partial state is base 2 as well.
 #pragma once
 
+#include <cooperative_groups.h>
+
 #include "pg_common.cuh"
 
 namespace pg {
@@ -74,6 +76,11 @@ struct DecodeParams {
   int32_t* sem;
   const int32_t* item_off;
   int* error_flag;
+  // > 1: single launch, CTAs grouped in clusters of this many consecutive
+  // work items merge their states through distributed shared memory and
+  // the last cluster of a head finishes it (no merge kernel).  The grid is
+  // padded to whole clusters; CTAs past num_items are empty.
+  int32_t cluster;
 };
 
 constexpr int kStagesI8 = 4;              // INT8 stages per warp
@@ -909,6 +916,245 @@ __device__ __forceinline__ void merge_head(const DecodeParams& p, int r, int h,
   }
 }
 
+// Single-launch merge through thread-block clusters.  Every CTA folds its
+// warps' states into one normalised state (o, base-2 lse) in its shared
+// memory; after a cluster barrier, the cluster's first CTA reads the states
+// of its cluster (distributed shared memory) and merges each run of CTAs
+// that share a (request, KV head): a run holding all of the head's items
+// writes the final output directly, otherwise it stores one partial at the
+// run's first item index and the last cluster of the head to arrive (an
+// atomic counter per head, re-armed to zero) merges the head's cluster
+// partials.  A second cluster barrier keeps every CTA's state alive until
+// the first CTA has read it.
+// Cluster partials of one head that the finishing CTA weighs through its
+// shared-memory table; heads with more take a slower two-pass fold.
+constexpr int kClusterMaxParts = 128;
+
+__device__ __noinline__ void cluster_epilogue(const DecodeParams& p, int W, const float* cm,
+                                              const float* cl, const float* co, float* xls) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int C = static_cast<int>(cluster.num_blocks());
+  const int rank = static_cast<int>(cluster.block_rank());
+  const int group = p.group;
+  const int total = group * kHeadDim;
+  float* st_o = xls + 16;               // [group][128], this CTA's state
+  float* st_lse = st_o + 8 * kHeadDim;  // [group]
+  float* wts = st_lse + 8;              // [parts][group] merge weights
+  float* fin = wts + kClusterMaxParts * 8;  // [group] final lse
+  int* s_int = reinterpret_cast<int*>(fin + 8);  // [0] flag, [1..C] run ends
+  for (int idx = threadIdx.x; idx < total; idx += blockDim.x) {
+    const int q = idx >> 7, d = idx & 127;
+    float M = kNegInf;
+    for (int w = 0; w < W; ++w) M = fmaxf(M, cm[w * 8 + q]);
+    float L = 0.f, O = 0.f;
+    if (M != kNegInf) {
+      for (int w = 0; w < W; ++w) {
+        const float mw = cm[w * 8 + q];
+        if (mw == kNegInf) continue;
+        const float e = fast_exp2(mw - M);
+        L += cl[w * 8 + q] * e;
+        O += co[(w * 8 + q) * kCoStride + d] * e;
+      }
+    }
+    st_o[idx] = L > 0.f ? O / L : 0.f;
+    if (d == 0) st_lse[q] = L > 0.f ? M + fast_log2(L) : kNegInf;
+  }
+  cluster.sync();
+  // Turn n states' base-2 lse values (already in wts[j*group + q]) into
+  // normalised weights and write the merged lse of each row to fin[q].
+  auto weights = [&](int n) {
+    __syncthreads();
+    if (threadIdx.x < group) {
+      const int q = threadIdx.x;
+      float M = kNegInf;
+      for (int j = 0; j < n; ++j) M = fmaxf(M, wts[j * group + q]);
+      float L = 0.f;
+      if (M != kNegInf)
+        for (int j = 0; j < n; ++j) {
+          const float e = wts[j * group + q] == kNegInf ? 0.f : fast_exp2(wts[j * group + q] - M);
+          wts[j * group + q] = e;
+          L += e;
+        }
+      else
+        for (int j = 0; j < n; ++j) wts[j * group + q] = 0.f;
+      const float inv = L > 0.f ? 1.f / L : 0.f;
+      for (int j = 0; j < n; ++j) wts[j * group + q] *= inv;
+      fin[q] = L > 0.f ? M + fast_log2(L) : kNegInf;
+    }
+    __syncthreads();
+  };
+  if (rank == 0) {
+    const int base = static_cast<int>(blockIdx.x);
+    // Runs of consecutive CTAs of this cluster sharing a (request, head).
+    if (threadIdx.x == 0) {
+      int k = 0, nr = 0;
+      while (k < C && base + k < p.num_items) {
+        const DecodeItem it = p.items[base + k];
+        int k1 = k + 1;
+        while (k1 < C && base + k1 < p.num_items) {
+          const DecodeItem nx = p.items[base + k1];
+          if (nx.request != it.request || (nx.head_seg & 0xffff) != (it.head_seg & 0xffff)) break;
+          ++k1;
+        }
+        s_int[1 + nr++] = k1;
+        k = k1;
+      }
+      s_int[0] = nr;
+    }
+    __syncthreads();
+    const int nruns = s_int[0];
+    int k = 0;
+    for (int run = 0; run < nruns; ++run) {
+      const int k1 = s_int[1 + run];
+      const DecodeItem it = p.items[base + k];
+      const int r = it.request, h = it.head_seg & 0xffff;
+      const int rh = r * p.hkv + h;
+      const int i0 = p.item_off[rh], i1 = p.item_off[rh + 1];
+      const bool whole = i0 == base + k && i1 == base + k1;
+      const int n = k1 - k;
+      for (int e = threadIdx.x; e < n * group; e += blockDim.x)
+        wts[e] = cluster.map_shared_rank(st_lse, k + e / group)[e % group];
+      if (threadIdx.x < group)
+        xls[threadIdx.x] = (whole && p.extra_o != nullptr)
+                               ? p.extra_lse[static_cast<int64_t>(r) * (p.hkv * group) +
+                                             h * group + threadIdx.x]
+                               : kNegInf;
+      weights(n);
+      // Thread -> 4 consecutive dims of one row: one float4 per state.
+      for (int v = threadIdx.x; v < total / 4; v += blockDim.x) {
+        const int q = (4 * v) >> 7, d = (4 * v) & 127;
+        float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (j >= n) break;
+          const float w = wts[j * group + q];
+          const float4 o = reinterpret_cast<const float4*>(cluster.map_shared_rank(st_o, k + j))[v];
+          O.x += w * o.x; O.y += w * o.y; O.z += w * o.z; O.w += w * o.w;
+        }
+        if (whole) {
+          store_final(p, r, h, q, d + 0, O.x, fin[q], xls[q], d == 0);
+          store_final(p, r, h, q, d + 1, O.y, fin[q], xls[q], false);
+          store_final(p, r, h, q, d + 2, O.z, fin[q], xls[q], false);
+          store_final(p, r, h, q, d + 3, O.w, fin[q], xls[q], false);
+        } else {
+          const int64_t slot = static_cast<int64_t>(base + k) * group + q;
+          *reinterpret_cast<float4*>(p.part_o + slot * kHeadDim + d) = O;
+          if (d == 0) p.part_lse[slot] = fin[q];
+        }
+      }
+      if (!whole) {
+        __threadfence();
+        __syncthreads();
+        const int first_c = i0 / C, last_c = (i1 - 1) / C;
+        if (threadIdx.x == 0) {
+          const int prev = atomicAdd(p.sem + rh, 1);
+          const int last = prev == last_c - first_c;
+          if (last) p.sem[rh] = 0;  // re-armed for the next launch
+          s_int[0] = last;
+        }
+        __syncthreads();
+        if (s_int[0]) {
+          __threadfence();
+          const int parts = last_c - first_c + 1;
+          if (threadIdx.x < group)
+            xls[threadIdx.x] = p.extra_o != nullptr
+                                   ? p.extra_lse[static_cast<int64_t>(r) * (p.hkv * group) +
+                                                 h * group + threadIdx.x]
+                                   : kNegInf;
+          if (parts <= kClusterMaxParts) {
+            for (int e = threadIdx.x; e < parts * group; e += blockDim.x) {
+              const int c = first_c + e / group;
+              wts[e] = __ldcg(p.part_lse + (i0 > c * C ? i0 : c * C) * group + e % group);
+            }
+            weights(parts);
+            // Thread -> 4 consecutive dims of one row; the partials' float4
+            // loads go out 16 at a time.
+            for (int v = threadIdx.x; v < total / 4; v += blockDim.x) {
+              const int q = (4 * v) >> 7, d = (4 * v) & 127;
+              float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+              for (int j0 = 0; j0 < parts; j0 += 16) {
+                float4 o[16];
+#pragma unroll
+                for (int u = 0; u < 16; ++u) {
+                  const int c = first_c + j0 + u;
+                  const int64_t slot = static_cast<int64_t>(i0 > c * C ? i0 : c * C) * group + q;
+                  o[u] = j0 + u < parts
+                             ? __ldcg(reinterpret_cast<const float4*>(p.part_o + slot * kHeadDim + d))
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+#pragma unroll
+                for (int u = 0; u < 16; ++u) {
+                  const float w = j0 + u < parts ? wts[(j0 + u) * group + q] : 0.f;
+                  O.x += w * o[u].x; O.y += w * o[u].y; O.z += w * o[u].z; O.w += w * o[u].w;
+                }
+              }
+              store_final(p, r, h, q, d + 0, O.x, fin[q], xls[q], d == 0);
+              store_final(p, r, h, q, d + 1, O.y, fin[q], xls[q], false);
+              store_final(p, r, h, q, d + 2, O.z, fin[q], xls[q], false);
+              store_final(p, r, h, q, d + 3, O.w, fin[q], xls[q], false);
+            }
+          } else {
+            // More partials than the weight table holds (very long runs):
+            // per row, the maximum and the sum of exp2 over all partials,
+            // then each output element folds every partial.
+            __syncthreads();
+            for (int q = 0; q < group; ++q) {
+              float m = kNegInf;
+              for (int j = threadIdx.x; j < parts; j += blockDim.x) {
+                const int c = first_c + j;
+                m = fmaxf(m, __ldcg(p.part_lse + (i0 > c * C ? i0 : c * C) * group + q));
+              }
+              wts[threadIdx.x] = m;
+              __syncthreads();
+              if (threadIdx.x == 0) {
+                float mm = kNegInf;
+                for (int t2 = 0; t2 < static_cast<int>(blockDim.x); ++t2) mm = fmaxf(mm, wts[t2]);
+                fin[q] = mm;
+              }
+              __syncthreads();
+              const float M = fin[q];
+              float l = 0.f;
+              if (M != kNegInf)
+                for (int j = threadIdx.x; j < parts; j += blockDim.x) {
+                  const int c = first_c + j;
+                  const float lj = __ldcg(p.part_lse + (i0 > c * C ? i0 : c * C) * group + q);
+                  if (lj != kNegInf) l += fast_exp2(lj - M);
+                }
+              wts[threadIdx.x] = l;
+              __syncthreads();
+              if (threadIdx.x == 0) {
+                float L = 0.f;
+                for (int t2 = 0; t2 < static_cast<int>(blockDim.x); ++t2) L += wts[t2];
+                wts[kClusterMaxParts * 8 - 8 + q] = L;  // row sums after the scratch lanes
+              }
+              __syncthreads();
+            }
+            for (int idx = threadIdx.x; idx < total; idx += blockDim.x) {
+              const int q = idx >> 7, d = idx & 127;
+              const float M = fin[q], L = wts[kClusterMaxParts * 8 - 8 + q];
+              float O = 0.f;
+              if (M != kNegInf)
+                for (int j = 0; j < parts; ++j) {
+                  const int c = first_c + j;
+                  const int64_t slot = static_cast<int64_t>(i0 > c * C ? i0 : c * C) * group + q;
+                  const float lj = __ldcg(p.part_lse + slot);
+                  if (lj != kNegInf) O += fast_exp2(lj - M) * __ldcg(p.part_o + slot * kHeadDim + d);
+                }
+              store_final(p, r, h, q, d, L > 0.f ? O / L : 0.f,
+                          L > 0.f ? M + fast_log2(L) : kNegInf, xls[q], d == 0);
+            }
+          }
+        }
+        // s_int[0] (flag) is rewritten by the next run only after a barrier.
+      }
+      __syncthreads();
+      k = k1;
+    }
+  }
+  cluster.sync();
+}
+
 // 168 registers per thread at most: three 4-warp CTAs per SM (the host
 // planner's slot count assumes it).
 __global__ void __maxnreg__(168)
@@ -929,7 +1175,12 @@ __global__ void __maxnreg__(168)
   uint8_t* ring = smem + warp * kRingBytes;
 
   DecodeItem item;
-  if (p.items != nullptr) {
+  if (static_cast<int>(blockIdx.x) >= p.num_items) {
+    item.request = 0;  // cluster padding: no pages, no output
+    item.head_seg = 0;
+    item.idx_begin = 0;
+    item.count = 0;
+  } else if (p.items != nullptr) {
     item = p.items[blockIdx.x];
   } else {
     item.request = static_cast<int>(blockIdx.x) / p.hkv;
@@ -1038,6 +1289,10 @@ __global__ void __maxnreg__(168)
   if (p.final_mode && p.extra_o != nullptr && threadIdx.x < group)
     xls[threadIdx.x] = p.extra_lse[static_cast<int64_t>(r) * (p.hkv * group) + h * group + threadIdx.x];
   __syncthreads();
+  if (p.cluster > 1 && !p.final_mode) {
+    cluster_epilogue(p, W, cm, cl, co, xls);
+    return;
+  }
   const int total = group * kHeadDim;
   for (int idx = threadIdx.x; idx < total; idx += blockDim.x) {
     const int q = idx >> 7, d = idx & 127;

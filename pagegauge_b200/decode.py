@@ -73,7 +73,12 @@ class PageGaugeDecode:
     def run(self, q: torch.Tensor, key_codes, value_codes, key_scales, value_scales,
             exact_key, exact_value, value_center: torch.Tensor | None,
             out: torch.Tensor | None = None, lse: torch.Tensor | None = None,
-            sm_scale: float | None = None, fused_merge: bool = False) -> torch.Tensor:
+            sm_scale: float | None = None, fused_merge: bool = False,
+            cluster: int = 0) -> torch.Tensor:
+        """``cluster`` = 2..8 runs the decode as one launch whose CTAs merge
+        in thread-block clusters (the single-launch ABI of the reference's
+        heterogeneous path); ``fused_merge`` merges in the last CTA of each
+        head; otherwise a merge kernel follows the split kernel."""
         plan = self.work_plan
         key = None
         if out is not None:
@@ -82,7 +87,7 @@ class PageGaugeDecode:
                    exact_key.data_ptr(), exact_key.shape, exact_value.data_ptr(),
                    None if value_center is None else (value_center.data_ptr(), value_center.shape),
                    out.data_ptr(), out.shape, out.stride(), None if lse is None else lse.data_ptr(),
-                   sm_scale, fused_merge, q.dtype, out.dtype)
+                   sm_scale, fused_merge, cluster, q.dtype, out.dtype)
             if key == self._last_key:
                 _lib.check(_lib.load().pg_decode_run(self._last_args_ref, _stream(q)))
                 return out
@@ -102,7 +107,8 @@ class PageGaugeDecode:
                                          or not value_center.is_contiguous()):
             raise ValueError("value_center must be contiguous float16")
         args = launch_decode(plan, q, segs, self.sm_scale if sm_scale is None else sm_scale, out,
-                             lse, value_center=value_center, fused_merge=fused_merge)
+                             lse, value_center=value_center, fused_merge=fused_merge,
+                             cluster=cluster)
         if key is not None:
             self._last_key, self._last_args = key, args
             self._last_args_ref = ctypes.byref(args)

@@ -142,7 +142,7 @@ def check_cache(cache: torch.Tensor, name: str, dtype: torch.dtype, kv_heads: in
 def launch_decode(plan: PagedDecodePlan, q: torch.Tensor, segments, sm_scale: float,
                   out: torch.Tensor, lse: torch.Tensor | None, extra=None,
                   value_center: torch.Tensor | None = None, final_ok: bool = True,
-                  fused_merge: bool = False) -> "_lib.PgDecodeArgs":
+                  fused_merge: bool = False, cluster: int = 0) -> "_lib.PgDecodeArgs":
     """Fill the C argument block and launch split decode (+ merge); returns
     the argument block so a caller may relaunch it unchanged."""
     if q.dtype != torch.float16 or q.dim() != 3 or q.stride(2) != 1:
@@ -162,7 +162,11 @@ def launch_decode(plan: PagedDecodePlan, q: torch.Tensor, segments, sm_scale: fl
     a.part_o = plan.o_ptr
     a.part_lse = plan.lse_ptr
     a.final_mode = 1 if (final_ok and plan.single and plan.num_items > 0) else 0
-    a.merge_sem = plan.sem_ptr if fused_merge else None
+    # One launch: the last CTA of a head merges it (fused_merge), or CTAs in
+    # clusters of `cluster` work items merge through distributed shared
+    # memory and the last cluster of a head finishes it.
+    a.merge_sem = plan.sem_ptr if (fused_merge or cluster > 1) else None
+    a.cluster = cluster
     a.out = out.data_ptr()
     a.out_stride_b, a.out_stride_h = out.stride(0), out.stride(1)
     a.lse_out = None if lse is None else lse.data_ptr()

@@ -29,7 +29,8 @@ def workspace(mb=64):
     return torch.empty(mb << 20, dtype=torch.uint8, device="cuda")
 
 
-def run_fused(q, cache, tables, split_old=0, split_exact=0, warps=4, with_center=True):
+def run_fused(q, cache, tables, split_old=0, split_exact=0, warps=4, with_center=True,
+              cluster=0):
     dec = PageGaugeDecode(workspace(), warps_per_cta=warps)
     dec.plan(tables.old_indptr, tables.old_indices, tables.exact_indptr, tables.exact_indices,
              tables.exact_last_page_len, q.shape[1], cache.key_codes.shape[2],
@@ -37,7 +38,7 @@ def run_fused(q, cache, tables, split_old=0, split_exact=0, warps=4, with_center
     lse = torch.empty(q.shape[0], q.shape[1], device="cuda", dtype=torch.float32)
     out = dec.run(q, cache.key_codes, cache.value_codes, cache.key_scales, cache.value_scales,
                   cache.exact_key, cache.exact_value, cache.value_center if with_center else None,
-                  lse=lse)
+                  lse=lse, cluster=cluster)
     torch.cuda.synchronize()
     assert read_device_error() == 0
     return out, lse, dec
@@ -309,4 +310,31 @@ def test_repeated_run_relaunches_with_new_contents(cuda_lib):
     dec.run(q, *args, out=other)
     torch.cuda.synchronize()
     assert torch.equal(other, out)
+    assert read_device_error() == 0
+
+
+@pytest.mark.parametrize("cluster", [2, 3, 4, 8])
+@pytest.mark.parametrize("lengths,split", [([4096], 7), ([1000, 333, 2050], 5), ([17, 256, 257, 4095], 3),
+                                           ([49152], 0), ([5000, 300], 64)])
+def test_single_launch_cluster_merge(cuda_lib, cluster, lengths, split):
+    """One launch: CTAs merge in thread-block clusters of `cluster`
+    consecutive work items (heads split across clusters and clusters
+    spanning heads both occur), the last cluster of a head finishes it."""
+    q, dk, dv, cache, tables = make_case(lengths, seed=5 + cluster)
+    out, lse, dec = run_fused(q, cache, tables, split_old=split, split_exact=split,
+                              cluster=cluster)
+    for r in range(len(lengths)):
+        exp, exp_lse = oracle_decode(q, cache, tables, lengths, r)
+        assert_close_decode(out[r], exp)
+        np.testing.assert_allclose(cpu(lse[r]), exp_lse, atol=LSE_ATOL, rtol=0)
+    # The per-head counters are left at zero: a replay gives the same result.
+    dec.run(q, cache.key_codes, cache.value_codes, cache.key_scales, cache.value_scales,
+            cache.exact_key, cache.exact_value, cache.value_center, out=out, lse=lse,
+            cluster=cluster)
+    again = out.clone()
+    dec.run(q, cache.key_codes, cache.value_codes, cache.key_scales, cache.value_scales,
+            cache.exact_key, cache.exact_value, cache.value_center, out=out, lse=lse,
+            cluster=cluster)
+    torch.cuda.synchronize()
+    assert torch.equal(out, again)
     assert read_device_error() == 0
