@@ -401,6 +401,13 @@ class AttentionBench:
         dist.barrier()
         return dist.reduce(start.elapsed_time(end) / steps, "max")
 
+    def layer_tensors(self, layer: int):
+        """(key codes, value codes, key scales, value scales, exact key,
+        exact value, (k_bias, v_bias) or None) of one layer copy."""
+        c = self.caches[layer]
+        return (c.key_codes, c.value_codes, c.key_scales, c.value_scales, c.exact_key,
+                c.exact_value, None)
+
     def kernel_ms(self, steps: int) -> float:
         """The split-KV decode kernel alone (partials only), graphs of
         ``chunk`` launches cycling the layers, CUDA events on the replay
@@ -411,15 +418,18 @@ class AttentionBench:
         plan, dec, q, out = self.plan, self.dec, self.q, self.out
         lib = _lib.load()
         blocks = []
-        for c in self.caches:
+        for layer in range(self.layers):
+            kc, vc, ks, vs, ek, ev, affine = self.layer_tensors(layer)
             a = _lib.PgDecodeArgs()
             a.q = q.data_ptr()
             a.q_stride_b, a.q_stride_h = q.stride(0), q.stride(1)
             a.batch, a.kv_heads, a.group = plan.batch, plan.kv_heads, plan.group
             a.sm_scale = dec.sm_scale
-            a.seg[0] = W._segment(c.key_codes, c.value_codes, dec._old_indices, dec._old_last,
-                                  c.key_scales, c.value_scales)
-            a.seg[1] = W._segment(c.exact_key, c.exact_value, dec._exact_indices, dec._exact_last)
+            a.seg[0] = W._segment(kc, vc, dec._old_indices, dec._old_last, ks, vs)
+            a.seg[1] = W._segment(ek, ev, dec._exact_indices, dec._exact_last)
+            if affine is not None:
+                a.representation = 1
+                a.k_bias, a.v_bias = affine[0].data_ptr(), affine[1].data_ptr()
             a.items, a.item_off, a.num_items = plan.items_ptr, plan.off_ptr, plan.num_items
             a.warps_per_cta = plan.warps
             a.part_o, a.part_lse = plan.o_ptr, plan.lse_ptr
@@ -520,6 +530,61 @@ class AttentionBench:
         h2d = hqkv.numel() * 2
         return {"eager_ms": eager_ms, "graph_ms": graph_ms, "graph_error": err,
                 "h2d": h2d, "d2h": hout.numel() * 2, "launches_per_step": 1 + self.launches_per_step}
+
+
+class AffineBench(AttentionBench):
+    """The reference's alternative representation, affine_group16 (INT8
+    codes with an FP16 scale and bias per page, head and 16-dim group; no
+    centres), on the same workload: every completed page quantised by the
+    bulk affine quantiser, the last TAIL_PAGES pages read as plain FP16 from
+    the dense cache (the reference's exact-segments run of this
+    representation, scripts/benchmark_flashinfer_page_affine_int8.py:528-602)."""
+
+    def __init__(self, lengths, layers: int, split: int, seed: int, warps: int = 4):
+        from pagegauge_b200 import scheduler
+        from pagegauge_b200.cache import synthetic_dense_cache
+        from pagegauge_b200.decode import PageGaugeDecode, split_tables
+        from pagegauge_b200.quantize import quantize_pages
+
+        self.lengths = lengths
+        self.layers = max(1, layers)
+        self.fused, self.cluster = False, 0
+        pages = [-(-n // PAGE) for n in lengths]
+        o_ptr, o_idx, e_ptr, e_idx = split_tables(pages, TAIL_PAGES)
+        self.data = []
+        self.q = None
+        for layer in range(self.layers):
+            qi, dk, dv = synthetic_dense_cache(lengths, seed=seed + layer, device="cuda")
+            kc, kb, ks, _ = quantize_pages(dk)
+            vc, vb, vs, _ = quantize_pages(dv)
+            self.data.append((kc, vc, ks, vs, dk, dv, (kb, vb)))
+            self.q = qi if self.q is None else self.q
+        torch.cuda.synchronize()
+        if split < 0:
+            split = scheduler.lookup(len(lengths), max(lengths))
+        last = torch.tensor([(n - 1) % PAGE + 1 for n in lengths], dtype=torch.int32, device="cuda")
+        self.ws = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+        self.dec = PageGaugeDecode(self.ws, warps_per_cta=warps)
+        self.dec.plan(o_ptr, torch.from_numpy(o_idx).cuda(), e_ptr, torch.from_numpy(e_idx).cuda(),
+                      last, HQ, HKV, old_split_pages=split, exact_split_pages=0)
+        self.plan = self.dec.work_plan
+        self.out = torch.empty_like(self.q)
+        old_pages = [int(o_ptr[r + 1] - o_ptr[r]) for r in range(len(lengths))]
+        # codes (K+V) + 64 bytes of group scales/biases per (page, head) +
+        # the FP16 tail
+        self.nbytes = sum(op * HKV * (2 * PAGE * DIM + 64) + 2 * 2 * (n - op * PAGE) * HKV * DIM
+                          for op, n in zip(old_pages, lengths))
+        self.launches_per_step = 1 if (self.plan.single and self.plan.num_items) else 2
+        self.stream = torch.cuda.Stream()
+        self.chunk = 8 * self.layers
+
+    def layer_tensors(self, layer: int):
+        return self.data[layer]
+
+    def step(self, layer: int, q=None, out=None):
+        kc, vc, ks, vs, dk, dv, affine = self.data[layer]
+        self.dec.run(self.q if q is None else q, kc, vc, ks, vs, dk, dv, None,
+                     out=self.out if out is None else out, affine_bias=affine)
 
 
 class _Null:
@@ -840,6 +905,24 @@ def main() -> None:
         app["increment_pct_of_attention_step"] = round(
             100 * app["increment_us_per_step"] / app["layers"] / attn_layer_us, 2)
         workloads["append_b8_32l"] = app
+        aff = AffineBench(lengths, args.layers, args.split, seed=SEED + 1000 * rank + 900,
+                          warps=args.warps)
+        aff.capture()
+        aff_steps = max(200, args.steps // 10)
+        aff_ms = aff.time_steps(aff_steps, args.warmup, dist)
+        aff_kms = dist.reduce(aff.kernel_ms(aff_steps), "max")
+        workloads["affine_group16_" + args.workload] = {
+            "metric": f"decode-attn HBM GB/s (affine_group16, {args.workload})", "unit": "GB/s",
+            "value": round(dist.reduce(float(aff.nbytes), "sum") / (aff_ms * 1e-3) / 1e9, 2),
+            "us_per_step": aff_ms * 1e3, "steps": aff_steps, "kernel_us": aff_kms * 1e3,
+            "roofline_frac": round(aff.nbytes / (aff_kms * 1e-3) / 1e9 / peak, 4),
+            "algorithmic_bytes_per_step_per_rank": aff.nbytes,
+            "split_pages": aff.plan.split_pages[0], "work_items": aff.plan.num_items,
+            "note": "the reference's rejected representation, same kernel family; "
+                    "page_gauge is the headline",
+        }
+        del aff
+        torch.cuda.empty_cache()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -29,6 +29,8 @@
  *                                   scripts/page_gauge_heterogeneous_fa2.py:330-379
  *   pg_merge_state_in_place      <- flashinfer.merge_state_in_place
  *                                   scripts/benchmark_page_gauge_transformer.py:2300-2305
+ *   pg_quantize_affine_group16   <- quantize_pages (affine_group16)
+ *                                   scripts/benchmark_flashinfer_page_affine_int8.py:234-253
  *   pg_quantize_pages            <- quantize_completed_kv_pages
  *                                   scripts/benchmark_page_gauge_overheads.py:208-239
  *                                   and the codes/scales of quantize_page_gauge
@@ -221,6 +223,15 @@ typedef struct pg_decode_args {
                          launch of the heterogeneous run_decode ABI,
                          scripts/page_gauge_heterogeneous_fa2.py:286-379);
                          0 or 1: last-CTA merge */
+  int32_t representation; /* 0: PageGauge (seg[0] scales fp16 [pages, Hkv]);
+                             1: affine_group16 (seg[0].k_scale / v_scale are
+                             fp16 [pages, Hkv, 8] group scales, k_bias /
+                             v_bias the group biases; 16-byte aligned) -- the
+                             make_affine_wrapper run(q, (k_codes, v_codes),
+                             k_bias, k_scale, v_bias, v_scale, sm_scale) of
+                             scripts/benchmark_flashinfer_page_affine_int8.py:166-189, :567-578 */
+  const void* k_bias;
+  const void* v_bias;
 } pg_decode_args;
 
 int32_t pg_decode_run(const pg_decode_args* args, void* stream);
@@ -266,6 +277,15 @@ int32_t pg_quantize_pages(const void* key, const void* value,
                           void* value_codes, void* key_scales,
                           void* value_scales, int64_t num_pages,
                           int32_t kv_heads, int32_t rounding, void* stream);
+
+/* affine_group16 bulk quantiser (quantize_pages,
+ * scripts/benchmark_flashinfer_page_affine_int8.py:234-253), bit-exact:
+ * values fp16 [pages, 16, Hkv, 128] -> codes int8 (same shape), bias and
+ * scale fp16 [pages, Hkv, 8] (one pair per 16-dim group), reconstructed fp16
+ * (same shape as values; NULL to skip).                                   */
+int32_t pg_quantize_affine_group16(const void* values, int64_t num_pages, int32_t kv_heads,
+                                   void* codes, void* bias, void* scale, void* reconstructed,
+                                   void* stream);
 
 /* ---------------------------------------------------------------------- */
 /* Decoder-layer element-wise steps around the attention path (the Mistral   */

@@ -123,6 +123,71 @@ def quantize_page_gauge(values: np.ndarray):
     return codes, center, scales
 
 
+def quantize_pages_affine(values: np.ndarray):
+    """The reference's alternative "affine_group16" representation,
+    quantize_pages (scripts/benchmark_flashinfer_page_affine_int8.py:234-253):
+    per (page, head, 16-dim group) over the group's 16 tokens x 16 dims in
+    float32, scale = fp16(max((max - min) / 255, 2^-20)), mn = fp16(min),
+    u = clamp(rint((x - mn) / scale), 0, 255) (half to even), code = u - 128,
+    bias = fp16(mn + fp16(128 * scale)), reconstructed = fp16(fp32(code *
+    scale) + bias).  Returns (codes int8 [P,16,H,128], bias fp16 [P,H,8],
+    scale fp16 [P,H,8], reconstructed fp16 [P,16,H,128])."""
+    v = np.asarray(values, np.float16)
+    P, T, H, D = v.shape
+    G = D // 16
+    x = v.astype(np.float32).transpose(0, 2, 1, 3).reshape(P, H, T, G, 16)
+    mn = x.min(axis=(2, 4), keepdims=True)
+    mx = x.max(axis=(2, 4), keepdims=True)
+    scale = np.maximum((mx - mn) / np.float32(255.0), SCALE_FLOOR).astype(np.float16)
+    mn16 = mn.astype(np.float16)
+    s32 = scale.astype(np.float32)
+    u = np.clip(np.rint((x - mn16.astype(np.float32)) / s32), 0, 255)
+    signed = (u - 128).astype(np.int8)
+    b128 = (np.float32(128.0) * s32).astype(np.float16)
+    bias = (mn16.astype(np.float32) + b128.astype(np.float32)).astype(np.float16)
+    recon = (signed.astype(np.float32) * s32 + bias.astype(np.float32)).astype(np.float16)
+    codes = signed.reshape(P, H, T, D).transpose(0, 2, 1, 3)
+    recon = recon.reshape(P, H, T, D).transpose(0, 2, 1, 3)
+    return (np.ascontiguousarray(codes), bias.reshape(P, H, G), scale.reshape(P, H, G),
+            np.ascontiguousarray(recon))
+
+
+def affine_tokens(codes, bias, scale, ids, n_tokens):
+    """Old-page tokens of the affine_group16 representation as the reference's
+    FA2 variant rebuilds them (patch compute_qk affine branch: code -> half,
+    one half2 FMA with the group's scale and bias): fp16(z * s + b), rounded
+    once.  Returns float64 [n_tokens, Hkv, 128]."""
+    ids = np.asarray(ids, dtype=np.int64)
+    if ids.size == 0:
+        return np.zeros((0,) + codes.shape[2:])
+    z = codes[ids].astype(np.float64)                                    # [n,16,H,128]
+    s = np.repeat(scale[ids].astype(np.float64), 16, axis=-1)[:, None]  # [n,1,H,128]
+    b = np.repeat(bias[ids].astype(np.float64), 16, axis=-1)[:, None]
+    x = (z * s + b).astype(np.float16).astype(np.float64)
+    return x.reshape((-1,) + codes.shape[2:])[:n_tokens]
+
+
+def affine_decode(q, codes_k, codes_v, k_bias, k_scale, v_bias, v_scale, old_ids, old_tokens,
+                  exact_k=None, exact_v=None, exact_ids=(), exact_tokens=0, sm_scale=None):
+    """affine_group16 decode of one request (scripts/benchmark_flashinfer_page_affine_int8.py:
+    567-602): old pages rebuilt per group, optional FP16 exact segment merged
+    by LSE; no centres.  Returns (output float64 [Hq,128], lse base 2)."""
+    sm_scale = sm_scale if sm_scale is not None else 1.0 / math.sqrt(DIM)
+    hq = q.shape[0]
+    states = []
+    if old_tokens:
+        states.append(attention_state(q, affine_tokens(codes_k, k_bias, k_scale, old_ids, old_tokens),
+                                      affine_tokens(codes_v, v_bias, v_scale, old_ids, old_tokens),
+                                      sm_scale))
+    if exact_tokens:
+        states.append(attention_state(q, gather_tokens(exact_k, exact_ids, exact_tokens).astype(np.float64),
+                                      gather_tokens(exact_v, exact_ids, exact_tokens).astype(np.float64),
+                                      sm_scale))
+    if not states:
+        return np.zeros((hq, DIM)), np.full(hq, -np.inf)
+    return merge_states(states)
+
+
 # ----------------------------------------------------------------- append
 @dataclass
 class GaugeState:

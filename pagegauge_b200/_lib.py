@@ -49,6 +49,7 @@ class PgDecodeArgs(ctypes.Structure):
         ("extra_o", c_vp), ("extra_stride_b", c_i64), ("extra_stride_h", c_i64), ("extra_lse", c_vp),
         ("value_center", c_vp), ("vc_stride_b", c_i64), ("stage_mask", c_i32),
         ("merge_sem", c_vp), ("cluster", c_i32),
+        ("representation", c_i32), ("k_bias", c_vp), ("v_bias", c_vp),
     ]
 
 
@@ -101,6 +102,7 @@ _SIGNATURES = {
                                          ctypes.POINTER(c_i64), c_i32p]),
     "pg_skinny_gemm": (c_i32, [ctypes.POINTER(PgGemmArgs), c_vp]),
     "pg_quantize_pages": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, c_i64, c_i32, c_i32, c_vp]),
+    "pg_quantize_affine_group16": (c_i32, [c_vp, c_i64, c_i32, c_vp, c_vp, c_vp, c_vp, c_vp]),
 }
 
 EXPORTED = tuple(_SIGNATURES)

@@ -14,6 +14,7 @@
 #include <vector>
 
 #include "pagegauge_b200.h"
+#include "pg_affine.cuh"
 #include "pg_append.cuh"
 #include "pg_decode.cuh"
 #include "pg_decoder.cuh"
@@ -140,10 +141,16 @@ int32_t ensure_decode_smem() {
   std::lock_guard<std::mutex> lock(mu);
   if (!done[dev]) {
     int32_t rc = cuda_check(
-        cudaFuncSetAttribute(pg::pg_decode_split_kernel,
+        cudaFuncSetAttribute(pg::pg_decode_split_kernel<pg::kRepGauge>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             pg::decode_smem_bytes(pg::kMaxWarps)),
+                             pg::decode_smem_bytes_rep(pg::kRepGauge, pg::kMaxWarps)),
         "cudaFuncSetAttribute(decode smem)");
+    if (rc != PG_OK) return rc;
+    rc = cuda_check(
+        cudaFuncSetAttribute(pg::pg_decode_split_kernel<pg::kRepAffine16>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             pg::decode_smem_bytes_rep(pg::kRepAffine16, pg::kMaxWarps)),
+        "cudaFuncSetAttribute(affine decode smem)");
     if (rc != PG_OK) return rc;
     done[dev] = true;
   }
@@ -153,7 +160,7 @@ int32_t ensure_decode_smem() {
 int32_t launch_decode(const pg::DecodeParams& p, const CUtensorMap& k8,
                       const CUtensorMap& v8, const CUtensorMap& k16,
                       const CUtensorMap& v16, int num_ctas, int warps,
-                      cudaStream_t stream, int cluster = 1) {
+                      cudaStream_t stream, int cluster = 1, int rep = pg::kRepGauge) {
   int32_t rc = ensure_decode_smem();
   if (rc != PG_OK) return rc;
   // Programmatic dependent launch: the kernel's prologue (work item, page
@@ -163,7 +170,7 @@ int32_t launch_decode(const pg::DecodeParams& p, const CUtensorMap& k8,
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(num_ctas);
   cfg.blockDim = dim3(warps * 32);
-  cfg.dynamicSmemBytes = pg::decode_smem_bytes(warps);
+  cfg.dynamicSmemBytes = pg::decode_smem_bytes_rep(rep, warps);
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -174,8 +181,13 @@ int32_t launch_decode(const pg::DecodeParams& p, const CUtensorMap& k8,
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = cluster > 1 ? 2 : 1;
-  return cuda_check(cudaLaunchKernelEx(&cfg, pg::pg_decode_split_kernel, k8, v8, k16, v16, p),
-                    "decode kernel launch");
+  if (rep == pg::kRepAffine16)
+    return cuda_check(
+        cudaLaunchKernelEx(&cfg, pg::pg_decode_split_kernel<pg::kRepAffine16>, k8, v8, k16, v16, p),
+        "affine decode kernel launch");
+  return cuda_check(
+      cudaLaunchKernelEx(&cfg, pg::pg_decode_split_kernel<pg::kRepGauge>, k8, v8, k16, v16, p),
+      "decode kernel launch");
 }
 
 // Launch as a programmatic dependent of the previous kernel in the stream:
@@ -214,7 +226,7 @@ extern "C" {
 
 const char* pg_last_error(void) { return g_last_error.c_str(); }
 
-int32_t pg_abi_version(void) { return 101; }
+int32_t pg_abi_version(void) { return 102; }
 
 int32_t pg_read_device_error(int32_t* code_out) {
   int* p = device_error_ptr();
@@ -631,8 +643,12 @@ int32_t pg_decode_run(const pg_decode_args* a, void* stream) {
   PG_REQUIRE(a->out != nullptr, "output is required");
   PG_REQUIRE(a->num_items >= 0, "negative item count");
   const int W = a->warps_per_cta <= 0 ? 4 : std::min(a->warps_per_cta, pg::kMaxWarps);
+  PG_REQUIRE(a->representation == 0 || a->representation == 1,
+             "representation must be 0 (page gauge) or 1 (affine_group16)");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   pg::DecodeParams p{};
+  p.k_bias = static_cast<const __half*>(a->k_bias);
+  p.v_bias = static_cast<const __half*>(a->v_bias);
   p.q = static_cast<const __half*>(a->q);
   p.q_stride_b = a->q_stride_b;
   p.q_stride_h = a->q_stride_h;
@@ -648,6 +664,10 @@ int32_t pg_decode_run(const pg_decode_args* a, void* stream) {
     if (s == 0)
       PG_REQUIRE(sg.k_scale != nullptr && sg.v_scale != nullptr,
                  "INT8 segment needs k/v page scales");
+    if (s == 0 && a->representation == 1)
+      PG_REQUIRE(aligned(sg.k_scale, 16) && aligned(sg.v_scale, 16) && a->k_bias != nullptr &&
+                     a->v_bias != nullptr && aligned(a->k_bias, 16) && aligned(a->v_bias, 16),
+                 "affine_group16 needs 16-byte aligned [pages,Hkv,8] group scales and biases");
     int32_t rc = make_page_map(&maps[2 * s], sg.k_cache, sg.num_pages, a->kv_heads, s == 1);
     if (rc != PG_OK) return rc;
     rc = make_page_map(&maps[2 * s + 1], sg.v_cache, sg.num_pages, a->kv_heads, s == 1);
@@ -697,7 +717,8 @@ int32_t pg_decode_run(const pg_decode_args* a, void* stream) {
       PG_REQUIRE(a->part_o != nullptr && a->part_lse != nullptr,
                  "split decode needs a partial-state workspace");
     const int ctas = (a->num_items + cluster - 1) / cluster * cluster;
-    int32_t rc = launch_decode(p, maps[0], maps[1], maps[2], maps[3], ctas, W, st, cluster);
+    int32_t rc = launch_decode(p, maps[0], maps[1], maps[2], maps[3], ctas, W, st, cluster,
+                               a->representation == 1 ? pg::kRepAffine16 : pg::kRepGauge);
     if (rc != PG_OK) return rc;
   }
   if (a->final_mode && a->num_items > 0) return PG_OK;
@@ -753,7 +774,7 @@ int32_t pg_decode_max_clusters(int32_t warps, int32_t cluster, int32_t* out) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int n = 0;
-  rc = cuda_check(cudaOccupancyMaxActiveClusters(&n, pg::pg_decode_split_kernel, &cfg),
+  rc = cuda_check(cudaOccupancyMaxActiveClusters(&n, pg::pg_decode_split_kernel<pg::kRepGauge>, &cfg),
                   "cudaOccupancyMaxActiveClusters");
   if (rc != PG_OK) return rc;
   *out = n;
@@ -804,6 +825,33 @@ int32_t pg_quantize_pages(const void* key, const void* value,
   pg::pg_quantize_pages_kernel<<<static_cast<unsigned>(num_pages * kv_heads), 64, 0,
                                  static_cast<cudaStream_t>(stream)>>>(p);
   return cuda_check(cudaGetLastError(), "quantize launch");
+}
+
+int32_t pg_quantize_affine_group16(const void* values, int64_t num_pages, int32_t kv_heads,
+                                   void* codes, void* bias, void* scale, void* reconstructed,
+                                   void* stream) {
+  PG_REQUIRE(num_pages >= 0 && kv_heads > 0, "page and head counts must be positive");
+  if (num_pages == 0) return PG_OK;
+  PG_REQUIRE(num_pages * kv_heads < (int64_t(1) << 31), "too many pages");
+  PG_REQUIRE(values != nullptr && codes != nullptr && bias != nullptr && scale != nullptr,
+             "values, codes, bias and scale are required");
+  PG_REQUIRE(aligned(values, 8) && aligned(codes, 4) && aligned(bias, 2) && aligned(scale, 2) &&
+                 aligned(reconstructed, 8),
+             "tensors must be aligned");
+  pg::AffineQuantParams p{};
+  p.values = static_cast<const __half*>(values);
+  p.codes = static_cast<int8_t*>(codes);
+  p.bias = static_cast<__half*>(bias);
+  p.scale = static_cast<__half*>(scale);
+  p.recon = static_cast<__half*>(reconstructed);
+  p.num_pages = num_pages;
+  p.hkv = kv_heads;
+  const int64_t warps = num_pages * kv_heads;
+  const unsigned blocks =
+      static_cast<unsigned>((warps + pg::kAffineQuantWarps - 1) / pg::kAffineQuantWarps);
+  pg::pg_quantize_affine_kernel<<<blocks, pg::kAffineQuantWarps * 32, 0,
+                                  static_cast<cudaStream_t>(stream)>>>(p);
+  return cuda_check(cudaGetLastError(), "affine quantize launch");
 }
 
 // ------------------------------------------------ decoder layer element-wise

@@ -206,6 +206,33 @@ __device__ __forceinline__ void ldsm_x4_trans(const uint8_t* addr, uint32_t& r0,
       : "r"(smem_addr(addr)));
 }
 
+// Four 8x8 b16 matrices from shared memory (not transposed); lane l
+// supplies the address of row l%8 of matrix l/8 and receives, for matrix j,
+// the 32-bit word (l%4) of row l/4.
+__device__ __forceinline__ void ldsm_x4(const uint8_t* addr, uint32_t& r0, uint32_t& r1,
+                                        uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(smem_addr(addr)));
+}
+
+__device__ __forceinline__ uint32_t hfma2_u32(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t r;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+  return r;
+}
+
+// Untiled bulk copy global -> this CTA's shared memory, completing on bar
+// (16-byte aligned addresses, size a multiple of 16).
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
 // Programmatic dependent launch controls (no-ops when launched normally).
 __device__ __forceinline__ void pdl_wait_primary() {
   asm volatile("griddepcontrol.wait;" ::: "memory");

@@ -67,12 +67,6 @@ __host__ __device__ constexpr int gemm_smem_bytes(int nt) {
   return gemm_stages(nt) * gemm_stage_bytes(nt) + gemm_stages(nt) * 8 + 1024;
 }
 
-__device__ __forceinline__ void ldsm_x4(const uint8_t* addr, uint32_t& r0, uint32_t& r1,
-                                        uint32_t& r2, uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(smem_addr(addr)));
-}
 __device__ __forceinline__ void ldsm_x2(const uint8_t* addr, uint32_t& r0, uint32_t& r1) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];"
                : "=r"(r0), "=r"(r1)
@@ -95,15 +89,6 @@ constexpr int kGemmMaxContrib = 16;  // CTAs sharing one tile (host-checked)
 __device__ __forceinline__ void gemm_contributors(const GemmParams& p, int t, int& c0, int& c1) {
   c0 = ((t * p.kblocks + 1) * p.grid - 1) / p.total;
   c1 = (((t + 1) * p.kblocks) * p.grid - 1) / p.total;
-}
-
-__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
-                                          uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
-          "r"(smem_addr(dst)),
-      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_addr(bar))
-      : "memory");
 }
 
 // Request the packed weight block (tile, kb) and expect the whole stage,

@@ -74,11 +74,14 @@ class PageGaugeDecode:
             exact_key, exact_value, value_center: torch.Tensor | None,
             out: torch.Tensor | None = None, lse: torch.Tensor | None = None,
             sm_scale: float | None = None, fused_merge: bool = False,
-            cluster: int = 0) -> torch.Tensor:
+            cluster: int = 0, affine_bias=None) -> torch.Tensor:
         """``cluster`` = 2..8 runs the decode as one launch whose CTAs merge
         in thread-block clusters (the single-launch ABI of the reference's
         heterogeneous path); ``fused_merge`` merges in the last CTA of each
-        head; otherwise a merge kernel follows the split kernel."""
+        head; otherwise a merge kernel follows the split kernel.
+        ``affine_bias = (k_bias, v_bias)`` selects the affine_group16
+        representation for the INT8 pages: key/value_scales and the biases
+        are then [pages, Hkv, 8] (one pair per 16-dim group)."""
         plan = self.work_plan
         key = None
         if out is not None:
@@ -87,7 +90,9 @@ class PageGaugeDecode:
                    exact_key.data_ptr(), exact_key.shape, exact_value.data_ptr(),
                    None if value_center is None else (value_center.data_ptr(), value_center.shape),
                    out.data_ptr(), out.shape, out.stride(), None if lse is None else lse.data_ptr(),
-                   sm_scale, fused_merge, cluster, q.dtype, out.dtype)
+                   sm_scale, fused_merge, cluster, q.dtype, out.dtype,
+                   None if affine_bias is None else (affine_bias[0].data_ptr(),
+                                                     affine_bias[1].data_ptr()))
             if key == self._last_key:
                 _lib.check(_lib.load().pg_decode_run(self._last_args_ref, _stream(q)))
                 return out
@@ -106,9 +111,17 @@ class PageGaugeDecode:
         if value_center is not None and (value_center.dtype != torch.float16
                                          or not value_center.is_contiguous()):
             raise ValueError("value_center must be contiguous float16")
+        if affine_bias is not None:
+            shape = (key_codes.size(0), self._num_kv_heads, 8)
+            for name, t in (("key_scales", key_scales), ("value_scales", value_scales),
+                            ("k_bias", affine_bias[0]), ("v_bias", affine_bias[1])):
+                if (t.dtype != torch.float16 or not t.is_contiguous() or tuple(t.shape) != shape
+                        or t.data_ptr() % 16):
+                    raise ValueError(f"{name} must be contiguous 16-byte aligned "
+                                     f"[pages,{self._num_kv_heads},8] float16")
         args = launch_decode(plan, q, segs, self.sm_scale if sm_scale is None else sm_scale, out,
                              lse, value_center=value_center, fused_merge=fused_merge,
-                             cluster=cluster)
+                             cluster=cluster, affine_bias=affine_bias)
         if key is not None:
             self._last_key, self._last_args = key, args
             self._last_args_ref = ctypes.byref(args)

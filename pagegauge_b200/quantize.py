@@ -88,3 +88,24 @@ def quantize_page_gauge(values: torch.Tensor):
     reconstructed = (codes.float() * scale.float()[:, None, :, None]).half()
     centered = (values.float() - center.float()[None, None]).half()
     return codes, center, scale, reconstructed, centered
+
+
+def quantize_pages(values: torch.Tensor):
+    """affine_group16 representation (scripts/benchmark_flashinfer_page_affine_int8.py:234-253),
+    bit-exact: per (page, KV head, 16-dim group) an FP16 scale and bias,
+    codes = round_half_even((x - min) / scale) - 128.  Returns (codes int8
+    [pages,16,H,128], bias [pages,H,8], scale [pages,H,8], reconstructed
+    FP16 [pages,16,H,128]) like the reference."""
+    if values.ndim != 4 or values.shape[1] != PAGE or values.shape[3] != DIM:
+        raise ValueError("values must be [pages, 16, HKV, 128]")
+    if not values.is_cuda or values.dtype != torch.float16:
+        raise ValueError("values must be a CUDA float16 tensor")
+    values = values.contiguous()
+    pages, _, heads, _ = values.shape
+    codes = torch.empty(values.shape, device=values.device, dtype=torch.int8)
+    bias = torch.empty(pages, heads, DIM // 16, device=values.device, dtype=torch.float16)
+    scale = torch.empty_like(bias)
+    recon = torch.empty_like(values)
+    _lib.call("pg_quantize_affine_group16", values.data_ptr(), pages, heads, codes.data_ptr(),
+              bias.data_ptr(), scale.data_ptr(), recon.data_ptr(), _stream(values))
+    return codes, bias, scale, recon

@@ -7,6 +7,10 @@ PageGauge reference drives, backed by the sm_100a split-KV kernels.
   v_scale, sm_scale, out=, lse=, return_lse=)`` returns the *centred*
   partial output and its base-2 log-sum-exp (c_V is not added), as the
   patched FA2 kernel does.
+* ``make_affine_wrapper(flashinfer, workspace)`` replaces :166-189, the
+  "affine_group16" representation: INT8 codes with an FP16 scale and bias
+  per (page, KV head, 16-dim group); ``run(q, (k_codes, v_codes), k_bias,
+  k_scale, v_bias, v_scale, sm_scale, out=, lse=, return_lse=)``.
 * ``BatchDecodeWithPagedKVCacheWrapper(workspace, "NHD", ...)`` is the FP16
   paged decode used for the exact tail segment and the FP16 baseline.
 * ``plan(wrapper, indptr, indices, last_page_len, kv_dtype, fixed_split_pages)``
@@ -41,7 +45,10 @@ def num_sms(device: torch.device) -> int:
     return torch.cuda.get_device_properties(device).multi_processor_count
 
 
-def host_indptr(indptr: torch.Tensor) -> np.ndarray:
+def host_indptr(indptr) -> np.ndarray:
+    """A host int32 copy of a CSR indptr given as a tensor or an array."""
+    if isinstance(indptr, np.ndarray):
+        return indptr.astype(np.int32, copy=True)
     return indptr.detach().to("cpu", torch.int32).numpy().astype(np.int32, copy=True)
 
 
@@ -142,7 +149,8 @@ def check_cache(cache: torch.Tensor, name: str, dtype: torch.dtype, kv_heads: in
 def launch_decode(plan: PagedDecodePlan, q: torch.Tensor, segments, sm_scale: float,
                   out: torch.Tensor, lse: torch.Tensor | None, extra=None,
                   value_center: torch.Tensor | None = None, final_ok: bool = True,
-                  fused_merge: bool = False, cluster: int = 0) -> "_lib.PgDecodeArgs":
+                  fused_merge: bool = False, cluster: int = 0,
+                  affine_bias=None) -> "_lib.PgDecodeArgs":
     """Fill the C argument block and launch split decode (+ merge); returns
     the argument block so a caller may relaunch it unchanged."""
     if q.dtype != torch.float16 or q.dim() != 3 or q.stride(2) != 1:
@@ -178,6 +186,12 @@ def launch_decode(plan: PagedDecodePlan, q: torch.Tensor, segments, sm_scale: fl
     if value_center is not None:
         a.value_center = value_center.data_ptr()
         a.vc_stride_b = 0 if value_center.dim() == 2 else value_center.stride(0)
+    if affine_bias is not None:
+        # affine_group16: segment 0's scales are per 16-dim group, and these
+        # are the matching biases.
+        a.representation = 1
+        a.k_bias = affine_bias[0].data_ptr()
+        a.v_bias = affine_bias[1].data_ptr()
     _lib.check(_lib.load().pg_decode_run(ctypes.byref(a), _stream(q)))
     return a
 
@@ -185,7 +199,9 @@ def launch_decode(plan: PagedDecodePlan, q: torch.Tensor, segments, sm_scale: fl
 class BatchDecodeWithPagedKVCacheWrapper:
     """FlashInfer-shaped paged decode wrapper (NHD, page 16, head_dim 128).
 
-    ``page_gauge=True`` selects INT8 codes with per-(page, head) FP16 scales.
+    ``page_gauge=True`` selects INT8 codes with per-(page, head) FP16 scales;
+    ``affine_group16=True`` INT8 codes with an FP16 scale and bias per
+    (page, head, 16-dim group).
     """
 
     def __init__(self, float_workspace_buffer: torch.Tensor, kv_layout: str = "NHD",
@@ -193,7 +209,8 @@ class BatchDecodeWithPagedKVCacheWrapper:
                  paged_kv_indptr_buffer: torch.Tensor | None = None,
                  paged_kv_indices_buffer: torch.Tensor | None = None,
                  paged_kv_last_page_len_buffer: torch.Tensor | None = None,
-                 backend: str = "auto", jit_args=None, page_gauge: bool = False, **_ignored):
+                 backend: str = "auto", jit_args=None, page_gauge: bool = False,
+                 affine_group16: bool = False, **_ignored):
         if kv_layout != "NHD":
             raise ValueError("only the NHD page layout is supported")
         self._ws = _Workspace(float_workspace_buffer)
@@ -204,12 +221,15 @@ class BatchDecodeWithPagedKVCacheWrapper:
         self._paged_kv_indptr_buf = paged_kv_indptr_buffer
         self._paged_kv_indices_buf = paged_kv_indices_buffer
         self._paged_kv_last_page_len_buf = paged_kv_last_page_len_buffer
-        self.page_gauge = bool(page_gauge)
+        if page_gauge and affine_group16:
+            raise ValueError("choose one INT8 representation")
+        self.affine_group16 = bool(affine_group16)
+        self.page_gauge = bool(page_gauge) or self.affine_group16  # INT8 segment
         self._plan: PagedDecodePlan | None = None
         self._indices: torch.Tensor | None = None
         self._last_len: torch.Tensor | None = None
         self._sm_scale = 1.0 / math.sqrt(HEAD_DIM)
-        self._kv_dtype = torch.int8 if page_gauge else torch.float16
+        self._kv_dtype = torch.int8 if self.page_gauge else torch.float16
         self.plan_invocations = 0
 
     @property
@@ -290,7 +310,23 @@ class BatchDecodeWithPagedKVCacheWrapper:
         k_cache, v_cache = paged_kv_cache
         sm_scale = self._sm_scale
         k_page_scale = v_page_scale = None
-        if self.page_gauge:
+        affine_bias = None
+        if self.affine_group16:
+            # make_affine_wrapper's run(q, kv, k_bias, k_scale, v_bias, v_scale, sm_scale)
+            if len(args) < 4:
+                raise ValueError("affine run needs k_bias, k_scale, v_bias and v_scale")
+            k_bias, k_page_scale, v_bias, v_page_scale = args[:4]
+            if len(args) >= 5:
+                sm_scale = float(args[4])
+            shape = (k_cache.size(0), self._num_kv_heads, HEAD_DIM // 16)
+            for name, t in (("k_bias", k_bias), ("k_scale", k_page_scale), ("v_bias", v_bias),
+                            ("v_scale", v_page_scale)):
+                if (not t.is_cuda or t.dtype != torch.float16 or not t.is_contiguous()
+                        or tuple(t.shape) != shape or t.data_ptr() % 16):
+                    raise ValueError(f"{name} must be contiguous 16-byte aligned CUDA "
+                                     f"[pages,{self._num_kv_heads},8] float16")
+            affine_bias = (k_bias, v_bias)
+        elif self.page_gauge:
             if len(args) < 2:
                 raise ValueError("page-gauge run needs k_page_scale and v_page_scale")
             k_page_scale, v_page_scale = args[0], args[1]
@@ -313,7 +349,7 @@ class BatchDecodeWithPagedKVCacheWrapper:
             lse = torch.empty(batch, self._num_qo_heads, device=q.device, dtype=torch.float32)
         seg = _segment(k_cache, v_cache, self._indices, self._last_len, k_page_scale, v_page_scale)
         segments = (seg, None) if self.page_gauge else (None, seg)
-        launch_decode(self._plan, q, segments, sm_scale, out, lse)
+        launch_decode(self._plan, q, segments, sm_scale, out, lse, affine_bias=affine_bias)
         return (out, lse) if return_lse else out
 
     forward = run
@@ -328,6 +364,19 @@ def make_page_gauge_wrapper(flashinfer=None, workspace: torch.Tensor | None = No
     wrapper_kwargs.pop("jit_args", None)
     wrapper = BatchDecodeWithPagedKVCacheWrapper(workspace, "NHD", page_gauge=True, **wrapper_kwargs)
     wrapper.page_gauge_module_uri = "pagegauge_b200.sm100a.page_affine_int8"
+    return wrapper
+
+
+def make_affine_wrapper(flashinfer=None, workspace: torch.Tensor | None = None,
+                        **wrapper_kwargs) -> BatchDecodeWithPagedKVCacheWrapper:
+    """scripts/benchmark_flashinfer_page_affine_int8.py:166-189: the
+    affine_group16 decode (the ``flashinfer`` argument is ignored)."""
+    if workspace is None:
+        raise ValueError("a CUDA uint8 workspace is required")
+    wrapper_kwargs.pop("jit_args", None)
+    wrapper = BatchDecodeWithPagedKVCacheWrapper(workspace, "NHD", affine_group16=True,
+                                                 **wrapper_kwargs)
+    wrapper.page_gauge_module_uri = "pagegauge_b200.sm100a.page_affine_int8_group16"
     return wrapper
 
 

@@ -128,6 +128,22 @@ def main() -> None:
             flat[f"t{t}_{key_name}"] = arr
     np.savez_compressed(HERE / "tail_merge.npz", **flat)
 
+    # 6. affine_group16 quantize_pages (scripts/benchmark_flashinfer_page_affine_int8.py:234-253):
+    # random pages, a constant page (scale floor) and a page of exact
+    # half-step ties (round half to even).
+    g = torch.Generator().manual_seed(20261003)
+    values = torch.randn(4, 16, 8, 128, generator=g) * 0.35
+    values[1] = 0.75
+    ramp = torch.arange(16 * 128, dtype=torch.float32).remainder(256).reshape(16, 128) * 0.125
+    values[2] = ramp[:, None, :] + 0.0625  # (x - min) / (1/8) lands on k + 0.5
+    values[2, 0, :, :] = 0.0
+    values[2, 1, :, :] = 255 * 0.125
+    values = values.half()
+    a_codes, a_bias, a_scale, a_recon = affine.quantize_pages(values)
+    np.savez_compressed(HERE / "quantize_affine_group16.npz", values=values.numpy(),
+                        codes=a_codes.numpy(), bias=a_bias.numpy(), scale=a_scale.numpy(),
+                        reconstructed=a_recon.numpy())
+
     # 5. Page-table helpers (scripts/benchmark_page_gauge_transformer.py:383-667;
     # scripts/benchmark_flashinfer_page_affine_int8.py:392-420).
     tables = {"segment_page_table": [], "request_major_page_table": [],

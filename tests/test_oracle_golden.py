@@ -152,3 +152,32 @@ def test_attention_oracle_segments_equal_dense_reconstruction():
     # softmax unchanged up to the constant row offset.
     shifted, _ = O.attention_state(q, keys + center_k.astype(np.float64)[None], vals, 128 ** -0.5)
     np.testing.assert_allclose(shifted + np.repeat(center_v.astype(np.float64), 4, axis=0), dense, atol=1e-10)
+
+
+def test_affine_group16_quantiser_bit_exact_against_reference():
+    """quantize_pages (scripts/benchmark_flashinfer_page_affine_int8.py:234-253),
+    run by the reference on CPU: random pages, a constant page (scale
+    floor) and a page of exact half-step ties (half to even)."""
+    g = np.load(GOLDEN / "quantize_affine_group16.npz")
+    codes, bias, scale, recon = O.quantize_pages_affine(g["values"])
+    np.testing.assert_array_equal(codes, g["codes"])
+    np.testing.assert_array_equal(bias.view(np.uint16), g["bias"].view(np.uint16))
+    np.testing.assert_array_equal(scale.view(np.uint16), g["scale"].view(np.uint16))
+    np.testing.assert_array_equal(recon.view(np.uint16), g["reconstructed"].view(np.uint16))
+    # The tie page really has ties: (x - min) / scale = k + 0.5 exactly.
+    x = g["values"][2].astype(np.float32)
+    assert np.any(np.mod(x / np.float32(0.125), 1) == 0.5)
+    assert np.all(scale[1] == np.float16(2.0**-20))
+
+
+def test_affine_tokens_match_the_reference_reconstruction():
+    """The decode oracle's single-rounding rebuild fp16(z*s+b) equals the
+    reference's fp32 product + add + fp16 cast except where the two roundings
+    differ (at most one FP16 step)."""
+    g = np.load(GOLDEN / "quantize_affine_group16.npz")
+    ids = [0, 3, 1]
+    got = O.affine_tokens(g["codes"], g["bias"], g["scale"], ids, 40)
+    ref = g["reconstructed"][ids].reshape(-1, 8, 128)[:40].astype(np.float64)
+    step = np.abs(ref) * 2.0 ** -10 + 2.0 ** -24
+    assert np.all(np.abs(got - ref) <= step)
+    assert np.mean(got == ref) > 0.99
