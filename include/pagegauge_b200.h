@@ -138,6 +138,35 @@ int32_t pg_rope_append_page_gauge_batched(
     int64_t exact_sink_pages, const int32_t* positions,
     int64_t rope_row_stride, int64_t rope_rows, void* stream);
 
+/* The fused append on the served pool layout (the device side of the
+ * serving decode metadata, experiments/mlsys2027/serving_v1/pagegauge_vllm/
+ * decode_metadata.py:28-35, whose columns are "for a future device ABI"):
+ * per batch row r, positions[r], token_slots[r] = physical code page * 16 +
+ * token (pool planes [num_code_pages, 16, Hkv, 128]), exact_slots[r] = exact
+ * sidecar page * 16 + token ([num_exact_pages, 16, Hkv, 128], centred FP16)
+ * and center_rows[r] = the request's lease slot in the centre sidecars
+ * [num_centers, Hkv, 128].  A closing page's codes go to its physical code
+ * page; the row's value centre is copied to value_center_out [B, Hkv, 128]
+ * for the decode.  Rows whose slots disagree with their position or fall
+ * outside the pool are skipped and reported (PG_DEV_BAD_PAGE_ID).          */
+int32_t pg_rope_append_page_gauge_served(
+    const void* query, const void* key, const void* value, const void* cosine,
+    const void* sine, const void* key_center, const void* value_center,
+    void* rotated_query, void* exact_key_pages, void* exact_value_pages, void* key_codes,
+    void* value_codes, void* key_scales, void* value_scales, void* value_center_out,
+    int64_t query_batch_stride, int64_t key_batch_stride, int64_t value_batch_stride,
+    int32_t batch, int32_t query_heads, int32_t kv_heads, int64_t num_code_pages,
+    int64_t num_exact_pages, int64_t num_centers, const int32_t* positions,
+    const int32_t* token_slots, const int32_t* exact_slots, const int32_t* center_rows,
+    int64_t rope_row_stride, int64_t rope_rows, void* stream);
+
+/* Zero the four planes of `count` pool pages (page_ids device int32), the
+ * served pool's zero_physical_pages
+ * (experiments/mlsys2027/serving_v1/pagegauge_vllm/cache_views.py:42-62). */
+int32_t pg_zero_pool_pages(void* key_codes, void* value_codes, void* key_scales,
+                           void* value_scales, int64_t num_pages, int32_t kv_heads,
+                           const int32_t* page_ids, int32_t count, void* stream);
+
 /* Exact FP16 tail attention merged into (old_output, old_lse) in place,
  * plus the value centre.  exact_page_indices [B*n] int32,
  * exact_last_page_len [B] int32 (device), old_lse base 2 [B,Hq].          */

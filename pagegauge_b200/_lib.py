@@ -78,6 +78,10 @@ _SIGNATURES = {
         c_i32,
         [c_vp] * 14 + [c_i64] * 4 + [c_i32] * 3 + [c_i64] * 3 + [c_vp, c_i64, c_i64, c_vp],
     ),
+    "pg_rope_append_page_gauge_served": (
+        c_i32, [c_vp] * 15 + [c_i64] * 3 + [c_i32] * 3 + [c_i64] * 3 + [c_vp] * 4 + [c_i64, c_i64, c_vp],
+    ),
+    "pg_zero_pool_pages": (c_i32, [c_vp] * 4 + [c_i64, c_i32, c_vp, c_i32, c_vp]),
     "pg_exact_tail_merge_center": (
         c_i32,
         [c_vp, c_vp, c_vp, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, c_i64, c_i32, c_i32, c_i32,

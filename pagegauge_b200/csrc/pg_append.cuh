@@ -53,6 +53,16 @@ struct AppendParams {
   int64_t exact_sink_pages;
   int64_t code_pages_per_request;
   int* error_flag;
+  // Served pool layout (the served kernel instantiation only): per batch
+  // row the physical token slot in the code pool (page * 16 + token), the
+  // token slot in the exact sidecar and the centre row (the request's
+  // lease slot); the row's value centre is also copied to center_out
+  // [B, Hkv, 128] for the decode's c_V.
+  const int32_t* token_slots;
+  const int32_t* exact_slots;
+  const int32_t* center_rows;
+  __half* center_out;
+  int64_t num_code_pages, num_exact_pages, num_centers;
 };
 
 __device__ __forceinline__ uint32_t hmul2_rn(uint32_t a, uint32_t b) {
@@ -294,6 +304,10 @@ __device__ __forceinline__ uint2 quantize_half8(const uint4& v, float scale, flo
 // the position is known (in parallel with the RoPE work), the new token
 // comes through shared memory; the CTA reduces the two abs-maxima, and each
 // thread quantises and writes its 8 + 8 codes (8-byte stores).
+// SERVED: pages addressed through the served pool's per-row slots
+// (token_slots / exact_slots / center_rows) instead of the request-major
+// layout.
+template <bool SERVED>
 __global__ void __launch_bounds__(kAppendThreads)
     pg_rope_append_page_gauge_kernel(const __grid_constant__ AppendParams p) {
   __shared__ float red[2][kAppendThreads / 32];
@@ -309,9 +323,17 @@ __global__ void __launch_bounds__(kAppendThreads)
   const int h = blockIdx.x % p.hkv;
   const int g = threadIdx.x >> 6, j = threadIdx.x & 63;
   const AppendInputs in = load_append_inputs(p, r, h, g, j);
+  int64_t crow = r;
+  if constexpr (SERVED) {
+    crow = __ldg(p.center_rows + r);
+    if (crow < 0 || crow >= p.num_centers) {
+      if (threadIdx.x == 0) record_error(p.error_flag, kDevBadPageId);
+      return;
+    }
+  }
   uint32_t center = 0u;
   if (g < 2) {
-    const int64_t cofs = r * p.center_stride_b + static_cast<int64_t>(h) * kHeadDim;
+    const int64_t cofs = crow * p.center_stride_b + static_cast<int64_t>(h) * kHeadDim;
     center = reinterpret_cast<const uint32_t*>((g == 0 ? p.key_center : p.value_center) + cofs)[j];
   }
   int64_t pos;
@@ -327,10 +349,26 @@ __global__ void __launch_bounds__(kAppendThreads)
 
   const int page = static_cast<int>(pos / kPage);
   const int token = static_cast<int>(pos % kPage);
-  const int sink = static_cast<int>(p.exact_sink_pages);
-  const int tail_pages = static_cast<int>(p.exact_pages_per_request) - sink;
-  const int local = page < sink ? page : sink + page % tail_pages;
-  const int64_t ring_page = r * p.exact_pages_per_request + local;
+  int64_t ring_page, code_page;
+  if constexpr (SERVED) {
+    const int32_t ts = __ldg(p.token_slots + r), es = __ldg(p.exact_slots + r);
+    if (ts < 0 || es < 0 || (ts & (kPage - 1)) != token || (es & (kPage - 1)) != token ||
+        (ts >> 4) >= p.num_code_pages || (es >> 4) >= p.num_exact_pages) {
+      if (threadIdx.x == 0) record_error(p.error_flag, kDevBadPageId);
+      return;
+    }
+    ring_page = es >> 4;
+    code_page = ts >> 4;
+    if (g == 1)
+      reinterpret_cast<uint32_t*>(p.center_out +
+                                  (static_cast<int64_t>(r) * p.hkv + h) * kHeadDim)[j] = center;
+  } else {
+    const int sink = static_cast<int>(p.exact_sink_pages);
+    const int tail_pages = static_cast<int>(p.exact_pages_per_request) - sink;
+    const int local = page < sink ? page : sink + page % tail_pages;
+    ring_page = r * p.exact_pages_per_request + local;
+    code_page = r * p.code_pages_per_request + page;
+  }
   const int64_t row_stride = static_cast<int64_t>(p.hkv) * kHeadDim;  // per token
   __half* kring = p.key_pages + (ring_page * kPage * p.hkv + h) * kHeadDim;
   __half* vring = p.value_pages + (ring_page * kPage * p.hkv + h) * kHeadDim;
@@ -373,13 +411,37 @@ __global__ void __launch_bounds__(kAppendThreads)
   }
   const __half ks_h = __float2half_rn(fmaxf(__fdiv_rn(km, 127.f), 0x1p-20f));
   const __half vs_h = __float2half_rn(fmaxf(__fdiv_rn(vm, 127.f), 0x1p-20f));
-  const int64_t code_page = r * p.code_pages_per_request + page;
   if (threadIdx.x == 0) p.key_scales[code_page * p.hkv + h] = ks_h;
   if (threadIdx.x == 1) p.value_scales[code_page * p.hkv + h] = vs_h;
   const int64_t cbase = (code_page * kPage * p.hkv + h) * kHeadDim + tk * row_stride + col;
   const float ksf = __half2float(ks_h), vsf = __half2float(vs_h);
   *reinterpret_cast<uint2*>(p.key_codes + cbase) = quantize_half8(kx, ksf, __frcp_rn(ksf));
   *reinterpret_cast<uint2*>(p.value_codes + cbase) = quantize_half8(vx, vsf, __frcp_rn(vsf));
+}
+
+// Zero the four planes (K/V codes, K/V scales) of the listed pool pages:
+// one CTA per listed page; ids outside the pool are skipped and reported.
+__global__ void __launch_bounds__(256)
+    pg_zero_pool_pages_kernel(int8_t* key_codes, int8_t* value_codes, __half* key_scales,
+                              __half* value_scales, int64_t num_pages, int32_t hkv,
+                              const int32_t* page_ids, int* error_flag) {
+  const int32_t id = __ldg(page_ids + blockIdx.x);
+  if (id < 0 || id >= num_pages) {
+    if (threadIdx.x == 0) record_error(error_flag, kDevBadPageId);
+    return;
+  }
+  const int64_t chunks = static_cast<int64_t>(kPage) * hkv * kHeadDim / 16;
+  uint4* kc = reinterpret_cast<uint4*>(key_codes + static_cast<int64_t>(id) * chunks * 16);
+  uint4* vc = reinterpret_cast<uint4*>(value_codes + static_cast<int64_t>(id) * chunks * 16);
+  const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+  for (int64_t i = threadIdx.x; i < chunks; i += blockDim.x) {
+    kc[i] = z;
+    vc[i] = z;
+  }
+  if (threadIdx.x < hkv) {
+    key_scales[static_cast<int64_t>(id) * hkv + threadIdx.x] = __float2half_rn(0.f);
+    value_scales[static_cast<int64_t>(id) * hkv + threadIdx.x] = __float2half_rn(0.f);
+  }
 }
 
 // ------------------------------------------------ bulk page quantisation

@@ -417,7 +417,7 @@ static int32_t append_page_gauge_impl(
   p.exact_sink_pages = exact_sink_pages;
   p.code_pages_per_request = code_ppr;
   p.error_flag = device_error_ptr();
-  return launch_pdl(pg::pg_rope_append_page_gauge_kernel, dim3(batch * kv_heads),
+  return launch_pdl(pg::pg_rope_append_page_gauge_kernel<false>, dim3(batch * kv_heads),
                     dim3(pg::kAppendThreads), 0, static_cast<cudaStream_t>(stream),
                     "rope_append_page_gauge launch", p);
 }
@@ -440,6 +440,97 @@ int32_t pg_rope_append_page_gauge(
       query_batch_stride, key_batch_stride, value_batch_stride, center_batch_stride, batch,
       query_heads, kv_heads, exact_pages, code_pages, exact_sink_pages, position,
       device_position, 0, rope_row_stride, rope_rows, stream);
+}
+
+int32_t pg_rope_append_page_gauge_served(
+    const void* query, const void* key, const void* value, const void* cosine,
+    const void* sine, const void* key_center, const void* value_center,
+    void* rotated_query, void* exact_key_pages, void* exact_value_pages, void* key_codes,
+    void* value_codes, void* key_scales, void* value_scales, void* value_center_out,
+    int64_t query_batch_stride, int64_t key_batch_stride, int64_t value_batch_stride,
+    int32_t batch, int32_t query_heads, int32_t kv_heads, int64_t num_code_pages,
+    int64_t num_exact_pages, int64_t num_centers, const int32_t* positions,
+    const int32_t* token_slots, const int32_t* exact_slots, const int32_t* center_rows,
+    int64_t rope_row_stride, int64_t rope_rows, void* stream) {
+  PG_REQUIRE(batch > 0, "Q/K/V batch sizes must match and be positive");
+  PG_REQUIRE(query_heads > 0 && kv_heads > 0 && query_heads % kv_heads == 0,
+             "head counts must be positive with Hq a multiple of Hkv");
+  PG_REQUIRE(positions != nullptr && token_slots != nullptr && exact_slots != nullptr &&
+                 center_rows != nullptr,
+             "served append needs device positions, token slots, exact slots and centre rows");
+  PG_REQUIRE(value_center_out != nullptr, "served append needs the per-row value centre output");
+  PG_REQUIRE(rope_rows > 0, "dynamic RoPE tables must be matching [positions,128] tensors");
+  PG_REQUIRE(num_code_pages > 0 && num_exact_pages > 0 && num_centers > 0,
+             "pool, sidecar and centre counts must be positive");
+  PG_REQUIRE(num_code_pages < (int64_t(1) << 27) && num_exact_pages < (int64_t(1) << 27),
+             "pool page count out of range");
+  PG_REQUIRE(aligned(query, 4) && aligned(key, 4) && aligned(value, 4) && aligned(cosine, 4) &&
+                 aligned(sine, 4) && aligned(key_center, 4) && aligned(value_center, 4) &&
+                 aligned(rotated_query, 4) && aligned(value_center_out, 4),
+             "tensors must be 4-byte aligned");
+  PG_REQUIRE(aligned(exact_key_pages, 16) && aligned(exact_value_pages, 16) &&
+                 aligned(key_codes, 8) && aligned(value_codes, 8),
+             "exact pages must be 16-byte and INT8 codes 8-byte aligned");
+  PG_REQUIRE(query_batch_stride % 2 == 0 && key_batch_stride % 2 == 0 &&
+                 value_batch_stride % 2 == 0 && rope_row_stride % 2 == 0,
+             "batch strides must be even");
+  pg::AppendParams p{};
+  p.q = static_cast<const __half*>(query);
+  p.k = static_cast<const __half*>(key);
+  p.v = static_cast<const __half*>(value);
+  p.q_stride_b = query_batch_stride;
+  p.k_stride_b = key_batch_stride;
+  p.v_stride_b = value_batch_stride;
+  p.cos = static_cast<const __half*>(cosine);
+  p.sin = static_cast<const __half*>(sine);
+  p.device_position = positions;
+  p.position_stride = 1;
+  p.rope_row_stride = rope_row_stride;
+  p.rope_rows = rope_rows;
+  p.rotated_q = static_cast<__half*>(rotated_query);
+  p.key_pages = static_cast<__half*>(exact_key_pages);
+  p.value_pages = static_cast<__half*>(exact_value_pages);
+  p.key_center = static_cast<const __half*>(key_center);
+  p.value_center = static_cast<const __half*>(value_center);
+  p.center_stride_b = static_cast<int64_t>(kv_heads) * pg::kHeadDim;
+  p.key_codes = static_cast<int8_t*>(key_codes);
+  p.value_codes = static_cast<int8_t*>(value_codes);
+  p.key_scales = static_cast<__half*>(key_scales);
+  p.value_scales = static_cast<__half*>(value_scales);
+  p.batch = batch;
+  p.hq = query_heads;
+  p.hkv = kv_heads;
+  // Positions are bounded by the RoPE table only; the slots carry the pages.
+  p.code_pages_per_request = (int64_t(1) << 40);
+  p.error_flag = device_error_ptr();
+  p.token_slots = token_slots;
+  p.exact_slots = exact_slots;
+  p.center_rows = center_rows;
+  p.center_out = static_cast<__half*>(value_center_out);
+  p.num_code_pages = num_code_pages;
+  p.num_exact_pages = num_exact_pages;
+  p.num_centers = num_centers;
+  return launch_pdl(pg::pg_rope_append_page_gauge_kernel<true>, dim3(batch * kv_heads),
+                    dim3(pg::kAppendThreads), 0, static_cast<cudaStream_t>(stream),
+                    "served rope_append_page_gauge launch", p);
+}
+
+int32_t pg_zero_pool_pages(void* key_codes, void* value_codes, void* key_scales,
+                           void* value_scales, int64_t num_pages, int32_t kv_heads,
+                           const int32_t* page_ids, int32_t count, void* stream) {
+  PG_REQUIRE(count >= 0 && num_pages > 0 && kv_heads > 0 && kv_heads <= 256,
+             "page counts must be positive and kv_heads in 1..256");
+  if (count == 0) return PG_OK;
+  PG_REQUIRE(page_ids != nullptr, "page ids are required");
+  PG_REQUIRE(aligned(key_codes, 16) && aligned(value_codes, 16) && aligned(key_scales, 2) &&
+                 aligned(value_scales, 2),
+             "code planes must be 16-byte aligned");
+  pg::pg_zero_pool_pages_kernel<<<static_cast<unsigned>(count), 256, 0,
+                                  static_cast<cudaStream_t>(stream)>>>(
+      static_cast<int8_t*>(key_codes), static_cast<int8_t*>(value_codes),
+      static_cast<__half*>(key_scales), static_cast<__half*>(value_scales), num_pages, kv_heads,
+      page_ids, device_error_ptr());
+  return cuda_check(cudaGetLastError(), "zero pool pages launch");
 }
 
 int32_t pg_rope_append_page_gauge_batched(
