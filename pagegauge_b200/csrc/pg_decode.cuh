@@ -174,6 +174,20 @@ __device__ __forceinline__ void load_window_set(const DecodeParams& p,
   }
 }
 
+// The V/K scales of a window set whose page ids are already loaded (the
+// ids gate the first tile copies; the scales are only needed once the
+// first tiles have landed, so they are requested after those copies).
+__device__ __forceinline__ void load_window_scales(const DecodeParams& p, const SegmentDesc& sd,
+                                                   int n_w, int h, int first, int lane, int id,
+                                                   float& sk, float& sv) {
+  sk = 0.f;
+  sv = 0.f;
+  if (first + lane < n_w) {
+    sk = __half2float(sd.k_scale[static_cast<int64_t>(id) * p.hkv + h]);
+    sv = __half2float(sd.v_scale[static_cast<int64_t>(id) * p.hkv + h]);
+  }
+}
+
 __device__ __forceinline__ int win_id(const PageWindow& w, int u) {
   const int k = u - w.base;
   const int a = __shfl_sync(0xffffffffu, w.id_a, k & 31);
@@ -591,12 +605,13 @@ __device__ __forceinline__ bool run_warp_pages_int8(
   PageWindow win;
   win.base = 0;
   win.two = n_w > 32;
-  load_window_set<0>(p, sd, idx_begin, warp, W, n_w, h, 0, lane, win.id_a, win.sk_a,
+  // Page ids first: they gate the prologue's tile copies.
+  load_window_set<1>(p, sd, idx_begin, warp, W, n_w, h, 0, lane, win.id_a, win.sk_a,
                      win.sv_a);
   win.id_b = 0;
   win.sk_b = win.sv_b = 0.f;
   if (win.two)
-    load_window_set<0>(p, sd, idx_begin, warp, W, n_w, h, 32, lane, win.id_b, win.sk_b,
+    load_window_set<1>(p, sd, idx_begin, warp, W, n_w, h, 32, lane, win.id_b, win.sk_b,
                        win.sv_b);
 
   // Prologue: pairs 0 and 1 (pages 0-3).
@@ -610,6 +625,9 @@ __device__ __forceinline__ bool run_warp_pages_int8(
       if (lane == 0) issue_pair_int8(tk, tv, ring + q * 8192, bars + q, n, id0, id1, h);
     }
   }
+  // The scales travel while the first tiles are in flight.
+  load_window_scales(p, sd, n_w, h, 0, lane, win.id_a, win.sk_a, win.sv_a);
+  if (win.two) load_window_scales(p, sd, n_w, h, 32, lane, win.id_b, win.sk_b, win.sv_b);
 
   uint32_t vaddr[4];
   {
