@@ -24,9 +24,13 @@ PAGE = 16
 
 
 def bucket(batch: int, context: int) -> str:
-    """Batch exact, context rounded down to a power of two (>= 1024): a
-    bucket c covers contexts [c, 2c)."""
-    c = 1 << max(10, int(math.floor(math.log2(max(context, 1)))))
+    """Batch exact, context rounded down to a half octave (2^k or 1.5 * 2^k,
+    >= 1024): bucket 2^k covers [2^k, 1.5 * 2^k), bucket 1.5 * 2^k covers
+    [1.5 * 2^k, 2^(k+1))."""
+    k = max(10, int(math.floor(math.log2(max(context, 1)))))
+    c = 1 << k
+    if k >= 11 and context >= c + c // 2:
+        c += c // 2
     return f"b{batch}_c{c}"
 
 
@@ -66,19 +70,24 @@ def record(batch: int, context: int, results: dict[int, float], path: Path = TAB
 
 def sweep(batch: int, context: int, repeats: int = 30, seeds=(20261001, 20261002, 20261003),
           write: bool = True, path: Path = TABLE_PATH, lengths: list[int] | None = None,
-          burst: int = 16) -> dict[int, float]:
+          burst: int = 16, mode: str = "steady", layers: int = 4) -> dict[int, float]:
     """Time every candidate split on the current GPU and record the winner.
 
-    Each candidate's decode (split kernel + merge) is captured in a CUDA
-    graph behind a 256 MiB scrub (so every step starts from a cold L2); a
-    sample replays that graph ``burst`` times between CUDA events, minus
-    the same burst of a scrub-only graph, divided by ``burst`` (one replay
-    alone is below the event timer's resolution).  The p50 over
-    ``repeats`` samples per seed is averaged over the seeds.  ``lengths``
-    (default ``[context] * batch``) gives ragged batches; the table bucket
-    is (batch, max length)."""
+    ``mode="steady"`` (the default): ``layers`` caches of the shape (more
+    bytes than the 126 MB L2 together) decoded back to back in a CUDA
+    graph of ``8 * layers`` steps cycling the caches, as a decoder runs its
+    layers (each launch overlaps its start-up with the previous step's tail
+    through programmatic dependent launch); a sample is one replay between
+    CUDA events divided by its steps.  ``mode="burst"``: each candidate's
+    decode behind a 256 MiB scrub in one graph, ``burst`` replays minus the
+    same burst of a scrub-only graph (every step starts from a cold L2 and
+    an idle GPU).  The p50 over ``repeats`` samples per seed is averaged
+    over the seeds.  ``lengths`` (default ``[context] * batch``) gives
+    ragged batches; the table bucket is (batch, max length)."""
     import torch
 
+    if mode == "steady":
+        return _sweep_steady(batch, context, repeats, seeds, write, path, lengths, layers)
     from .cache import build_gauge_cache, synthetic_dense_cache
     from .decode import PageGaugeDecode
 
@@ -149,6 +158,68 @@ def sweep(batch: int, context: int, repeats: int = 30, seeds=(20261001, 20261002
     return p50
 
 
+def _sweep_steady(batch, context, repeats, seeds, write, path, lengths, layers):
+    import torch
+
+    from .cache import build_gauge_cache, synthetic_dense_cache
+    from .decode import PageGaugeDecode
+
+    lengths = list(lengths) if lengths is not None else [context] * batch
+    batch, context = len(lengths), max(lengths)
+    ws = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.Stream()
+    results: dict[int, list[float]] = {}
+    chunk = 8 * layers
+    for seed in seeds:
+        caches = []
+        for layer in range(layers):
+            q, dk, dv = synthetic_dense_cache(lengths, seed=seed + 7919 * layer, device="cuda")
+            cache, tables = build_gauge_cache(dk, dv, lengths)
+            del dk, dv
+            caches.append(cache)
+        out = torch.empty_like(q)
+        old_pages = max(t // PAGE for t in tables.old_tokens)
+        for split in candidates(old_pages):
+            dec = PageGaugeDecode(ws)
+            dec.plan(tables.old_indptr, tables.old_indices, tables.exact_indptr,
+                     tables.exact_indices, tables.exact_last_page_len, 32, 8,
+                     old_split_pages=split)
+
+            def run(c):
+                dec.run(q, c.key_codes, c.value_codes, c.key_scales, c.value_scales, c.exact_key,
+                        c.exact_value, c.value_center, out=out)
+
+            with torch.cuda.stream(stream):
+                for c in caches:
+                    run(c)
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=stream):
+                    for i in range(chunk):
+                        run(caches[i % layers])
+                for _ in range(3):
+                    graph.replay()
+                times = []
+                for _ in range(repeats):
+                    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    s.record()
+                    graph.replay()
+                    e.record()
+                    e.synchronize()
+                    times.append(s.elapsed_time(e) * 1e3 / chunk)
+            torch.cuda.synchronize()
+            del graph
+            results.setdefault(split, []).append(statistics.median(times))
+        del caches
+    p50 = {k: statistics.fmean(v) for k, v in results.items()}
+    if write:
+        record(batch, context, p50, path=path,
+               meta={"gpu": torch.cuda.get_device_name(), "repeats": repeats,
+                     "seeds": list(seeds), "lengths": lengths, "layers": layers,
+                     "mode": (f"steady: CUDA graph of {chunk} back-to-back decode steps "
+                              f"(split + merge) cycling {layers} caches")})
+    return p50
+
+
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__)
     parser.add_argument("--sweep", action="store_true")
@@ -158,18 +229,23 @@ def main() -> None:
     parser.add_argument("--ragged", type=int, default=0,
                         help="also sweep a ragged batch of this size (contexts U[4096, 32768])")
     parser.add_argument("--table", type=Path, default=TABLE_PATH)
+    parser.add_argument("--mode", choices=("steady", "burst"), default="steady")
+    parser.add_argument("--reset", action="store_true", help="start from an empty table")
     args = parser.parse_args()
+    if args.reset and args.sweep:
+        args.table.write_text(json.dumps({"entries": {}}, indent=1) + "\n")
     if not args.sweep:
         print(json.dumps(load_table(args.table), indent=1))
         return
     for b in args.batch:
         for c in args.context:
-            print(b, c, json.dumps(sweep(b, c, args.repeats, path=args.table)), flush=True)
+            print(b, c, json.dumps(sweep(b, c, args.repeats, path=args.table, mode=args.mode)),
+                  flush=True)
     if args.ragged:
         from .shard import ragged_lengths
         lengths = ragged_lengths(args.ragged, 20261001)
         print("ragged", lengths, json.dumps(sweep(0, 0, args.repeats, path=args.table,
-                                                  lengths=lengths)), flush=True)
+                                                  lengths=lengths, mode=args.mode)), flush=True)
 
 
 if __name__ == "__main__":

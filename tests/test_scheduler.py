@@ -6,20 +6,24 @@ from __future__ import annotations
 from pagegauge_b200 import scheduler as S
 
 
-def test_buckets_cover_power_of_two_ranges():
-    assert S.bucket(1, 16384) == S.bucket(1, 32767) == "b1_c16384"
-    assert S.bucket(1, 49152) == "b1_c32768"
-    assert S.bucket(8, 100) == "b8_c1024"
+def test_buckets_cover_half_octaves():
+    assert S.bucket(1, 16384) == S.bucket(1, 24575) == "b1_c16384"
+    assert S.bucket(1, 24576) == S.bucket(1, 32767) == "b1_c24576"
+    assert S.bucket(1, 49152) == S.bucket(1, 65535) == "b1_c49152"
+    assert S.bucket(1, 32768) == S.bucket(1, 49151) == "b1_c32768"
+    assert S.bucket(8, 100) == S.bucket(8, 1535) == "b8_c1024"
+    assert S.bucket(8, 3000) == "b8_c2048" and S.bucket(8, 3072) == "b8_c3072"
 
 
 def test_committed_table_has_the_benchmark_shapes():
     entries = S.load_table()["entries"]
-    for key in ("b1_c4096", "b1_c16384", "b1_c32768", "b8_c16384", "b32_c16384"):
+    for key in ("b1_c4096", "b1_c16384", "b1_c32768", "b1_c49152", "b8_c24576", "b32_c16384"):
         e = entries[key]
         assert e["split_pages"] == min(e["candidates_us"], key=lambda k: e["candidates_us"][k]) \
             or str(e["split_pages"]) == min(e["candidates_us"], key=e["candidates_us"].get)
         assert e["p50_us"] == min(e["candidates_us"].values())
-    assert S.lookup(1, 49152) == entries["b1_c32768"]["split_pages"]
+    assert S.lookup(1, 49152) == entries["b1_c49152"]["split_pages"]
+    assert all(e["mode"].startswith("steady") for e in entries.values())
 
 
 def test_unmeasured_bucket_falls_back_to_heuristic(tmp_path):
