@@ -354,6 +354,10 @@ typedef struct pg_gemm_args {
   int64_t partial_floats;
   int32_t* counters;
   int32_t num_counters;
+  const void* norm_weight; /* fp16 [k] or NULL: the input rows are first
+                              RMS-normalised, f16(w * f16(x * rsqrt(mean(x^2)
+                              + eps))) (MistralRMSNorm), inside the GEMM */
+  float norm_eps;
 } pg_gemm_args;
 
 /* Pack W [n, k] (row stride ld, FP16) for pg_skinny_gemm with the same

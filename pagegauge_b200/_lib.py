@@ -59,7 +59,7 @@ class PgGemmArgs(ctypes.Structure):
         ("residual", c_vp), ("ldr", c_i64),
         ("n", c_i32), ("k", c_i32), ("batch", c_i32), ("mode", c_i32), ("grid", c_i32),
         ("pdl", c_i32), ("partials", c_vp), ("partial_floats", c_i64), ("counters", c_vp),
-        ("num_counters", c_i32),
+        ("num_counters", c_i32), ("norm_weight", c_vp), ("norm_eps", ctypes.c_float),
     ]
 
 

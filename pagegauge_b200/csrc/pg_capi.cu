@@ -1076,20 +1076,19 @@ int32_t ensure_gemm_smem() {
     return fail(PG_ERR_CUDA, "cudaGetDevice failed");
   std::lock_guard<std::mutex> lock(mu);
   if (!done[dev]) {
-    int32_t rc = cuda_check(cudaFuncSetAttribute(pg::pg_skinny_gemm_kernel<1>,
-                                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 pg::gemm_smem_bytes(1)),
-                            "cudaFuncSetAttribute(gemm 1)");
-    if (rc == PG_OK)
-      rc = cuda_check(cudaFuncSetAttribute(pg::pg_skinny_gemm_kernel<2>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           pg::gemm_smem_bytes(2)),
-                      "cudaFuncSetAttribute(gemm 2)");
-    if (rc == PG_OK)
-      rc = cuda_check(cudaFuncSetAttribute(pg::pg_skinny_gemm_kernel<4>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           pg::gemm_smem_bytes(4)),
-                      "cudaFuncSetAttribute(gemm 4)");
+    int32_t rc = PG_OK;
+    auto set = [&](auto kernel, int nt) {
+      if (rc == PG_OK)
+        rc = cuda_check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             pg::gemm_smem_bytes(nt)),
+                        "cudaFuncSetAttribute(gemm)");
+    };
+    set(pg::pg_skinny_gemm_kernel<1, false>, 1);
+    set(pg::pg_skinny_gemm_kernel<2, false>, 2);
+    set(pg::pg_skinny_gemm_kernel<4, false>, 4);
+    set(pg::pg_skinny_gemm_kernel<1, true>, 1);
+    set(pg::pg_skinny_gemm_kernel<2, true>, 2);
+    set(pg::pg_skinny_gemm_kernel<4, true>, 4);
     if (rc != PG_OK) return rc;
     done[dev] = true;
   }
@@ -1172,6 +1171,14 @@ int32_t pg_skinny_gemm(const pg_gemm_args* a, void* stream) {
   p.partials = a->partials;
   p.counters = a->counters;
   p.error_flag = device_error_ptr();
+  if (a->norm_weight != nullptr) {
+    PG_REQUIRE(aligned(a->norm_weight, 16), "the norm weight must be 16-byte aligned");
+    PG_REQUIRE(a->norm_eps > 0.f && std::isfinite(a->norm_eps), "norm eps must be positive");
+    p.norm_w = static_cast<const __half*>(a->norm_weight);
+    p.x = static_cast<const __half*>(a->x);
+    p.ldx = a->ldx;
+    p.norm_eps = a->norm_eps;
+  }
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(g.grid);
   cfg.blockDim = dim3(pg::kGemmWarps * 32);
@@ -1182,16 +1189,18 @@ int32_t pg_skinny_gemm(const pg_gemm_args* a, void* stream) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = a->pdl ? 1 : 0;
+  const __half* wp = static_cast<const __half*>(a->w);
+  const bool norm = p.norm_w != nullptr;
   cudaError_t e;
   if (nt == 1)
-    e = cudaLaunchKernelEx(&cfg, pg::pg_skinny_gemm_kernel<1>,
-                           static_cast<const __half*>(a->w), tx, p);
+    e = norm ? cudaLaunchKernelEx(&cfg, pg::pg_skinny_gemm_kernel<1, true>, wp, tx, p)
+             : cudaLaunchKernelEx(&cfg, pg::pg_skinny_gemm_kernel<1, false>, wp, tx, p);
   else if (nt == 2)
-    e = cudaLaunchKernelEx(&cfg, pg::pg_skinny_gemm_kernel<2>,
-                           static_cast<const __half*>(a->w), tx, p);
+    e = norm ? cudaLaunchKernelEx(&cfg, pg::pg_skinny_gemm_kernel<2, true>, wp, tx, p)
+             : cudaLaunchKernelEx(&cfg, pg::pg_skinny_gemm_kernel<2, false>, wp, tx, p);
   else
-    e = cudaLaunchKernelEx(&cfg, pg::pg_skinny_gemm_kernel<4>,
-                           static_cast<const __half*>(a->w), tx, p);
+    e = norm ? cudaLaunchKernelEx(&cfg, pg::pg_skinny_gemm_kernel<4, true>, wp, tx, p)
+             : cudaLaunchKernelEx(&cfg, pg::pg_skinny_gemm_kernel<4, false>, wp, tx, p);
   return cuda_check(e, "skinny gemm launch");
 }
 

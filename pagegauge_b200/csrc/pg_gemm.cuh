@@ -24,6 +24,12 @@
 //   silu_mul  Y = f16(f16(silu(f16(acc_gate))) * f16(acc_up)); W rows
 //             [0, n/2) are gate rows and [n/2, n) up rows, a 64-row tile
 //             holds 32 gate rows and the matching 32 up rows.
+// Optional prologue (kernel instantiation NORM): the decoder's RMSNorm of
+// the input rows.  Each CTA reduces the rows' sums of squares itself at
+// its start, and every activation fragment is normalised in registers
+// right after its ldmatrix, f16(w * f16(x * inv_rms)), with no extra
+// barrier in the stage loop; this removes the separate norm launch before
+// the qkv and gate/up projections.
 //
 // Programmatic dependent launch: a CTA requests its first weight stages
 // before griddepcontrol.wait (weights are never written by a predecessor),
@@ -58,6 +64,12 @@ struct GemmParams {
   float* partials;   // [grid * max_seg][64][8*NT]
   int32_t* counters; // [tiles], zero between launches
   int* error_flag;
+  // Fused RMSNorm prologue (null: none): the GEMM's input is
+  // f16(norm_w * f16(x * rsqrt(mean(x^2) + eps))) of the rows of x.
+  const __half* norm_w;
+  const __half* x;
+  int64_t ldx;
+  float norm_eps;
 };
 
 __host__ __device__ constexpr int gemm_stage_bytes(int nt) {
@@ -83,6 +95,14 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
 }
 
 constexpr int kGemmMaxContrib = 16;  // CTAs sharing one tile (host-checked)
+
+// f16(w * f16(x * inv)) on a half2 (MistralRMSNorm's rounding points).
+__device__ __forceinline__ uint32_t rms_scale_h2(uint32_t x, float inv, uint32_t w) {
+  const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&x));
+  const __half2 n = __floats2half2_rn(f.x * inv, f.y * inv);
+  const __half2 r = __hmul2(*reinterpret_cast<const __half2*>(&w), n);
+  return *reinterpret_cast<const uint32_t*>(&r);
+}
 
 // The CTAs whose k-block ranges intersect tile t (ranges are
 // [floor(c*T/G), floor((c+1)*T/G))).
@@ -215,7 +235,7 @@ __device__ __forceinline__ void gemm_flush(const GemmParams& p, const float (&ac
   __syncthreads();
 }
 
-template <int NT>
+template <int NT, bool NORM>
 __global__ void __launch_bounds__(kGemmWarps * 32)
     pg_skinny_gemm_kernel(const __half* __restrict__ w_packed,
                           const __grid_constant__ CUtensorMap tm_x,
@@ -230,6 +250,7 @@ __global__ void __launch_bounds__(kGemmWarps * 32)
   __shared__ int s_last;
   __shared__ int s_seg[kGemmMaxContrib];
   __shared__ float s_tile[kGemmTileRows * ES];
+  __shared__ float s_inv[XR];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int c = blockIdx.x;
   const int b0 = c * p.total / p.grid, b1 = (c + 1) * p.total / p.grid;
@@ -259,6 +280,57 @@ __global__ void __launch_bounds__(kGemmWarps * 32)
       if (++ikb == p.kblocks) ikb = 0, ++itile;
     }
   }
+  if constexpr (NORM) {
+    // Sum of squares of every input row, all rows at once so that the
+    // loads of a pass are independent (one L2 round trip per pass): thread
+    // t reads the 16-byte chunks t, t + 128, ... of each row.
+    __shared__ float s_red[kGemmWarps][XR];
+    const int chunks = p.k / 8;
+#pragma unroll 1
+    for (int r0 = 0; r0 < XR; r0 += 8) {  // eight rows per pass
+      float ss[8];
+#pragma unroll
+      for (int r = 0; r < 8; ++r) ss[r] = 0.f;
+#pragma unroll 2
+      for (int ch = threadIdx.x; ch < chunks; ch += kGemmWarps * 32) {
+        uint4 v[8];
+#pragma unroll
+        for (int r = 0; r < 8; ++r)
+          v[r] = r0 + r < p.batch ? reinterpret_cast<const uint4*>(p.x + (r0 + r) * p.ldx)[ch]
+                                  : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+          const uint32_t w4[4] = {v[r].x, v[r].y, v[r].z, v[r].w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w4[e]));
+            ss[r] = fmaf(f.x, f.x, ss[r]);
+            ss[r] = fmaf(f.y, f.y, ss[r]);
+          }
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        float v = ss[r];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (lane == 0) s_red[warp][r0 + r] = v;
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x < XR) {
+      const int r = threadIdx.x;
+      float total = 0.f;
+#pragma unroll
+      for (int w = 0; w < kGemmWarps; ++w) total += s_red[w][r];
+      s_inv[r] = r < p.batch ? rsqrtf(total / static_cast<float>(p.k) + p.norm_eps) : 0.f;
+    }
+    __syncthreads();
+  }
+  // Per n-tile q, the inverse RMS of this lane's batch row 8q + g.
+  float inv_g[NT];
+#pragma unroll
+  for (int q = 0; q < NT; ++q) inv_g[q] = NORM ? s_inv[8 * q + (lane >> 2)] : 0.f;
 
   // ldmatrix lane addresses (128-byte swizzle: chunk ^ (row & 7)).
   const int mat = lane >> 3, rr = lane & 7;
@@ -297,6 +369,14 @@ __global__ void __launch_bounds__(kGemmWarps * 32)
     for (int j = 0; j < 4; ++j) {
       uint32_t a[4];
       ldsm_x4(ws + arow * 128 + (((2 * j + achunk) ^ rr) << 4), a[0], a[1], a[2], a[3]);
+      // NORM: this lane's B fragments hold k = 16j + 2t, +1 (x0) and
+      // 16j + 8 + 2t, +1 (x1) of batch row 8q + g.
+      uint32_t wlo = 0u, whi = 0u;
+      if constexpr (NORM) {
+        const uint32_t* nw = reinterpret_cast<const uint32_t*>(p.norm_w + ckb * kGemmBK + 16 * j);
+        wlo = __ldg(nw + (lane & 3));
+        whi = __ldg(nw + 4 + (lane & 3));
+      }
 #pragma unroll
       for (int q = 0; q < NT; q += 2) {
         if (q + 1 < NT) {
@@ -304,12 +384,22 @@ __global__ void __launch_bounds__(kGemmWarps * 32)
           const int xrow = 8 * (q + (mat >> 1)) + rr;
           uint32_t x0, x1, x2, x3;
           ldsm_x4(xs + xrow * 128 + (((2 * j + (mat & 1)) ^ rr) << 4), x0, x1, x2, x3);
+          if constexpr (NORM) {
+            x0 = rms_scale_h2(x0, inv_g[q], wlo);
+            x1 = rms_scale_h2(x1, inv_g[q], whi);
+            x2 = rms_scale_h2(x2, inv_g[q + 1], wlo);
+            x3 = rms_scale_h2(x3, inv_g[q + 1], whi);
+          }
           mma_16816(acc[q], a, x0, x1);
           mma_16816(acc[q + 1], a, x2, x3);
         } else {
           const int xrow = 8 * q + rr;
           uint32_t x0, x1;
           ldsm_x2(xs + xrow * 128 + (((2 * j + (mat & 1)) ^ rr) << 4), x0, x1);
+          if constexpr (NORM) {
+            x0 = rms_scale_h2(x0, inv_g[q], wlo);
+            x1 = rms_scale_h2(x1, inv_g[q], whi);
+          }
           mma_16816(acc[q], a, x0, x1);
         }
       }

@@ -251,16 +251,22 @@ class PageGaugeDecoder:
     """Greedy decoding with PageGauge attention on this rank's shard.
 
     ``process_group``: the tensor-parallel group (NCCL) or None for one GPU.
+    ``fuse_norm`` (one GPU, streaming GEMMs): compute the RMSNorms inside the
+    qkv, gate/up and LM-head GEMMs instead of separate launches; measured
+    slower on B200 (4.1-4.4 ms against 3.6-3.9 ms per B=1 step), so off by
+    default.
     """
 
     def __init__(self, weights: DecoderWeights, batch: int, max_context: int,
                  process_group=None, ring_pages: int = 16, workspace_mb: int = 32,
-                 gemm: str = "auto", sink_pages: int = 0, suffix_pages: int = 0):
+                 gemm: str = "auto", sink_pages: int = 0, suffix_pages: int = 0,
+                 fuse_norm: bool = False):
         cfg, tp = weights.cfg, weights.tp
         if cfg.head_dim != HEAD_DIM:
             raise ValueError("head_dim must be 128")
         self.cfg, self.tp, self.w = cfg, tp, weights
         self.pg = process_group
+        self.fuse_norm = bool(fuse_norm)
         self.batch = batch
         dev = weights.embed.device
         self.device = dev
@@ -507,12 +513,18 @@ class PageGaugeDecoder:
         torch.index_select(self.w.embed, 0, self.tokens, out=self.residual)
         q_w, kv_w = self.hq * d, self.hkv * d
         fused = self.gemm_impl == "pg" and self.pg is None
+        fuse_norm = fused and self.fuse_norm
         delta = None
+        eps = self.cfg.rms_eps
         for l, lw in enumerate(self.w.layers):
             c = self.caches[l]
             pk = self.packed[l] if self.packed else {}
-            self._norm(self.residual, delta, lw.attn_norm, self.normed)
-            self._linear(self.normed, lw.qkv, self.qkv, pk.get("qkv"))
+            if fuse_norm:
+                # RMSNorm inside the qkv projection.
+                self.sk(self.residual, pk["qkv"], out=self.qkv, norm_weight=lw.attn_norm, eps=eps)
+            else:
+                self._norm(self.residual, delta, lw.attn_norm, self.normed)
+                self._linear(self.normed, lw.qkv, self.qkv, pk.get("qkv"))
             q = self.qkv[:, :q_w].view(B, self.hq, d)
             k = self.qkv[:, q_w:q_w + kv_w].view(B, self.hkv, d)
             v = self.qkv[:, q_w + kv_w:].view(B, self.hkv, d)
@@ -527,8 +539,12 @@ class PageGaugeDecoder:
                 # SiLU(gate) * up fused into the gate/up projection and the
                 # down projection added into the residual.
                 self.sk(self.attn.view(B, -1), pk["o"], mode=RESIDUAL, residual=self.residual)
-                self._norm(self.residual, None, lw.mlp_norm, self.normed)
-                self.sk(self.normed, pk["gate_up"], out=self.act, mode=SILU_MUL)
+                if fuse_norm:
+                    self.sk(self.residual, pk["gate_up"], out=self.act, mode=SILU_MUL,
+                            norm_weight=lw.mlp_norm, eps=eps)
+                else:
+                    self._norm(self.residual, None, lw.mlp_norm, self.normed)
+                    self.sk(self.normed, pk["gate_up"], out=self.act, mode=SILU_MUL)
                 self.sk(self.act, pk["down"], mode=RESIDUAL, residual=self.residual)
                 delta = None
                 continue
@@ -543,9 +559,13 @@ class PageGaugeDecoder:
             self._linear(self.act, lw.down, self.down, pk.get("down"))
             self._all_reduce(self.down)
             delta = self.down
-        self._norm(self.residual, delta, self.w.final_norm, self.normed)
-        self._linear(self.normed, self.w.lm_head, self.logits,
-                     self.lm_head_packed if self.packed else None)
+        if fuse_norm:
+            self.sk(self.residual, self.lm_head_packed, out=self.logits,
+                    norm_weight=self.w.final_norm, eps=eps)
+        else:
+            self._norm(self.residual, delta, self.w.final_norm, self.normed)
+            self._linear(self.normed, self.w.lm_head, self.logits,
+                         self.lm_head_packed if self.packed else None)
         self.tokens.copy_(self._greedy(self.logits))
         _call("pg_step_positions", self.positions.data_ptr(), self.last_len.data_ptr(), B, 1,
               _stream())
@@ -564,9 +584,14 @@ class PageGaugeDecoder:
         if entry is not None:
             plan = entry["dec"].work_plan
             attn = 1 if (plan.single and plan.num_items) else 2
+        if self.gemm_impl == "pg" and self.pg is None and self.fuse_norm:
+            # qkv (+RMSNorm), append, o (+residual), gate_up (+RMSNorm,
+            # SiLU), down (+residual) per layer; the LM head (+final norm),
+            # argmax and position update.
+            return self.cfg.layers * (5 + attn) + 3
         if self.gemm_impl == "pg":
-            # norm, qkv, append, o, norm, gate_up(+SiLU), down per layer; the
-            # final norm, LM head, argmax and position update.
+            # norm, qkv, append, o, all-reduce-fed norm, gate_up(+SiLU), down
+            # per layer; the final norm, LM head, argmax and position update.
             return self.cfg.layers * (7 + attn) + 4
         return self.cfg.layers * (4 + attn) + 3
 

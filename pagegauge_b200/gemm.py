@@ -62,9 +62,13 @@ class SkinnyGemm:
 
     def __call__(self, x: torch.Tensor, w: PackedWeight, out: torch.Tensor | None = None,
                  mode: int = STORE, residual: torch.Tensor | None = None, pdl: bool = True,
-                 grid: int = 0) -> torch.Tensor | None:
+                 grid: int = 0, norm_weight: torch.Tensor | None = None,
+                 eps: float = 1e-5) -> torch.Tensor | None:
         """y = x @ W^T with W packed for this ``mode`` (silu_mul needs the
-        silu_mul packing; store and residual share theirs)."""
+        silu_mul packing; store and residual share theirs).  ``norm_weight``
+        ([k] float16) first RMS-normalises the rows of x inside the GEMM
+        (transformers' MistralRMSNorm: f16(w * f16(x * rsqrt(mean(x^2) +
+        eps))))."""
         if x.dtype != torch.float16 or x.dim() != 2 or x.stride(1) != 1:
             raise ValueError("x must be a float16 [batch, k] tensor with contiguous rows")
         if (w.mode == SILU_MUL) != (mode == SILU_MUL):
@@ -90,5 +94,12 @@ class SkinnyGemm:
         a.n, a.k, a.batch, a.mode, a.grid, a.pdl = n, k, batch, mode, grid, int(pdl)
         a.partials, a.partial_floats = self.partials.data_ptr(), self.partials.numel()
         a.counters, a.num_counters = self.counters.data_ptr(), self.counters.numel()
+        if norm_weight is not None:
+            if (norm_weight.dtype != torch.float16 or norm_weight.shape != (k,)
+                    or not norm_weight.is_contiguous()):
+                raise ValueError(f"norm_weight must be a contiguous float16 [{k}] tensor")
+            if x.data_ptr() % 16 or x.stride(0) % 8:
+                raise ValueError("the normalised x must be 16-byte aligned with rows of 8k halves")
+            a.norm_weight, a.norm_eps = norm_weight.data_ptr(), float(eps)
         _lib.check(_lib.load().pg_skinny_gemm(ctypes.byref(a), _stream()))
         return out if mode != RESIDUAL else residual

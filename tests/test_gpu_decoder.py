@@ -134,3 +134,26 @@ def test_prepare_captures_future_page_structures(cuda_lib):
     before = dec.replans
     dec.generate(16)
     assert dec.replans == before
+
+
+def test_fused_norm_option_matches_oracle(cuda_lib):
+    """fuse_norm=True (RMSNorm inside the qkv / gate-up / LM-head GEMMs)
+    stays within the decoder tolerance of the oracle."""
+    batch, prompt_len = 2, 300
+    weights = random_decoder_weights(CFG, SEED, device="cuda", gen_device="cpu")
+    dec = PageGaugeDecoder(weights, batch=batch, max_context=512, gemm="pg", fuse_norm=True)
+    prompt = torch.randint(0, CFG.vocab, (batch, prompt_len),
+                           generator=torch.Generator().manual_seed(8))
+    dec.prefill(prompt.cuda())
+    w, cfg = oracle_weights(CFG), oracle_cfg(CFG)
+    cfg["rope"] = (dec.cos.cpu().numpy(), dec.sin.cpu().numpy())
+    caches = _oracle_caches(dec)
+    tokens = dec.tokens.cpu().numpy().copy()
+    for i in range(8):
+        exp = D.decode_step(w, cfg, caches, tokens, [prompt_len + i] * batch, dec.capacity_pages)
+        dec.step(use_graph=True)
+        got = dec.logits.float().cpu().numpy()
+        for r in range(batch):
+            _close(got[r], exp[r])
+        tokens = dec.tokens.cpu().numpy().copy()
+    assert dec.launches_per_step() in (CFG.layers * 6 + 3, CFG.layers * 7 + 3)

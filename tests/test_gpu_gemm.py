@@ -158,3 +158,43 @@ def test_packed_layout(cuda_lib):
             else:
                 row = 32 * t + r if r < 32 else n // 2 + 32 * t + (r - 32)
             assert torch.equal(pw[t, kb, r, c ^ (r & 7)], w[row, 64 * kb + 8 * c:64 * kb + 8 * c + 8])
+
+
+def _rms_norm_ref(x, w, eps=1e-5):
+    """transformers MistralRMSNorm on FP16 rows: f16(w * f16(x * rsqrt(ms + eps)))."""
+    xf = x.float()
+    inv = torch.rsqrt((xf * xf).mean(-1, keepdim=True) + eps)
+    return (w.float() * (xf * inv).half().float()).half()
+
+
+@pytest.mark.parametrize("mode,batch,grid", [(STORE, 1, 0), (STORE, 5, 0), (SILU_MUL, 1, 0),
+                                             (SILU_MUL, 8, 37), (STORE, 32, 0)])
+def test_fused_rms_norm_prologue(cuda_lib, mode, batch, grid):
+    """The GEMM's RMSNorm prologue equals normalising first and multiplying
+    after: the normalised FP16 input may differ by one FP16 step where the
+    two reductions round the mean square differently."""
+    n, k = (2048, 4096) if mode == SILU_MUL else (1536, 4096)
+    w, _ = _data(n, k, batch, 41 + batch)
+    g = torch.Generator(device="cuda").manual_seed(7 * batch)
+    x = (torch.randn(batch, k, generator=g, device="cuda") * 3).half()
+    nw = (1 + 0.1 * torch.randn(k, generator=g, device="cuda")).half()
+    gemm = SkinnyGemm("cuda")
+    gemm.reserve(n, k, batch, mode)
+    pw = PackedWeight(w, mode)
+    fused = gemm(x, pw, mode=mode, grid=grid, norm_weight=nw)
+    xn = _rms_norm_ref(x, nw)
+    plain = gemm(xn, pw, mode=mode, grid=grid)
+    torch.cuda.synchronize()
+    assert read_device_error() == 0
+    assert torch.equal(x, x)  # the input rows are read, never written
+    if mode == STORE:
+        ref = _ref(xn, w)
+        slack = (xn.float().abs() * 2.0 ** -11) @ w.float().abs().t()
+        tol = ref.abs() * 2.0 ** -10 + 1e-6 * k ** 0.5 + slack
+        assert bool(((fused.float() - ref).abs() <= tol).all())
+    # Against the two-step path: identical except for rare one-step input
+    # differences.
+    diff = (fused.float() - plain.float()).abs()
+    assert diff.max().item() < 2e-2 and (diff == 0).float().mean().item() > 0.9
+    with pytest.raises(ValueError, match="norm_weight"):
+        gemm(x, pw, mode=mode, norm_weight=nw[:100])
