@@ -70,6 +70,12 @@ int32_t pg_abi_version(void);
 /* Read and clear the device guard word of the current device. */
 int32_t pg_read_device_error(int32_t* code_out);
 
+/* Device address of a page-locked, mapped host buffer (cudaHostAlloc /
+ * pinned memory): kernels may take it wherever an input or output pointer
+ * is expected and then read or write the host buffer directly over the
+ * host link (zero copy).  Fails for memory that is not mapped.            */
+int32_t pg_host_device_pointer(const void* host, void** device_out);
+
 /* ---------------------------------------------------------------------- */
 /* Fused RoPE + FP16 append (the comparator path).                         */
 /* query [B,Hq,128], key/value [B,Hkv,128] fp16 with contiguous heads;      */

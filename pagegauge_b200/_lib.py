@@ -68,6 +68,7 @@ _SIGNATURES = {
     "pg_last_error": (ctypes.c_char_p, []),
     "pg_abi_version": (c_i32, []),
     "pg_read_device_error": (c_i32, [c_i32p]),
+    "pg_host_device_pointer": (c_i32, [c_vp, ctypes.POINTER(c_vp)]),
     "pg_rope_append_fp16": (c_i32, [c_vp] * 8 + [c_i64] * 3 + [c_i32] * 3 + [c_i64, c_i64, c_vp, c_i64, c_i64, c_vp]),
     "pg_rope_append_page_gauge": (
         c_i32,
@@ -148,3 +149,16 @@ def check(rc: int) -> None:
 
 def call(name: str, *args) -> None:
     check(getattr(load(), name)(*args))
+
+
+def kernel_pointer(t, name: str) -> int:
+    """Address a kernel may use for tensor ``t``: its device address, or for
+    a page-locked host tensor the mapped device address of the host buffer
+    (read or written over the host link, zero copy)."""
+    if t.is_cuda:
+        return t.data_ptr()
+    if t.is_pinned():
+        out = c_vp()
+        check(load().pg_host_device_pointer(c_vp(t.data_ptr()), ctypes.byref(out)))
+        return int(out.value)
+    raise RuntimeError(f"{name} must be CUDA or page-locked host memory")

@@ -226,7 +226,17 @@ extern "C" {
 
 const char* pg_last_error(void) { return g_last_error.c_str(); }
 
-int32_t pg_abi_version(void) { return 102; }
+int32_t pg_abi_version(void) { return 103; }
+
+int32_t pg_host_device_pointer(const void* host, void** device_out) {
+  PG_REQUIRE(host != nullptr && device_out != nullptr, "null pointer");
+  void* d = nullptr;
+  int32_t rc = cuda_check(cudaHostGetDevicePointer(&d, const_cast<void*>(host), 0),
+                          "cudaHostGetDevicePointer (the buffer must be page-locked and mapped)");
+  if (rc != PG_OK) return rc;
+  *device_out = d;
+  return PG_OK;
+}
 
 int32_t pg_read_device_error(int32_t* code_out) {
   int* p = device_error_ptr();

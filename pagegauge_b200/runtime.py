@@ -69,6 +69,18 @@ def _check_qkv(query, key, value, rotated_query) -> None:
     _require(rotated_query.shape == query.shape, "rotated query shape mismatch")
 
 
+def _check_host_or_device_input(tensor, name: str) -> None:
+    """A head-major FP16 input that may also be page-locked host memory."""
+    if not (tensor.is_cuda or tensor.is_pinned()):
+        raise RuntimeError(f"{name} must be CUDA or page-locked host memory")
+    if tensor.dtype != torch.float16:
+        raise RuntimeError(f"{name} must be FP16")
+    if tensor.dim() != 3:
+        raise RuntimeError(f"{name} must have rank three")
+    if tensor.stride(2) != 1 or tensor.stride(1) != HEAD_DIM:
+        raise RuntimeError(f"{name} must be head-major with a contiguous head dimension")
+
+
 def _check_dynamic(query, cosine, sine, position) -> None:
     """tests/page_gauge_append_extension.cu:623-640."""
     check_tensor(cosine, "cosine", torch.float16, 2)
@@ -233,22 +245,37 @@ class AppendExtension:
                                        value_scales, exact_sink_pages: int) -> None:
         """rope_append_page_gauge_dynamic with one position per request
         (``positions`` int32 [B] on the device): request r appends at
-        positions[r] and closes its page when positions[r] % 16 == 15."""
-        _check_qkv(query, key, value, rotated_query)
+        positions[r] and closes its page when positions[r] % 16 == 15.
+        ``query``/``key``/``value`` may be page-locked host tensors: the
+        kernel then reads them over the host link (no separate copy)."""
+        host_in = not query.is_cuda
+        if host_in:
+            for name, t in (("query", query), ("key", key), ("value", value)):
+                _check_host_or_device_input(t, name)
+            check_tensor(rotated_query, "rotated_query", torch.float16, 3)
+            _require(query.size(0) > 0 and query.size(0) == key.size(0)
+                     and query.size(0) == value.size(0),
+                     "Q/K/V batch sizes must match and be positive")
+            _require(key.shape == value.shape, "K/V input shapes must match")
+            _require(rotated_query.shape == query.shape, "rotated query shape mismatch")
+            _check_positions(rotated_query, cosine, sine, positions)
+        else:
+            _check_qkv(query, key, value, rotated_query)
+            _check_positions(query, cosine, sine, positions)
         _check_pages(exact_key_pages, exact_value_pages, key, "exact_key_pages",
                      "exact_value_pages", "exact page cache must be NHD [pages,16,Hkv,128]")
-        _check_positions(query, cosine, sine, positions)
         cstride = _check_gauge_storage(query, key, key_center, value_center, key_codes,
                                        value_codes, key_scales, value_scales)
         _lib.call(
-            "pg_rope_append_page_gauge_batched", query.data_ptr(), key.data_ptr(),
-            value.data_ptr(), cosine.data_ptr(), sine.data_ptr(), key_center.data_ptr(),
+            "pg_rope_append_page_gauge_batched", _lib.kernel_pointer(query, "query"),
+            _lib.kernel_pointer(key, "key"), _lib.kernel_pointer(value, "value"),
+            cosine.data_ptr(), sine.data_ptr(), key_center.data_ptr(),
             value_center.data_ptr(), rotated_query.data_ptr(), exact_key_pages.data_ptr(),
             exact_value_pages.data_ptr(), key_codes.data_ptr(), value_codes.data_ptr(),
             key_scales.data_ptr(), value_scales.data_ptr(), query.stride(0), key.stride(0),
             value.stride(0), cstride, query.size(0), query.size(1), key.size(1),
             exact_key_pages.size(0), key_codes.size(0), int(exact_sink_pages),
-            positions.data_ptr(), cosine.stride(0), cosine.size(0), _stream(query))
+            positions.data_ptr(), cosine.stride(0), cosine.size(0), _stream(rotated_query))
 
     def _gauge_call(self, query, key, value, cosine, sine, key_center, value_center,
                     rotated_query, exact_k, exact_v, codes_k, codes_v, scales_k, scales_v,

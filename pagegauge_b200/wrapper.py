@@ -175,9 +175,11 @@ def launch_decode(plan: PagedDecodePlan, q: torch.Tensor, segments, sm_scale: fl
     # memory and the last cluster of a head finishes it.
     a.merge_sem = plan.sem_ptr if (fused_merge or cluster > 1) else None
     a.cluster = cluster
-    a.out = out.data_ptr()
+    # out / lse may be page-locked host tensors: the merge (or the final
+    # epilogue) then writes the result over the host link.
+    a.out = _lib.kernel_pointer(out, "out")
     a.out_stride_b, a.out_stride_h = out.stride(0), out.stride(1)
-    a.lse_out = None if lse is None else lse.data_ptr()
+    a.lse_out = None if lse is None else _lib.kernel_pointer(lse, "lse")
     if extra is not None:
         eo, el = extra
         a.extra_o = eo.data_ptr()

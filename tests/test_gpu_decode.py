@@ -338,3 +338,50 @@ def test_single_launch_cluster_merge(cuda_lib, cluster, lengths, split):
     torch.cuda.synchronize()
     assert torch.equal(out, again)
     assert read_device_error() == 0
+
+
+def test_zero_copy_host_inputs_and_output(cuda_lib):
+    """Page-locked host q/k/v read by the batched append and a page-locked
+    host output written by the merge equal the device-resident path bit for
+    bit; unpinned host memory is refused (never handed to a kernel)."""
+    lengths = [3000, 700]
+    q, dk, dv, cache, tables = make_case(lengths, seed=21, capacity_pages=200)
+    ext = load_append_extension()
+    B = len(lengths)
+    g = torch.Generator().manual_seed(4)
+    host = torch.randn(B, (32 + 16) * 128, generator=g).half().pin_memory()
+    hq = host[:, :32 * 128].view(B, 32, 128)
+    hk = host[:, 32 * 128:40 * 128].view(B, 8, 128)
+    hv = host[:, 40 * 128:].view(B, 8, 128)
+    dev = host.cuda()
+    dq, dkk, dvv = (dev[:, :32 * 128].view(B, 32, 128), dev[:, 32 * 128:40 * 128].view(B, 8, 128),
+                    dev[:, 40 * 128:].view(B, 8, 128))
+    from pagegauge_b200.cache import rope_tables
+    cos, sin = rope_tables(4096, device="cuda")
+    pos = torch.tensor([n - 1 for n in lengths], dtype=torch.int32, device="cuda")
+    outs = []
+    for qq, kk, vv in ((dq, dkk, dvv), (hq, hk, hv)):
+        c = {k: getattr(cache, k).clone() for k in ("exact_key", "exact_value", "key_codes",
+                                                    "value_codes", "key_scales", "value_scales")}
+        rq = torch.empty(B, 32, 128, dtype=torch.float16, device="cuda")
+        ext.rope_append_page_gauge_batched(qq, kk, vv, cos, sin, pos, cache.key_center,
+                                           cache.value_center, rq, c["exact_key"], c["exact_value"],
+                                           c["key_codes"], c["value_codes"], c["key_scales"],
+                                           c["value_scales"], 0)
+        dec = PageGaugeDecode(workspace())
+        dec.plan(tables.old_indptr, tables.old_indices, tables.exact_indptr, tables.exact_indices,
+                 tables.exact_last_page_len, 32, 8)
+        out = (torch.empty(B, 32, 128, dtype=torch.float16).pin_memory() if qq is hq
+               else torch.empty(B, 32, 128, dtype=torch.float16, device="cuda"))
+        dec.run(rq, c["key_codes"], c["value_codes"], c["key_scales"], c["value_scales"],
+                c["exact_key"], c["exact_value"], cache.value_center, out=out)
+        torch.cuda.synchronize()
+        outs.append((rq.cpu(), c["exact_key"].cpu(), out.cpu()))
+    assert read_device_error() == 0
+    for a, b in zip(outs[0], outs[1]):
+        assert torch.equal(a, b)
+    with pytest.raises(RuntimeError, match="page-locked"):
+        ext.rope_append_page_gauge_batched(hq.clone(), hk, hv, cos, sin, pos, cache.key_center,
+                                           cache.value_center, rq, cache.exact_key,
+                                           cache.exact_value, cache.key_codes, cache.value_codes,
+                                           cache.key_scales, cache.value_scales, 0)
