@@ -144,18 +144,6 @@ __device__ __forceinline__ bool resolve_position(const AppendParams& p, int r,
   return true;
 }
 
-// Rotate the query heads h, h + Hkv, ... of request r.
-__device__ __forceinline__ void rotate_queries(const AppendParams& p, int r,
-                                               int h, int j, uint32_t c,
-                                               uint32_t s) {
-  for (int qh = h; qh < p.hq; qh += p.hkv) {
-    const __half* src = p.q + r * p.q_stride_b + static_cast<int64_t>(qh) * kHeadDim;
-    const uint32_t rot = rope_pair(src, j, c, s);
-    reinterpret_cast<uint32_t*>(p.rotated_q +
-                                (static_cast<int64_t>(r) * p.hq + qh) * kHeadDim)[j] = rot;
-  }
-}
-
 constexpr int kAppendThreads = 256;
 
 // Loads of one append CTA that do not depend on the position: the token's
@@ -243,18 +231,6 @@ __global__ void __launch_bounds__(kAppendThreads)
     reinterpret_cast<uint32_t*>(p.key_pages + dst)[j] = rope_apply(in.x, in.partner, j, c, s);
   else
     reinterpret_cast<uint32_t*>(p.value_pages + dst)[j] = in.x;
-}
-
-// Reduce a max across the 256-thread CTA (8 warps).
-__device__ __forceinline__ float cta256_max(float v, float* scratch) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  if ((threadIdx.x & 31) == 0) scratch[threadIdx.x >> 5] = v;
-  __syncthreads();
-  float m = scratch[0];
-#pragma unroll
-  for (int w = 1; w < kAppendThreads / 32; ++w) m = fmaxf(m, scratch[w]);
-  return m;
 }
 
 __device__ __forceinline__ float absmax_half8(const uint4& v) {

@@ -97,18 +97,6 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map,
       : "memory");
 }
 
-// Bulk tensor prefetch of a tile into L2 only (no shared memory, no
-// completion tracking): pages further ahead than the shared-memory ring can
-// hold are pulled into L2 so the ring's loads hit L2.
-__device__ __forceinline__ void tma_prefetch_l2_3d(const CUtensorMap* map, int c0,
-                                                   int c1, int c2) {
-  asm volatile(
-      "cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
-          reinterpret_cast<uint64_t>(map)),
-      "r"(c0), "r"(c1), "r"(c2)
-      : "memory");
-}
-
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(
                    reinterpret_cast<uint64_t>(map))
@@ -143,7 +131,6 @@ __device__ __forceinline__ uint32_t hsub2_u32(uint32_t a, uint32_t b) {
 // the low mantissa bits of 0x64xx is the half 1024 + u.  With u = z ^ 0x80
 // (= z + 128 mod 256) the value is z + 1152 exactly, for every z in
 // [-128, 127]; the constant bias is removed after the matrix product.
-constexpr uint32_t kMagic = 0x64646464u;
 
 // Bytes 0 and 2 of w as the biased half2 (z0 + 1152, z2 + 1152): sign-flip,
 // mask and exponent in one bitwise select (a single LOP3).

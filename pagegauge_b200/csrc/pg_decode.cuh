@@ -549,27 +549,18 @@ __device__ __forceinline__ void page_fp16(WarpState& st, const uint8_t* stage,
   }
 }
 
-// Issue the TMA copies of warp-page u into ring stage `stage`.
-template <int SEG>
-__device__ __forceinline__ void issue_page(const CUtensorMap* tk,
-                                           const CUtensorMap* tv,
-                                           uint8_t* ring, uint64_t* bars,
-                                           int stage, int id, int h) {
-  if (SEG == 0) {
-    uint8_t* dst = ring + stage * 4096;
-    uint64_t* bar = bars + stage;
-    mbar_arrive_expect_tx(bar, 4096);
-    tma_load_3d(dst, tk, 0, h, id * kPage, bar);
-    tma_load_3d(dst + 2048, tv, 0, h, id * kPage, bar);
-  } else {
-    uint8_t* dst = ring + stage * 8192;
-    uint64_t* bar = bars + stage;
-    mbar_arrive_expect_tx(bar, 8192);
-    tma_load_3d(dst, tk, 0, 2 * h, id * kPage, bar);
-    tma_load_3d(dst + 2048, tk, 0, 2 * h + 1, id * kPage, bar);
-    tma_load_3d(dst + 4096, tv, 0, 2 * h, id * kPage, bar);
-    tma_load_3d(dst + 6144, tv, 0, 2 * h + 1, id * kPage, bar);
-  }
+// Issue the TMA copies of FP16 warp-page u into ring stage `stage` (8 KB:
+// K dims 0-63 / 64-127, then V likewise).
+__device__ __forceinline__ void issue_page_fp16(const CUtensorMap* tk, const CUtensorMap* tv,
+                                                uint8_t* ring, uint64_t* bars, int stage, int id,
+                                                int h) {
+  uint8_t* dst = ring + stage * 8192;
+  uint64_t* bar = bars + stage;
+  mbar_arrive_expect_tx(bar, 8192);
+  tma_load_3d(dst, tk, 0, 2 * h, id * kPage, bar);
+  tma_load_3d(dst + 2048, tk, 0, 2 * h + 1, id * kPage, bar);
+  tma_load_3d(dst + 4096, tv, 0, 2 * h, id * kPage, bar);
+  tma_load_3d(dst + 6144, tv, 0, 2 * h + 1, id * kPage, bar);
 }
 
 // INT8 pages of one warp, two at a time.  The 4-stage ring is used as two
@@ -736,130 +727,72 @@ __device__ __forceinline__ bool run_warp_pages_int8(
   return ok;
 }
 
-template <int SEG, typename QFrag>
-__device__ __forceinline__ bool run_warp_pages(
+// FP16 pages (the exact tail ring, or a plain FP16 cache) of one warp, one
+// at a time through a 2-stage ring of 8 KB stages.
+__device__ __forceinline__ bool run_warp_pages_fp16(
     const DecodeParams& p, const CUtensorMap* tk, const CUtensorMap* tv,
-    WarpState& st, uint8_t* ring, uint64_t* bars, QFrag& qf, int r,
+    WarpState& st, uint8_t* ring, uint64_t* bars, uint32_t* qf, int r,
     int h, int idx_begin, int n_pages, bool has_last, int warp, int W,
     int lane) {
-  constexpr int S = SEG == 0 ? kStagesI8 : kStagesI8 / 2;
-  constexpr int STAGE_BYTES = SEG == 0 ? 4096 : 8192;
+  constexpr int S = kStagesI8 / 2;
+  constexpr int STAGE_BYTES = 8192;
   const int g = lane >> 2, t = lane & 3;
-  const SegmentDesc& sd = p.seg[SEG];
+  const SegmentDesc& sd = p.seg[1];
   const int n_w = n_pages > warp ? (n_pages - warp + W - 1) / W : 0;
   if (n_w == 0) return true;
 
   // Programmatic dependent launch: the FP16 exact pages may have been
   // written by the kernel just before this one (the append), so their loads
-  // wait for it; completed INT8 pages never are, so their first tiles are
-  // requested before the wait and overlap the predecessor's tail.
-  if constexpr (SEG == 1) pdl_wait_primary();
+  // wait for it.
+  pdl_wait_primary();
 
   PageWindow win;
   win.base = 0;
   win.two = n_w > 32;
-  load_window_set<SEG>(p, sd, idx_begin, warp, W, n_w, h, 0, lane, win.id_a,
-                       win.sk_a, win.sv_a);
+  load_window_set<1>(p, sd, idx_begin, warp, W, n_w, h, 0, lane, win.id_a,
+                     win.sk_a, win.sv_a);
   win.id_b = 0;
   win.sk_b = win.sv_b = 0.f;
   if (win.two)
-    load_window_set<SEG>(p, sd, idx_begin, warp, W, n_w, h, 32, lane, win.id_b,
-                         win.sk_b, win.sv_b);
+    load_window_set<1>(p, sd, idx_begin, warp, W, n_w, h, 32, lane, win.id_b,
+                       win.sk_b, win.sv_b);
 
   // Prologue: fill the ring.
   const int pro = n_w < S ? n_w : S;
   for (int u = 0; u < pro; ++u) {
     const int id = win_id(win, u);
-    if (lane == 0) issue_page<SEG>(tk, tv, ring, bars, u, id, h);
+    if (lane == 0) issue_page_fp16(tk, tv, ring, bars, u, id, h);
   }
-
-  // ldmatrix row addresses for the V tile (see pv_int8): lane l reads row
-  // l%8 of matrix l/8; matrices alternate token halves (0-7 / 8-15) and the
-  // m-tile pair {2k, 2k+1}; chunks are 128B-swizzled by token row.
-  uint32_t vaddr[4] = {0u, 0u, 0u, 0u};
-  if constexpr (SEG == 0) {
-    const int j = lane >> 3, row = lane & 7;
-    const int tok = 8 * (j & 1) + row;
-#pragma unroll
-    for (int k = 0; k < 4; ++k)
-      vaddr[k] = tok * 128 + (((2 * k + (j >> 1)) ^ row) << 4);
-  }
-  if constexpr (SEG == 0) pdl_wait_primary();
   int last_valid = kPage;
   if (has_last) {
     const int lv = __ldg(sd.last_len + r);
     last_valid = lv < 1 ? 1 : (lv > kPage ? kPage : lv);
   }
   // Prepare Q while the first tiles are in flight.
-  if constexpr (SEG == 0)
-    load_q_int8(p, r, h, g, t, qf);
-  else
-    load_q_fp16(p, r, h, g, t, qf);
-  if (SEG == 0) st.sref = win_f(win, win.sv_a, win.sv_b, 0);
+  load_q_fp16(p, r, h, g, t, qf);
   bool ok = true;
   int u = 0;
   while (u < n_w) {
-    // INT8 pages are consumed in pairs (independent chains -> ILP); FP16
-    // tail pages (2 stages per warp) one at a time.
-    const int np = (SEG == 0 && u + 1 < n_w) ? 2 : 1;
-    bool waited = mbar_wait_bounded(bars + (u % S), static_cast<uint32_t>(u / S) & 1u);
-    if (np == 2)
-      waited = waited && mbar_wait_bounded(bars + ((u + 1) % S),
-                                           static_cast<uint32_t>((u + 1) / S) & 1u);
+    const bool waited = mbar_wait_bounded(bars + (u % S), static_cast<uint32_t>(u / S) & 1u);
     if (!__all_sync(0xffffffffu, waited)) {
       ok = false;
       break;
     }
-    if constexpr (SEG == 0) {
-      float sk[2], sv[2], rr[2];
-      int valid[2];
-      const uint8_t* stg[2];
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int uj = j < np ? u + j : u;
-        sk[j] = win_f(win, win.sk_a, win.sk_b, uj - win.base);
-        sv[j] = win_f(win, win.sv_a, win.sv_b, uj - win.base);
-        valid[j] = (has_last && warp + W * uj == n_pages - 1) ? last_valid : kPage;
-        stg[j] = ring + (uj % S) * STAGE_BYTES;
-      }
-      const float svmax = fmaxf(sv[0], sv[1]);
-      if (svmax > st.sref) {
-        // Keep P * (s_V / s_ref) <= P in FP16 by raising the reference.
-        const float f = st.sref / svmax;
-#pragma unroll
-        for (int i = 0; i < 32; ++i) st.o[i] *= f;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) st.o1[i] *= f;
-        st.sref = svmax;
-      }
-      const float inv_ref = st.sref > 0.f ? __fdividef(1.f, st.sref) : 1.f;
-      rr[0] = st.sref > 0.f ? sv[0] * inv_ref : 1.f;
-      rr[1] = st.sref > 0.f ? sv[1] * inv_ref : 1.f;
-      if (np == 2)
-        pages_int8<2>(st, stg, qf, sk, rr, valid, g, t, vaddr);
-      else
-        pages_int8<1>(st, stg, qf, sk, rr, valid, g, t, vaddr);
-    } else {
-      const int valid = (has_last && warp + W * u == n_pages - 1) ? last_valid : kPage;
-      page_fp16(st, ring + (u % S) * STAGE_BYTES, qf, p.sm_scale_log2, valid, g, t, p.group);
-    }
+    const int valid = (has_last && warp + W * u == n_pages - 1) ? last_valid : kPage;
+    page_fp16(st, ring + (u % S) * STAGE_BYTES, qf, p.sm_scale_log2, valid, g, t, p.group);
     __syncwarp();
-    for (int j = 0; j < np; ++j) {
-      const int nu = u + j + S;
-      if (nu < n_w) {
-        const int id = win_id(win, nu);
-        if (lane == 0) issue_page<SEG>(tk, tv, ring, bars, (u + j) % S, id, h);
-      }
+    const int nu = u + S;
+    if (nu < n_w) {
+      const int id = win_id(win, nu);
+      if (lane == 0) issue_page_fp16(tk, tv, ring, bars, u % S, id, h);
     }
-    u += np;
+    u += 1;
     // Slide the id window once the consumer leaves its first half.
     if (win.two && u - win.base >= 32) {
       win.base += 32;
       win.id_a = win.id_b;
-      win.sk_a = win.sk_b;
-      win.sv_a = win.sv_b;
-      load_window_set<SEG>(p, sd, idx_begin, warp, W, n_w, h, win.base + 32,
-                           lane, win.id_b, win.sk_b, win.sv_b);
+      load_window_set<1>(p, sd, idx_begin, warp, W, n_w, h, win.base + 32,
+                         lane, win.id_b, win.sk_b, win.sv_b);
     }
   }
   if (!ok) {
@@ -1532,7 +1465,7 @@ __global__ void __maxnreg__(168)
     }
   } else {
     uint32_t qf[16];
-    ok = run_warp_pages<1>(p, &tm_k16, &tm_v16, st, ring, bars, qf, r, h,
+    ok = run_warp_pages_fp16(p, &tm_k16, &tm_v16, st, ring, bars, qf, r, h,
                            item.idx_begin, n_pages, has_last, warp, W, lane);
   }
   // Warps without pages skipped the wait above; everything below writes.

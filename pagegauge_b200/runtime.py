@@ -23,10 +23,6 @@ def _stream(tensor: torch.Tensor) -> int:
     return torch.cuda.current_stream(tensor.device).cuda_stream
 
 
-def _ptr(t: torch.Tensor | None) -> int | None:
-    return None if t is None else t.data_ptr()
-
-
 def check_tensor(tensor: torch.Tensor, name: str, dtype: torch.dtype, dims: int) -> None:
     """tests/page_gauge_append_extension.cu:23-32."""
     if not tensor.is_cuda:

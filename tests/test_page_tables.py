@@ -97,3 +97,33 @@ def test_exact_physical_index_agrees_with_table():
     for r in range(3):
         for lp in range(40):
             assert PT.exact_physical_page_index(r, lp, 16, 2, 4, 30) == table[r, lp].item()
+
+
+def test_old_page_table_follows_the_partition():
+    """write_page_gauge_old_page_table gathers an exact-once old set (the
+    partition's old pages with an exact prefix and a static suffix) from
+    the request-major logical table, in logical order, with the reference's
+    validation messages."""
+    import torch
+
+    from pagegauge_b200.page_table import (page_gauge_logical_partition,
+                                           request_major_page_table,
+                                           write_page_gauge_old_page_table)
+
+    logical = request_major_page_table(3, 40, device="cpu")
+    part = page_gauge_logical_partition(37, 8, 2, 5, 4, 30)
+    old = part["old_logical_pages"]
+    dest = torch.full((3, 40), -1, dtype=torch.int32)
+    got = write_page_gauge_old_page_table(dest, logical, old)
+    assert got.shape == (3, len(old))
+    for r in range(3):
+        assert got[r].tolist() == [r * 40 + p for p in old]
+    assert (dest[:, len(old):] == -1).all()
+    with pytest.raises(ValueError, match="unique and increasing"):
+        write_page_gauge_old_page_table(dest, logical, (3, 2))
+    with pytest.raises(ValueError, match="cannot be empty"):
+        write_page_gauge_old_page_table(dest, logical, ())
+    with pytest.raises(ValueError, match="exceeds allocated capacity"):
+        write_page_gauge_old_page_table(dest, logical, (39, 40))
+    with pytest.raises(ValueError, match="int32"):
+        write_page_gauge_old_page_table(dest.long(), logical, old)
