@@ -65,6 +65,8 @@ def parse_args():
     p.add_argument("--decoder-steps", type=int, default=16)
     p.add_argument("--decoder-policy", default="S0/A0/T256",
                    help="exact pages: S<sink pages>/A<static suffix pages>/T<tail tokens>")
+    p.add_argument("--decoder-tp-reduce", choices=("peer", "nccl"), default="peer",
+                   help="tensor-parallel reduction of the streaming projections")
     p.add_argument("--decoder-gemm", choices=("auto", "pg", "cublas"), default="auto",
                    help="decoder projections: weight-streaming kernels (pg), cuBLAS, or by batch")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -766,7 +768,8 @@ def parse_policy(text: str) -> tuple[int, int, int]:
 
 
 def measure_decoder(dist: Dist, batch: int, context: int = 16384, steps: int = 16,
-                    seed: int = 20261004, gemm: str = "auto", policy: str = "S0/A0/T256") -> dict:
+                    seed: int = 20261004, gemm: str = "auto", policy: str = "S0/A0/T256",
+                    tp_reduce: str = "peer") -> dict:
     """Mistral-7B-shaped random-init FP16 decoder,
     prompt of ``context`` random tokens prefilled into PageGauge caches, one
     eager warm-up decode step, then ``steps`` greedy decode steps (CUDA
@@ -782,7 +785,8 @@ def measure_decoder(dist: Dist, batch: int, context: int = 16384, steps: int = 1
     w = random_decoder_weights(cfg, seed, device="cuda", tp=TensorParallel.of(cfg, rank, world))
     sink, suffix, ring = parse_policy(policy)
     dec = PageGaugeDecoder(w, batch, max_context=context + 4 * steps + 32, process_group=pg,
-                           gemm=gemm, ring_pages=ring, sink_pages=sink, suffix_pages=suffix)
+                           gemm=gemm, ring_pages=ring, sink_pages=sink, suffix_pages=suffix,
+                           tp_reduce=tp_reduce)
     prompt = torch.randint(0, cfg.vocab, (batch, context),
                            generator=torch.Generator().manual_seed(seed + batch))
     dec.prefill(prompt.cuda())
@@ -826,7 +830,9 @@ def measure_decoder(dist: Dist, batch: int, context: int = 16384, steps: int = 1
         "roofline_frac": round(achieved / peak, 4), "prefill_s": round(prefill_s, 2),
         "replans_in_timing": 0, "params": cfg.parameter_count(), "gemm": dec.gemm_impl,
         "exact_policy": policy,
+        "tp_reduce": (None if world == 1 or dec.gemm_impl != "pg" else tp_reduce),
     }
+    dec.close()
     del dec, w
     torch.cuda.empty_cache()
     return out
@@ -839,10 +845,11 @@ def run_decoder(args, dist: Dist, local: int) -> None:
     results = {}
     with clocks:
         results[batches[0]] = measure_decoder(dist, batches[0], steps=args.decoder_steps,
-                                              gemm=args.decoder_gemm, policy=args.decoder_policy)
+                                              gemm=args.decoder_gemm, policy=args.decoder_policy,
+                                              tp_reduce=args.decoder_tp_reduce)
     for b in batches[1:]:
         results[b] = measure_decoder(dist, b, steps=args.decoder_steps, gemm=args.decoder_gemm,
-                                     policy=args.decoder_policy)
+                                     policy=args.decoder_policy, tp_reduce=args.decoder_tp_reduce)
     b32 = results[batches[0]]
     peak, peak_src = peak_hbm()
     if rank == 0:

@@ -70,6 +70,29 @@ int32_t pg_abi_version(void);
 /* Read and clear the device guard word of the current device. */
 int32_t pg_read_device_error(int32_t* code_out);
 
+/* Exchange buffer of the tensor-parallel GEMM reduction, for up to
+ * tiles_cap output tiles of 64 rows: created zeroed on the current device
+ * with a CUDA IPC handle (64 bytes) the other ranks open.                 */
+int64_t pg_tp_exchange_bytes(int32_t tiles_cap);
+int32_t pg_tp_exchange_create(int32_t tiles_cap, void** buffer_out, void* ipc_handle_out);
+int32_t pg_tp_exchange_open(const void* ipc_handle, void** buffer_out);
+int32_t pg_tp_exchange_close(void* peer_buffer);
+int32_t pg_tp_exchange_destroy(void* buffer);
+
+/* Consume a tensor-parallel GEMM's published tiles on this rank: wait
+ * (about a second at most, then PG_DEV_WAIT_TIMEOUT) until all `world`
+ * ranks' tiles of the `tiles` output tiles have arrived in this rank's
+ * `exchange` buffer, sum them in rank order (FP32; identical on every
+ * rank) and, per batch row (batch = the GEMM's rows):
+ *   residual != NULL: residual = f16(residual + f16(sum)), then out =
+ *                     RMSNorm(residual) with norm_weight (MistralRMSNorm),
+ *                     or out = residual without it
+ *   residual == NULL: out = f16(sum)                                       */
+int32_t pg_tp_reduce(const void* exchange, int32_t world, int32_t tiles_cap, int32_t tiles,
+                     int32_t batch, void* residual, int64_t residual_stride,
+                     const void* norm_weight, float eps, void* out, int64_t out_stride,
+                     void* stream);
+
 /* Device address of a page-locked, mapped host buffer (cudaHostAlloc /
  * pinned memory): kernels may take it wherever an input or output pointer
  * is expected and then read or write the host buffer directly over the
@@ -364,6 +387,17 @@ typedef struct pg_gemm_args {
                               RMS-normalised, f16(w * f16(x * rsqrt(mean(x^2)
                               + eps))) (MistralRMSNorm), inside the GEMM */
   float norm_eps;
+  /* Tensor parallelism (tp_world 2..8, mode 0): the GEMM computes this
+   * rank's partial product and publishes every finished FP32 tile into
+   * every rank's exchange buffer (NVLink peer stores; tp_peers[r] = rank
+   * r's buffer as mapped here, from pg_tp_exchange_create / _open) with an
+   * arrival flag; it writes no y.  pg_tp_reduce, launched next on each
+   * rank, sums the ranks' tiles and applies the epilogue: the row-parallel
+   * projection and its all-reduce without a collective library
+   * (o_proj / down_proj, scripts/benchmark_page_gauge_transformer.py:
+   * 2754-2804 under TP).  Every rank must launch the same sequence.       */
+  int32_t tp_world, tp_rank, tp_tiles_cap;
+  void* tp_peers[8];
 } pg_gemm_args;
 
 /* Pack W [n, k] (row stride ld, FP16) for pg_skinny_gemm with the same

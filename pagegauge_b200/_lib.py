@@ -60,6 +60,7 @@ class PgGemmArgs(ctypes.Structure):
         ("n", c_i32), ("k", c_i32), ("batch", c_i32), ("mode", c_i32), ("grid", c_i32),
         ("pdl", c_i32), ("partials", c_vp), ("partial_floats", c_i64), ("counters", c_vp),
         ("num_counters", c_i32), ("norm_weight", c_vp), ("norm_eps", ctypes.c_float),
+        ("tp_world", c_i32), ("tp_rank", c_i32), ("tp_tiles_cap", c_i32), ("tp_peers", c_vp * 8),
     ]
 
 
@@ -69,6 +70,13 @@ _SIGNATURES = {
     "pg_abi_version": (c_i32, []),
     "pg_read_device_error": (c_i32, [c_i32p]),
     "pg_host_device_pointer": (c_i32, [c_vp, ctypes.POINTER(c_vp)]),
+    "pg_tp_exchange_bytes": (c_i64, [c_i32]),
+    "pg_tp_exchange_create": (c_i32, [c_i32, ctypes.POINTER(c_vp), c_vp]),
+    "pg_tp_exchange_open": (c_i32, [c_vp, ctypes.POINTER(c_vp)]),
+    "pg_tp_exchange_close": (c_i32, [c_vp]),
+    "pg_tp_exchange_destroy": (c_i32, [c_vp]),
+    "pg_tp_reduce": (c_i32, [c_vp, c_i32, c_i32, c_i32, c_i32, c_vp, c_i64, c_vp, ctypes.c_float,
+                             c_vp, c_i64, c_vp]),
     "pg_rope_append_fp16": (c_i32, [c_vp] * 8 + [c_i64] * 3 + [c_i32] * 3 + [c_i64, c_i64, c_vp, c_i64, c_i64, c_vp]),
     "pg_rope_append_page_gauge": (
         c_i32,

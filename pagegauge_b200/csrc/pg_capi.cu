@@ -226,7 +226,54 @@ extern "C" {
 
 const char* pg_last_error(void) { return g_last_error.c_str(); }
 
-int32_t pg_abi_version(void) { return 103; }
+int32_t pg_abi_version(void) { return 104; }
+
+int64_t pg_tp_exchange_bytes(int32_t tiles_cap) {
+  return tiles_cap > 0 ? pg::tp_exchange_bytes(tiles_cap) : -1;
+}
+
+int32_t pg_tp_exchange_create(int32_t tiles_cap, void** buffer_out, void* ipc_handle_out) {
+  PG_REQUIRE(tiles_cap > 0 && tiles_cap <= (1 << 16), "tile capacity out of range");
+  PG_REQUIRE(buffer_out != nullptr && ipc_handle_out != nullptr, "null pointer");
+  void* ptr = nullptr;
+  const size_t bytes = static_cast<size_t>(pg::tp_exchange_bytes(tiles_cap));
+  int32_t rc = cuda_check(cudaMalloc(&ptr, bytes), "cudaMalloc(exchange buffer)");
+  if (rc != PG_OK) return rc;
+  rc = cuda_check(cudaMemset(ptr, 0, bytes), "cudaMemset(exchange buffer)");
+  if (rc == PG_OK) {
+    cudaIpcMemHandle_t h;
+    rc = cuda_check(cudaIpcGetMemHandle(&h, ptr), "cudaIpcGetMemHandle");
+    if (rc == PG_OK) std::memcpy(ipc_handle_out, &h, sizeof(h));
+  }
+  if (rc != PG_OK) {
+    cudaFree(ptr);
+    return rc;
+  }
+  *buffer_out = ptr;
+  return PG_OK;
+}
+
+int32_t pg_tp_exchange_open(const void* ipc_handle, void** buffer_out) {
+  PG_REQUIRE(ipc_handle != nullptr && buffer_out != nullptr, "null pointer");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, ipc_handle, sizeof(h));
+  void* ptr = nullptr;
+  int32_t rc = cuda_check(cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess),
+                          "cudaIpcOpenMemHandle");
+  if (rc != PG_OK) return rc;
+  *buffer_out = ptr;
+  return PG_OK;
+}
+
+int32_t pg_tp_exchange_close(void* peer_buffer) {
+  PG_REQUIRE(peer_buffer != nullptr, "null pointer");
+  return cuda_check(cudaIpcCloseMemHandle(peer_buffer), "cudaIpcCloseMemHandle");
+}
+
+int32_t pg_tp_exchange_destroy(void* buffer) {
+  PG_REQUIRE(buffer != nullptr, "null pointer");
+  return cuda_check(cudaFree(buffer), "cudaFree(exchange buffer)");
+}
 
 int32_t pg_host_device_pointer(const void* host, void** device_out) {
   PG_REQUIRE(host != nullptr && device_out != nullptr, "null pointer");
@@ -1149,7 +1196,11 @@ int32_t pg_skinny_gemm(const pg_gemm_args* a, void* stream) {
   PG_REQUIRE(aligned(a->w, 16) && aligned(a->x, 16), "w and x must be 16-byte aligned");
   PG_REQUIRE(a->ldx >= a->k && a->ldx % 8 == 0,
              "the x row stride must cover k and be a multiple of 8 elements");
-  if (a->mode == pg::kGemmResidual)
+  if (a->tp_world > 1)
+    PG_REQUIRE(a->mode == pg::kGemmStore,
+               "a tensor-parallel GEMM publishes its tiles (store mode); pg_tp_reduce applies "
+               "the epilogue");
+  else if (a->mode == pg::kGemmResidual)
     PG_REQUIRE(a->residual != nullptr && a->ldr >= a->n, "residual mode needs residual [batch, n]");
   else
     PG_REQUIRE(a->y != nullptr && a->ldy >= (a->mode == pg::kGemmSiluMul ? a->n / 2 : a->n),
@@ -1181,6 +1232,19 @@ int32_t pg_skinny_gemm(const pg_gemm_args* a, void* stream) {
   p.partials = a->partials;
   p.counters = a->counters;
   p.error_flag = device_error_ptr();
+  p.tp_world = 1;
+  if (a->tp_world > 1) {
+    PG_REQUIRE(a->tp_world <= pg::kGemmMaxTp && a->tp_rank >= 0 && a->tp_rank < a->tp_world,
+               "tensor-parallel world must be 2..8 with 0 <= rank < world");
+    PG_REQUIRE(a->tp_tiles_cap >= g.tiles, "exchange buffers hold fewer tiles than the output");
+    for (int r = 0; r < a->tp_world; ++r)
+      PG_REQUIRE(a->tp_peers[r] != nullptr && aligned(a->tp_peers[r], 256),
+                 "every rank's exchange buffer is required");
+    p.tp_world = a->tp_world;
+    p.tp_rank = a->tp_rank;
+    p.tp_tiles_cap = a->tp_tiles_cap;
+    for (int r = 0; r < a->tp_world; ++r) p.tp_peers[r] = static_cast<uint8_t*>(a->tp_peers[r]);
+  }
   if (a->norm_weight != nullptr) {
     PG_REQUIRE(aligned(a->norm_weight, 16), "the norm weight must be 16-byte aligned");
     PG_REQUIRE(a->norm_eps > 0.f && std::isfinite(a->norm_eps), "norm eps must be positive");
@@ -1212,6 +1276,40 @@ int32_t pg_skinny_gemm(const pg_gemm_args* a, void* stream) {
     e = norm ? cudaLaunchKernelEx(&cfg, pg::pg_skinny_gemm_kernel<4, true>, wp, tx, p)
              : cudaLaunchKernelEx(&cfg, pg::pg_skinny_gemm_kernel<4, false>, wp, tx, p);
   return cuda_check(e, "skinny gemm launch");
+}
+
+int32_t pg_tp_reduce(const void* exchange, int32_t world, int32_t tiles_cap, int32_t tiles,
+                     int32_t batch, void* residual, int64_t residual_stride,
+                     const void* norm_weight, float eps, void* out, int64_t out_stride,
+                     void* stream) {
+  PG_REQUIRE(exchange != nullptr && aligned(exchange, 256), "the exchange buffer is required");
+  PG_REQUIRE(world >= 2 && world <= pg::kGemmMaxTp, "world must be 2..8");
+  PG_REQUIRE(tiles >= 1 && tiles <= tiles_cap && tiles * pg::kGemmTileRows <= 16384,
+             "tiles must be 1..tiles_cap with at most 16384 columns");
+  PG_REQUIRE(batch >= 1 && batch <= pg::kGemmMaxXR, "batch must be 1..32");
+  PG_REQUIRE(out != nullptr && aligned(out, 16) && out_stride % 8 == 0,
+             "out must be 16-byte aligned with rows of 8k halves");
+  if (residual != nullptr)
+    PG_REQUIRE(aligned(residual, 16) && residual_stride % 8 == 0,
+               "residual must be 16-byte aligned with rows of 8k halves");
+  if (norm_weight != nullptr) {
+    PG_REQUIRE(residual != nullptr, "the RMSNorm applies to the updated residual");
+    PG_REQUIRE(aligned(norm_weight, 16) && eps > 0.f, "norm weight / eps invalid");
+  }
+  pg::TpReduceParams p{};
+  p.exchange = static_cast<const uint8_t*>(exchange);
+  p.world = world;
+  p.cap = tiles_cap;
+  p.tiles = tiles;
+  p.residual = static_cast<__half*>(residual);
+  p.residual_stride = residual_stride;
+  p.norm_w = static_cast<const __half*>(norm_weight);
+  p.eps = eps;
+  p.out = static_cast<__half*>(out);
+  p.out_stride = out_stride;
+  p.error_flag = device_error_ptr();
+  return launch_pdl(pg::pg_tp_reduce_kernel, dim3(batch), dim3(pg::kTpReduceThreads), 0,
+                    static_cast<cudaStream_t>(stream), "tp reduce launch", p);
 }
 
 // --------------------------------------------- allocation-free decode

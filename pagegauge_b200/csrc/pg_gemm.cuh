@@ -41,6 +41,24 @@
 namespace pg {
 
 constexpr int kGemmTileRows = 64;  // W rows per output tile
+constexpr int kGemmMaxTp = 8;      // ranks of a peer-memory tile exchange
+constexpr int kGemmMaxXR = 32;     // activation rows of the widest instantiation
+
+// Exchange buffer of one rank (identical layout on every rank):
+//   seq  [cap] int32   exchanges of each output tile completed on this rank
+//   recv [2][kGemmMaxTp][cap][64 * kGemmMaxXR] (value, tag) pairs: the
+//        tiles by source rank, double-buffered by exchange parity; every
+//        FP32 value travels with the exchange count as its tag in one
+//        8-byte store, so a reader knows a value has arrived from the value
+//        itself (no separate flag, no fence).
+__host__ __device__ constexpr int64_t tp_seq_offset(int) { return 0; }
+__host__ __device__ constexpr int64_t tp_recv_offset(int cap) {
+  return (static_cast<int64_t>(cap) * 4 + 255) / 256 * 256;
+}
+__host__ __device__ constexpr int64_t tp_slot_pairs() { return kGemmTileRows * kGemmMaxXR; }
+__host__ __device__ constexpr int64_t tp_exchange_bytes(int cap) {
+  return tp_recv_offset(cap) + static_cast<int64_t>(2) * kGemmMaxTp * cap * tp_slot_pairs() * 8;
+}
 constexpr int kGemmBK = 64;        // k per stage: 128-byte rows
 // Ring depth: enough weight bytes in flight per SM at the CTAs per SM the
 // shared memory allows (3 at 9 KB stages, 2 at 10-12 KB stages).
@@ -64,6 +82,11 @@ struct GemmParams {
   float* partials;   // [grid * max_seg][64][8*NT]
   int32_t* counters; // [tiles], zero between launches
   int* error_flag;
+  // Tensor-parallel reduction of the finished tiles (world > 1): every
+  // rank's exchange buffer as mapped on this rank (peer memory over NVLink,
+  // this rank's own included), laid out as pg_tp_exchange_layout describes.
+  int32_t tp_world, tp_rank, tp_tiles_cap;
+  uint8_t* tp_peers[kGemmMaxTp];
   // Fused RMSNorm prologue (null: none): the GEMM's input is
   // f16(norm_w * f16(x * rsqrt(mean(x^2) + eps))) of the rows of x.
   const __half* norm_w;
@@ -150,6 +173,55 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, int tile, Src
   }
 }
 
+// Tensor-parallel publication of a finished tile: store this rank's FP32
+// tile (the batch rows only) into every rank's exchange buffer, each value
+// paired with the tile's exchange count in one 8-byte store (plain peer
+// stores over NVLink, this rank's own buffer included).  Nothing waits
+// here: the ranks' tiles are summed by the kernel that consumes the result
+// (pg_tp_reduce_kernel), which waits for the tags, so the GEMM's stream-K
+// CTAs never stall on another GPU.  Consecutive exchanges of a tile
+// alternate halves of the receive buffer; a rank can be at most one
+// exchange ahead of another, because its next exchange's inputs depend on
+// this one's reduction on every rank.
+// (value, tag) as one 64-bit scalar access, which is single-copy atomic:
+// a reader never sees a tag without its value.
+__device__ __forceinline__ uint2 ld_pair_relaxed_sys(const uint2* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return make_uint2(static_cast<uint32_t>(v), static_cast<uint32_t>(v >> 32));
+}
+
+__device__ __forceinline__ void st_pair_relaxed_sys(uint2* p, float v, int32_t tag) {
+  const unsigned long long w = static_cast<unsigned long long>(__float_as_uint(v)) |
+                               (static_cast<unsigned long long>(static_cast<uint32_t>(tag)) << 32);
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+
+template <int NT>
+__device__ __forceinline__ void gemm_tp_push(const GemmParams& p, int tile, const float* s_tile) {
+  constexpr int XR = 8 * NT;
+  constexpr int ES = XR + 1;
+  __shared__ int s_seq;
+  const int cap = p.tp_tiles_cap;
+  const int batch = p.batch;
+  int32_t* my_seq = reinterpret_cast<int32_t*>(p.tp_peers[p.tp_rank] + tp_seq_offset(cap));
+  if (threadIdx.x == 0) s_seq = my_seq[tile];
+  __syncthreads();
+  const int32_t seq = s_seq + 1;
+  const int64_t slot = (static_cast<int64_t>(seq & 1) * kGemmMaxTp + p.tp_rank) * cap + tile;
+  const int n = kGemmTileRows * batch;
+  for (int dst = 0; dst < p.tp_world; ++dst) {
+    uint2* out = reinterpret_cast<uint2*>(p.tp_peers[dst] + tp_recv_offset(cap)) +
+                 slot * tp_slot_pairs();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const int j = i / batch, b = i - j * batch;
+      st_pair_relaxed_sys(out + i, s_tile[j * ES + b], seq);
+    }
+  }
+  if (threadIdx.x == 0) my_seq[tile] = seq;
+  __syncthreads();
+}
+
 // Finish this CTA's segment [kb0, kb1) of tile `tile`: the whole tile goes
 // straight to the epilogue; a part is written to the CTA's partial slot and
 // the last contributor to arrive sums the tile's slots in CTA order.
@@ -171,7 +243,10 @@ __device__ __forceinline__ void gemm_flush(const GemmParams& p, const float (&ac
       s_tile[(row + 8) * ES + col + 1] = acc[i][3];
     }
     __syncthreads();
-    gemm_epilogue<NT>(p, tile, [&](int j, int b) { return s_tile[j * ES + b]; });
+    if (p.tp_world > 1)
+      gemm_tp_push<NT>(p, tile, s_tile);
+    else
+      gemm_epilogue<NT>(p, tile, [&](int j, int b) { return s_tile[j * ES + b]; });
     __syncthreads();
     return;
   }
@@ -230,7 +305,10 @@ __device__ __forceinline__ void gemm_flush(const GemmParams& p, const float (&ac
       s_tile[row * ES + col + 3] = acc4.w;
     }
     __syncthreads();
-    gemm_epilogue<NT>(p, tile, [&](int j, int b) { return s_tile[j * ES + b]; });
+    if (p.tp_world > 1)
+      gemm_tp_push<NT>(p, tile, s_tile);
+    else
+      gemm_epilogue<NT>(p, tile, [&](int j, int b) { return s_tile[j * ES + b]; });
   }
   __syncthreads();
 }
@@ -421,6 +499,136 @@ __global__ void __launch_bounds__(kGemmWarps * 32)
     return;
   }
   gemm_flush<NT>(p, acc, cur, seg_kb0, ckb, seg, s_tile, &s_last, s_seg);
+}
+
+// Consumer of a tensor-parallel GEMM's published tiles: one CTA of 512
+// threads per batch row b.  It waits (bounded) until every rank's tile of
+// every output tile has arrived, sums them in rank order in FP32 and then
+//   residual != null: r = f16(r + f16(sum)); with norm_w, out = RMSNorm(r)
+//   residual == null: out = f16(sum)
+// (the all-reduce and the decoder's residual add + RMSNorm in one launch).
+struct TpReduceParams {
+  const uint8_t* exchange;  // this rank's exchange buffer
+  int32_t world, cap, tiles;
+  __half* residual;
+  int64_t residual_stride;
+  const __half* norm_w;
+  float eps;
+  __half* out;
+  int64_t out_stride;
+  int* error_flag;
+};
+
+constexpr int kTpReduceThreads = 512;
+
+__global__ void __launch_bounds__(kTpReduceThreads)
+    pg_tp_reduce_kernel(const __grid_constant__ TpReduceParams p) {
+  __shared__ float part[kTpReduceThreads / 32];
+  pdl_launch_dependents();
+  pdl_wait_primary();  // the producer GEMM's own pushes and counters
+  const int b = blockIdx.x;
+  const int cap = p.cap;
+  const int32_t* seq = reinterpret_cast<const int32_t*>(p.exchange + tp_seq_offset(cap));
+  const uint2* recv = reinterpret_cast<const uint2*>(p.exchange + tp_recv_offset(cap));
+  const int n = p.tiles * kGemmTileRows;
+  const int batch = gridDim.x;
+  // Thread-owned 8-column chunks, as the add_rmsnorm kernel.
+  constexpr int kMaxChunks = 4;  // n <= 4 * 8 * 512
+  uint4 x[kMaxChunks];
+  float ss = 0.f;
+  bool ok = true;
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c) {
+    const int col = (c * kTpReduceThreads + threadIdx.x) * 8;
+    if (col >= n) break;
+    const int t = col / kGemmTileRows, j0 = col % kGemmTileRows;
+    const int32_t want = __ldcg(seq + t);
+    const int par = want & 1;
+    float d[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) d[e] = 0.f;
+    for (int src = 0; src < p.world; ++src) {
+      const uint2* slot = recv + ((static_cast<int64_t>(par) * kGemmMaxTp + src) * cap + t) *
+                                     tp_slot_pairs();
+      // All eight loads in flight, then re-read only values whose tag is not
+      // yet this exchange's count (not arrived), for about a second at most.
+      uint2 v[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = ld_pair_relaxed_sys(slot + (j0 + e) * batch + b);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        for (uint32_t spin = 0; ok && static_cast<int32_t>(v[e].y) != want; ++spin) {
+          if (spin == (1u << 24)) {
+            ok = false;
+            break;
+          }
+          __nanosleep(32);
+          v[e] = ld_pair_relaxed_sys(slot + (j0 + e) * batch + b);
+        }
+        d[e] += __uint_as_float(v[e].x);
+      }
+    }
+    uint32_t* xw = reinterpret_cast<uint32_t*>(&x[c]);
+    if (p.residual != nullptr) {
+      __half* res = p.residual + b * p.residual_stride + col;
+      const uint4 r = *reinterpret_cast<const uint4*>(res);
+      const uint32_t* rw = reinterpret_cast<const uint32_t*>(&r);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const __half2 s2 = __hadd2(*reinterpret_cast<const __half2*>(&rw[e]),
+                                   __floats2half2_rn(d[2 * e], d[2 * e + 1]));
+        xw[e] = *reinterpret_cast<const uint32_t*>(&s2);
+      }
+      *reinterpret_cast<uint4*>(res) = x[c];
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const __half2 s2 = __floats2half2_rn(d[2 * e], d[2 * e + 1]);
+        xw[e] = *reinterpret_cast<const uint32_t*>(&s2);
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&xw[e]));
+      ss = fmaf(f.x, f.x, ss);
+      ss = fmaf(f.y, f.y, ss);
+    }
+  }
+  if (!ok) record_error(p.error_flag, kDevWaitTimeout);
+  float inv = 1.f;
+  if (p.norm_w != nullptr) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float total = 0.f;
+#pragma unroll
+    for (int w = 0; w < kTpReduceThreads / 32; ++w) total += part[w];
+    inv = rsqrtf(total / static_cast<float>(n) + p.eps);
+  }
+  __half* out = p.out + b * p.out_stride;
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c) {
+    const int col = (c * kTpReduceThreads + threadIdx.x) * 8;
+    if (col >= n) break;
+    if (p.norm_w == nullptr) {
+      *reinterpret_cast<uint4*>(out + col) = x[c];
+      continue;
+    }
+    const uint4 wv = *reinterpret_cast<const uint4*>(p.norm_w + col);
+    const uint32_t* xw = reinterpret_cast<const uint32_t*>(&x[c]);
+    const uint32_t* ww = reinterpret_cast<const uint32_t*>(&wv);
+    uint4 y;
+    uint32_t* yw = reinterpret_cast<uint32_t*>(&y);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&xw[e]));
+      const __half2 nrm = __floats2half2_rn(f.x * inv, f.y * inv);
+      const __half2 r = __hmul2(*reinterpret_cast<const __half2*>(&ww[e]), nrm);
+      yw[e] = *reinterpret_cast<const uint32_t*>(&r);
+    }
+    *reinterpret_cast<uint4*>(out + col) = y;
+  }
 }
 
 // Weight packing: W [n, k] (row stride ld) -> [tiles][k/64][64][64] with the

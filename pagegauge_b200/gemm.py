@@ -63,12 +63,16 @@ class SkinnyGemm:
     def __call__(self, x: torch.Tensor, w: PackedWeight, out: torch.Tensor | None = None,
                  mode: int = STORE, residual: torch.Tensor | None = None, pdl: bool = True,
                  grid: int = 0, norm_weight: torch.Tensor | None = None,
-                 eps: float = 1e-5) -> torch.Tensor | None:
+                 eps: float = 1e-5, tp=None) -> torch.Tensor | None:
         """y = x @ W^T with W packed for this ``mode`` (silu_mul needs the
         silu_mul packing; store and residual share theirs).  ``norm_weight``
         ([k] float16) first RMS-normalises the rows of x inside the GEMM
         (transformers' MistralRMSNorm: f16(w * f16(x * rsqrt(mean(x^2) +
-        eps))))."""
+        eps)))).  ``tp`` (a ``peer.TpExchange``, store mode): this rank's
+        product is a partial sum; every finished tile is published to every
+        rank through peer memory and nothing is written here -- the next
+        ``tp.reduce`` sums the ranks' tiles (the row-parallel projection and
+        its all-reduce without a collective library)."""
         if x.dtype != torch.float16 or x.dim() != 2 or x.stride(1) != 1:
             raise ValueError("x must be a float16 [batch, k] tensor with contiguous rows")
         if (w.mode == SILU_MUL) != (mode == SILU_MUL):
@@ -80,7 +84,10 @@ class SkinnyGemm:
         a = _lib.PgGemmArgs()
         a.w, a.ldw = w.data.data_ptr(), w.k
         a.x, a.ldx = x.data_ptr(), x.stride(0)
-        if mode == RESIDUAL:
+        if tp is not None:
+            if mode != STORE:
+                raise ValueError("a tensor-parallel GEMM publishes its tiles (store mode)")
+        elif mode == RESIDUAL:
             if residual is None or residual.shape != (batch, n) or residual.stride(1) != 1:
                 raise ValueError("residual mode needs residual [batch, n]")
             a.residual, a.ldr = residual.data_ptr(), residual.stride(0)
@@ -94,6 +101,8 @@ class SkinnyGemm:
         a.n, a.k, a.batch, a.mode, a.grid, a.pdl = n, k, batch, mode, grid, int(pdl)
         a.partials, a.partial_floats = self.partials.data_ptr(), self.partials.numel()
         a.counters, a.num_counters = self.counters.data_ptr(), self.counters.numel()
+        if tp is not None:
+            tp.fill(a)
         if norm_weight is not None:
             if (norm_weight.dtype != torch.float16 or norm_weight.shape != (k,)
                     or not norm_weight.is_contiguous()):
@@ -102,4 +111,6 @@ class SkinnyGemm:
                 raise ValueError("the normalised x must be 16-byte aligned with rows of 8k halves")
             a.norm_weight, a.norm_eps = norm_weight.data_ptr(), float(eps)
         _lib.check(_lib.load().pg_skinny_gemm(ctypes.byref(a), _stream()))
+        if tp is not None:
+            return None
         return out if mode != RESIDUAL else residual

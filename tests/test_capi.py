@@ -43,7 +43,7 @@ def test_every_declared_symbol_is_exported(lib):
 def test_struct_sizes_match_header_layout(lib):
     assert ctypes.sizeof(_lib.PgDecodeItem) == 16
     assert ctypes.sizeof(_lib.PgSegment) == 56
-    assert lib.pg_abi_version() == 103
+    assert lib.pg_abi_version() == 104
 
 
 def test_planner_chunks_and_offsets(lib):

@@ -1,7 +1,9 @@
-"""Tensor-parallel PageGauge decoder on two GPUs (NCCL): each rank holds half
-of the KV heads, FFN columns and vocabulary; the gathered logits of the
+"""Tensor-parallel PageGauge decoder on two GPUs: each rank holds half of
+the KV heads, FFN columns and vocabulary; the gathered logits of the
 prefill and of graph-captured decode steps must match the single-model
-CPU oracle.  Skipped unless two GPUs are visible."""
+CPU oracle.  The streaming-GEMM decoder reduces o_proj / down_proj through
+peer memory inside the GEMM; the cuBLAS decoder uses NCCL all-reduces.
+Skipped unless two GPUs are visible."""
 
 from __future__ import annotations
 
@@ -25,7 +27,7 @@ def _cfg():
     return DecoderConfig(layers=2, hidden=512, heads=8, kv_heads=2, intermediate=1024, vocab=512)
 
 
-def _rank(rank, port, prompt, result):
+def _rank(rank, port, prompt, result, gemm):
     import torch.distributed as dist
 
     from pagegauge_b200.decoder import PageGaugeDecoder, TensorParallel, random_decoder_weights
@@ -40,7 +42,8 @@ def _rank(rank, port, prompt, result):
         w = random_decoder_weights(cfg, 41, device="cuda", gen_device="cpu",
                                    tp=TensorParallel.of(cfg, rank, WORLD))
         dec = PageGaugeDecoder(w, batch=prompt.shape[0], max_context=512,
-                               process_group=dist.group.WORLD)
+                               process_group=dist.group.WORLD, gemm=gemm)
+        assert (dec.tpx is not None) == (gemm == "pg")
         logits = [dec.prefill(prompt.cuda()).float()]
         tokens = [dec.tokens.clone()]
         # This rank's caches after the prefill (its KV heads), for the oracle.
@@ -67,14 +70,18 @@ def _rank(rank, port, prompt, result):
                      tokens=torch.stack(tokens).cpu().numpy(),
                      cos=dec.cos.cpu().numpy(), sin=dec.sin.cpu().numpy(),
                      capacity=dec.capacity_pages, **full)
+        from pagegauge_b200.runtime import read_device_error
+        assert read_device_error() == 0
         dist.barrier()
+        dec.close()
         del dec
     finally:
         dist.destroy_process_group()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs two GPUs")
-def test_two_gpu_tensor_parallel_decoder_matches_oracle(cuda_lib, tmp_path):
+@pytest.mark.parametrize("gemm", ["pg", "cublas"])
+def test_two_gpu_tensor_parallel_decoder_matches_oracle(cuda_lib, tmp_path, gemm):
     from oracle import decoder_oracle as D
     from oracle import pagegauge_oracle as O
 
@@ -86,7 +93,7 @@ def test_two_gpu_tensor_parallel_decoder_matches_oracle(cuda_lib, tmp_path):
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
     path = str(tmp_path / "tp.npz")
-    mp.spawn(_rank, args=(port, prompt, path), nprocs=WORLD, join=True)
+    mp.spawn(_rank, args=(port, prompt, path, gemm), nprocs=WORLD, join=True)
     got = np.load(path)
     logits, tokens = got["logits"], got["tokens"]
     w, ocfg = oracle_weights(cfg, seed=41), oracle_cfg(cfg)
