@@ -183,19 +183,31 @@ __device__ __forceinline__ void gemm_epilogue(const GemmParams& p, int tile, Src
 // alternate halves of the receive buffer; a rank can be at most one
 // exchange ahead of another, because its next exchange's inputs depend on
 // this one's reduction on every rank.
-// (value, tag) as one 64-bit scalar access, which is single-copy atomic:
-// a reader never sees a tag without its value.
+// (value, tag) as one 64-bit access, which is single-copy atomic: a reader
+// never sees a tag without its value.  The two-element forms move two such
+// pairs per instruction (each element still one atomic 64-bit access).
+__device__ __forceinline__ void ld_pairs2_relaxed_sys(const uint2* p, uint2& a, uint2& b) {
+  unsigned long long x, y;
+  asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(x), "=l"(y) : "l"(p)
+               : "memory");
+  a = make_uint2(static_cast<uint32_t>(x), static_cast<uint32_t>(x >> 32));
+  b = make_uint2(static_cast<uint32_t>(y), static_cast<uint32_t>(y >> 32));
+}
+
+__device__ __forceinline__ void st_pairs2_relaxed_sys(uint2* p, float v0, float v1, int32_t tag) {
+  const unsigned long long t = static_cast<unsigned long long>(static_cast<uint32_t>(tag)) << 32;
+  const unsigned long long x = static_cast<unsigned long long>(__float_as_uint(v0)) | t;
+  const unsigned long long y = static_cast<unsigned long long>(__float_as_uint(v1)) | t;
+  asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(x), "l"(y)
+               : "memory");
+}
+
 __device__ __forceinline__ uint2 ld_pair_relaxed_sys(const uint2* p) {
   unsigned long long v;
   asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return make_uint2(static_cast<uint32_t>(v), static_cast<uint32_t>(v >> 32));
 }
 
-__device__ __forceinline__ void st_pair_relaxed_sys(uint2* p, float v, int32_t tag) {
-  const unsigned long long w = static_cast<unsigned long long>(__float_as_uint(v)) |
-                               (static_cast<unsigned long long>(static_cast<uint32_t>(tag)) << 32);
-  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
-}
 
 template <int NT>
 __device__ __forceinline__ void gemm_tp_push(const GemmParams& p, int tile, const float* s_tile) {
@@ -209,13 +221,15 @@ __device__ __forceinline__ void gemm_tp_push(const GemmParams& p, int tile, cons
   __syncthreads();
   const int32_t seq = s_seq + 1;
   const int64_t slot = (static_cast<int64_t>(seq & 1) * kGemmMaxTp + p.tp_rank) * cap + tile;
-  const int n = kGemmTileRows * batch;
+  // Slot layout [batch row][64 output columns]: a reader's row is contiguous.
+  const int n2 = kGemmTileRows / 2 * batch;
   for (int dst = 0; dst < p.tp_world; ++dst) {
     uint2* out = reinterpret_cast<uint2*>(p.tp_peers[dst] + tp_recv_offset(cap)) +
                  slot * tp_slot_pairs();
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-      const int j = i / batch, b = i - j * batch;
-      st_pair_relaxed_sys(out + i, s_tile[j * ES + b], seq);
+    for (int i = threadIdx.x; i < n2; i += blockDim.x) {
+      const int b = i / (kGemmTileRows / 2), j = 2 * (i - b * (kGemmTileRows / 2));
+      st_pairs2_relaxed_sys(out + b * kGemmTileRows + j, s_tile[j * ES + b],
+                            s_tile[(j + 1) * ES + b], seq);
     }
   }
   if (threadIdx.x == 0) my_seq[tile] = seq;
@@ -552,9 +566,10 @@ __global__ void __launch_bounds__(kTpReduceThreads)
                                      tp_slot_pairs();
       // All eight loads in flight, then re-read only values whose tag is not
       // yet this exchange's count (not arrived), for about a second at most.
+      const uint2* row = slot + b * kGemmTileRows + j0;  // 8 contiguous pairs (64 B)
       uint2 v[8];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) v[e] = ld_pair_relaxed_sys(slot + (j0 + e) * batch + b);
+      for (int e = 0; e < 8; e += 2) ld_pairs2_relaxed_sys(row + e, v[e], v[e + 1]);
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         for (uint32_t spin = 0; ok && static_cast<int32_t>(v[e].y) != want; ++spin) {
@@ -563,7 +578,7 @@ __global__ void __launch_bounds__(kTpReduceThreads)
             break;
           }
           __nanosleep(32);
-          v[e] = ld_pair_relaxed_sys(slot + (j0 + e) * batch + b);
+          v[e] = ld_pair_relaxed_sys(row + e);
         }
         d[e] += __uint_as_float(v[e].x);
       }
