@@ -27,8 +27,10 @@ SOURCE = Path("tests") / "page_gauge_append_extension.cu"
 
 def main() -> int:
     parser = argparse.ArgumentParser(description=__doc__)
-    parser.add_argument("--reference", type=Path,
-                        default=Path(os.environ.get("PAGEGAUGE_REFERENCE", "/root/reference")))
+    # Default: $PAGEGAUGE_REFERENCE, else a "reference" checkout beside this
+    # repository.
+    default = os.environ.get("PAGEGAUGE_REFERENCE") or str(HERE.parent.parent / "reference")
+    parser.add_argument("--reference", type=Path, default=Path(default))
     args = parser.parse_args()
     src = args.reference / SOURCE
     if not src.is_file():
