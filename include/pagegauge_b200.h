@@ -67,6 +67,11 @@ const char* pg_last_error(void);
 /* ABI version (major*100 + minor). */
 int32_t pg_abi_version(void);
 
+/* sizeof of pg_decode_args, pg_gemm_args, pg_segment, pg_plan_info and
+ * pg_decode_item as compiled into the library (a binding checks its own
+ * structure layouts against these before the first call).                */
+int32_t pg_struct_sizes(int64_t* out, int32_t n);
+
 /* Read and clear the device guard word of the current device. */
 int32_t pg_read_device_error(int32_t* code_out);
 

@@ -69,6 +69,7 @@ _SIGNATURES = {
     "pg_last_error": (ctypes.c_char_p, []),
     "pg_abi_version": (c_i32, []),
     "pg_read_device_error": (c_i32, [c_i32p]),
+    "pg_struct_sizes": (c_i32, [ctypes.POINTER(c_i64), c_i32]),
     "pg_host_device_pointer": (c_i32, [c_vp, ctypes.POINTER(c_vp)]),
     "pg_tp_exchange_bytes": (c_i64, [c_i32]),
     "pg_tp_exchange_create": (c_i32, [c_i32, ctypes.POINTER(c_vp), c_vp]),
@@ -144,6 +145,15 @@ def load() -> ctypes.CDLL:
         fn = getattr(lib, name)
         fn.restype = restype
         fn.argtypes = argtypes
+    # The argument blocks cross the boundary by pointer: their layouts must
+    # match the library's exactly.
+    sizes = (c_i64 * 5)()
+    if lib.pg_struct_sizes(sizes, 5) != 0:
+        raise RuntimeError("pg_struct_sizes failed")
+    mine = (ctypes.sizeof(PgDecodeArgs), ctypes.sizeof(PgGemmArgs), ctypes.sizeof(PgSegment),
+            ctypes.sizeof(PgPlanInfo), ctypes.sizeof(PgDecodeItem))
+    if tuple(sizes) != mine:
+        raise RuntimeError(f"C ABI structure sizes {tuple(sizes)} differ from the binding's {mine}")
     _lib = lib
     return lib
 

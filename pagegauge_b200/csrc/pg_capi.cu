@@ -226,7 +226,7 @@ extern "C" {
 
 const char* pg_last_error(void) { return g_last_error.c_str(); }
 
-int32_t pg_abi_version(void) { return 104; }
+int32_t pg_abi_version(void) { return 105; }
 
 int64_t pg_tp_exchange_bytes(int32_t tiles_cap) {
   return tiles_cap > 0 ? pg::tp_exchange_bytes(tiles_cap) : -1;
@@ -282,6 +282,16 @@ int32_t pg_host_device_pointer(const void* host, void** device_out) {
                           "cudaHostGetDevicePointer (the buffer must be page-locked and mapped)");
   if (rc != PG_OK) return rc;
   *device_out = d;
+  return PG_OK;
+}
+
+int32_t pg_struct_sizes(int64_t* out, int32_t n) {
+  PG_REQUIRE(out != nullptr && n >= 5, "need room for 5 sizes");
+  out[0] = sizeof(pg_decode_args);
+  out[1] = sizeof(pg_gemm_args);
+  out[2] = sizeof(pg_segment);
+  out[3] = sizeof(pg_plan_info);
+  out[4] = sizeof(pg_decode_item);
   return PG_OK;
 }
 

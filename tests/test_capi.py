@@ -43,7 +43,12 @@ def test_every_declared_symbol_is_exported(lib):
 def test_struct_sizes_match_header_layout(lib):
     assert ctypes.sizeof(_lib.PgDecodeItem) == 16
     assert ctypes.sizeof(_lib.PgSegment) == 56
-    assert lib.pg_abi_version() == 104
+    sizes = (ctypes.c_int64 * 5)()
+    assert lib.pg_struct_sizes(sizes, 5) == 0
+    assert tuple(sizes) == (ctypes.sizeof(_lib.PgDecodeArgs), ctypes.sizeof(_lib.PgGemmArgs),
+                            ctypes.sizeof(_lib.PgSegment), ctypes.sizeof(_lib.PgPlanInfo),
+                            ctypes.sizeof(_lib.PgDecodeItem))
+    assert lib.pg_abi_version() == 105
 
 
 def test_planner_chunks_and_offsets(lib):
