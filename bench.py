@@ -776,6 +776,7 @@ def measure_decoder(dist: Dist, batch: int, context: int = 16384, steps: int = 1
     graphs prepared beforehand), tensor-parallel over the ranks."""
     from pagegauge_b200.decoder import (DecoderConfig, PageGaugeDecoder, TensorParallel,
                                         random_decoder_weights)
+    from pagegauge_b200.runtime import read_device_error
 
     world = dist.world
     rank = int(os.environ.get("RANK", "0"))
@@ -831,6 +832,7 @@ def measure_decoder(dist: Dist, batch: int, context: int = 16384, steps: int = 1
         "replans_in_timing": 0, "params": cfg.parameter_count(), "gemm": dec.gemm_impl,
         "exact_policy": policy,
         "tp_reduce": (None if world == 1 or dec.gemm_impl != "pg" else tp_reduce),
+        "device_guard": read_device_error(),
     }
     dec.close()
     del dec, w
