@@ -4,9 +4,11 @@ ceil(pages / split)) per (batch, context) bucket from measured timings.
 The reference froze one ``fixed_split_size`` per method from a pilot sweep
 over {auto, 64, 128, 256, 512} pages, keeping the cache-neutral p50 argmin
 (scripts/run_page_gauge_validation.py:277-316, B1/49K at :374-416).  Here
-the sweep covers num_splits 1..64 per KV head (and the heuristic), each
-candidate timed on the GPU with a >= 256 MiB scrub before every sample, and
-the argmin is stored per bucket in ``split_table.json`` next to this file.
+the sweep covers num_splits 1..64 per KV head (and the one-wave
+heuristic), each candidate timed on the GPU as a decoder runs it (back to
+back over caches larger than the L2; ``--mode burst`` times single decodes
+behind a 256 MiB scrub instead), and the argmin is stored per (batch,
+half-octave context) bucket in ``split_table.json`` next to this file.
 
     python -m pagegauge_b200.scheduler --sweep [--batch 1 --context 49152]
 """
