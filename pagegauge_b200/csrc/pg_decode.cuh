@@ -1430,6 +1430,12 @@ __global__ void __maxnreg__(168)
     }
   }
   __syncwarp();
+  // The dependent grid (the merge, or the next launch) may be scheduled as
+  // soon as every CTA of this one has started: its CTAs take SM slots as
+  // this grid's CTAs exit and start their own prologue (plan data, first
+  // cache tiles) during this grid's drain; they wait for this grid's
+  // completion before reading anything it writes.
+  pdl_launch_dependents();
 
   WarpState st;
   st.m0 = st.m1 = kNegInf;
@@ -1470,8 +1476,6 @@ __global__ void __maxnreg__(168)
   }
   // Warps without pages skipped the wait above; everything below writes.
   pdl_wait_primary();
-  // Let a dependent (merge) grid start launching while we finish.
-  pdl_launch_dependents();
 
   // Per-warp totals.  FP16 and affine paths: rows 2t/2t+1, reduce l over
   // the 8 token lanes.  INT8 PageGauge path: row g, reduce l over the 4
