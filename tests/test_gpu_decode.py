@@ -385,3 +385,44 @@ def test_zero_copy_host_inputs_and_output(cuda_lib):
                                            cache.value_center, rq, cache.exact_key,
                                            cache.exact_value, cache.key_codes, cache.value_codes,
                                            cache.key_scales, cache.value_scales, 0)
+
+
+def test_b1_49k_full_size(cuda_lib):
+    """configs[1] at its full size (3,056 INT8 pages + the 16-page tail,
+    the benchmark's measured split): two KV heads' query rows against the
+    float64 oracle, and a size-independent property -- storing the INT8
+    pages in a different physical order (page table permuted to match)
+    gives bit-identical outputs."""
+    from pagegauge_b200 import scheduler
+
+    lengths = [49152]
+    q, dk, dv, cache, tables = make_case(lengths, seed=20261001)
+    split = scheduler.lookup(1, 49152)
+    out, lse, dec = run_fused(q, cache, tables, split_old=split)
+    assert dec.work_plan.num_items <= 444  # one wave on 148 SMs at 3 CTAs/SM
+    heads = (0, 5)
+    ck, cv = cpu(cache.key_codes), cpu(cache.value_codes)
+    sk, sv = cpu(cache.key_scales), cpu(cache.value_scales)
+    ek, ev = cpu(cache.exact_key), cpu(cache.exact_value)
+    o_ptr, e_ptr = cpu(tables.old_indptr), cpu(tables.exact_indptr)
+    old_ids = cpu(tables.old_indices)[o_ptr[0]:o_ptr[1]]
+    ex_ids = cpu(tables.exact_indices)[e_ptr[0]:e_ptr[1]]
+    for h in heads:
+        hs = slice(h, h + 1)
+        exp, exp_lse = O.page_gauge_decode(
+            cpu(q[0, 4 * h:4 * h + 4]), ck[:, :, hs], cv[:, :, hs], sk[:, hs], sv[:, hs],
+            old_ids, tables.old_tokens[0], ek[:, :, hs], ev[:, :, hs], ex_ids,
+            tables.exact_tokens[0], cpu(cache.value_center[0, hs]), 128 ** -0.5)
+        assert_close_decode(out[0, 4 * h:4 * h + 4], exp)
+        np.testing.assert_allclose(cpu(lse[0, 4 * h:4 * h + 4]), exp_lse, atol=LSE_ATOL, rtol=0)
+    # Physical permutation of the INT8 pages.
+    n = cache.key_codes.shape[0]
+    perm = torch.randperm(n, generator=torch.Generator().manual_seed(3)).cuda()
+    inv = torch.empty_like(perm)
+    inv[perm] = torch.arange(n, device="cuda")
+    for name in ("key_codes", "value_codes", "key_scales", "value_scales"):
+        t = getattr(cache, name)
+        t.copy_(t[perm].clone())  # page p now lives at inv[p]
+    tables.old_indices.copy_(inv[tables.old_indices.long()].int())
+    out2, lse2, _ = run_fused(q, cache, tables, split_old=split)
+    assert torch.equal(out, out2) and torch.equal(lse, lse2)
