@@ -426,3 +426,48 @@ def test_b1_49k_full_size(cuda_lib):
     tables.old_indices.copy_(inv[tables.old_indices.long()].int())
     out2, lse2, _ = run_fused(q, cache, tables, split_old=split)
     assert torch.equal(out, out2) and torch.equal(lse, lse2)
+
+
+def test_b8_ragged_full_size_and_shards(cuda_lib):
+    """configs[2] at its full size: every request's first KV head against
+    the float64 oracle, and the per-rank shards of a 2-GPU run (decoded here
+    one after the other on one GPU, each its own batch over the same pages)
+    reproduce the whole batch's outputs within the tolerance after the host
+    gather."""
+    from pagegauge_b200.shard import gather_outputs, ragged_lengths, shard_requests
+
+    lengths = ragged_lengths(8, 20261001)
+    q, dk, dv, cache, tables = make_case(lengths, seed=20261002)
+    out, _, _ = run_fused(q, cache, tables)
+    ck, cv = cpu(cache.key_codes), cpu(cache.value_codes)
+    sk, sv = cpu(cache.key_scales), cpu(cache.value_scales)
+    ek, ev = cpu(cache.exact_key), cpu(cache.exact_value)
+    o_ptr, e_ptr = cpu(tables.old_indptr), cpu(tables.exact_indptr)
+    o_idx, e_idx = cpu(tables.old_indices), cpu(tables.exact_indices)
+    for r in range(len(lengths)):
+        exp, _ = O.page_gauge_decode(cpu(q[r, 0:4]), ck[:, :, :1], cv[:, :, :1], sk[:, :1],
+                                     sv[:, :1], o_idx[o_ptr[r]:o_ptr[r + 1]],
+                                     tables.old_tokens[r], ek[:, :, :1], ev[:, :, :1],
+                                     e_idx[e_ptr[r]:e_ptr[r + 1]], tables.exact_tokens[r],
+                                     cpu(cache.value_center[r, :1]), 128 ** -0.5)
+        assert_close_decode(out[r, 0:4], exp)
+    shards = shard_requests(lengths, 2)
+    parts = []
+    for idx in shards:
+        def sub(ptr, ids):
+            rows = [ids[ptr[r]:ptr[r + 1]] for r in idx]
+            indptr = np.concatenate([[0], np.cumsum([len(x) for x in rows])]).astype(np.int32)
+            return torch.from_numpy(indptr), torch.from_numpy(np.concatenate(rows)).cuda()
+        so_ptr, so_idx = sub(o_ptr, o_idx)
+        se_ptr, se_idx = sub(e_ptr, e_idx)
+        dec = PageGaugeDecode(workspace())
+        dec.plan(so_ptr, so_idx, se_ptr, se_idx, tables.exact_last_page_len[idx].contiguous(),
+                 32, 8)
+        part = dec.run(q[idx].contiguous(), cache.key_codes, cache.value_codes, cache.key_scales,
+                       cache.value_scales, cache.exact_key, cache.exact_value,
+                       cache.value_center[idx].contiguous())
+        torch.cuda.synchronize()
+        parts.append(cpu(part))
+    assert read_device_error() == 0
+    full = gather_outputs(shards, parts, len(lengths))
+    assert O.max_abs(full.astype(np.float64), cpu(out).astype(np.float64)) <= 2e-3
