@@ -49,7 +49,7 @@ def parse_args():
     p.add_argument("--steps", type=int, default=20000)
     p.add_argument("--warmup", type=int, default=50)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    p.add_argument("--workload", choices=("b1_49k", "b8_ragged", "b1_4k", "decoder"),
+    p.add_argument("--workload", choices=("b1_49k", "b8_ragged", "b1_4k", "decoder", "gemm"),
                    default="b1_49k")
     p.add_argument("--split", type=int, default=-1,
                    help="pages per work item (-1: measured scheduler table, 0: heuristic)")
@@ -876,6 +876,80 @@ def run_decoder(args, dist: Dist, local: int) -> None:
         print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------ projections
+def run_gemm(args) -> None:
+    """The decoder's projection GEMMs alone at its one-row shapes (configs[4]
+    layer: qkv, o + residual, gate|up + SiLU*up, down + residual; the LM
+    head), each streamed from enough weight copies to exceed the L2 and
+    replayed back to back in a CUDA graph (PDL between launches); a
+    secondary measurement of the weight-streaming kernel, not a headline."""
+    from pagegauge_b200.gemm import RESIDUAL, SILU_MUL, STORE, PackedWeight, SkinnyGemm
+
+    batch = 1
+    peak, peak_src = peak_hbm()
+    shapes = {"qkv": (6144, 4096, STORE), "o": (4096, 4096, RESIDUAL),
+              "gate_up": (28672, 4096, SILU_MUL), "down": (4096, 14336, RESIDUAL),
+              "lm_head": (32768, 4096, STORE)}
+    g = torch.Generator(device="cuda").manual_seed(SEED)
+    results, total_bytes, total_us = {}, 0, 0.0
+    for name, (n, k, mode) in shapes.items():
+        copies = max(2, int(400e6 // (n * k * 2)) + 1)
+        ws = [PackedWeight((torch.randn(n, k, generator=g, device="cuda") * 0.02).half(), mode)
+              for _ in range(copies)]
+        x = torch.randn(batch, k, generator=g, device="cuda").half()
+        res = torch.zeros(batch, n, device="cuda").half()
+        out = torch.empty(batch, n // 2 if mode == SILU_MUL else n, device="cuda").half()
+        gemm = SkinnyGemm("cuda")
+        gemm.reserve(n, k, batch, mode)
+        stream = torch.cuda.Stream()
+        torch.cuda.nvtx.range_push(f"gemm_{name}")
+
+        def run(w):
+            if mode == RESIDUAL:
+                gemm(x, w, mode=mode, residual=res)
+            else:
+                gemm(x, w, out=out, mode=mode)
+
+        with torch.cuda.stream(stream):
+            for w in ws:
+                run(w)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                for i in range(4 * copies):
+                    run(ws[i % copies])
+            for _ in range(max(args.warmup, 3) // 3 + 1):
+                graph.replay()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            reps = 5
+            e0.record(stream)
+            for _ in range(reps):
+                graph.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
+        us = e0.elapsed_time(e1) * 1e3 / (reps * 4 * copies)
+        nbytes = n * k * 2
+        results[name] = {"n": n, "k": k, "us": round(us, 3),
+                         "gbs": round(nbytes / (us * 1e-6) / 1e9, 1),
+                         "roofline_frac": round(nbytes / (us * 1e-6) / 1e9 / peak, 4)}
+        total_bytes += nbytes
+        total_us += us
+        del graph, ws
+        torch.cuda.empty_cache()
+    value = total_bytes / (total_us * 1e-6) / 1e9
+    print(json.dumps({
+        "metric": "decoder projection GEMMs, weight GB/s (B=1)", "value": round(value, 1),
+        "unit": "GB/s", "n_gpus": 1, "higher_is_better": True, "dtype": "fp16 in, fp32 accumulate",
+        "data": "synthetic random N(0,0.02) weights",
+        "config": {"workload": "gemm", "batch": batch, "shapes": list(shapes)},
+        "roofline": {"bound": "hbm", "achieved": round(value, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(value / peak, 4), "peak_source": peak_src,
+                     "kernel": "pg_skinny_gemm_kernel"},
+        "workloads": results}), flush=True)
+
+
 # -------------------------------------------------------------------- main
 def main() -> None:
     args = parse_args()
@@ -898,6 +972,13 @@ def main() -> None:
 
     if args.workload == "decoder":
         run_decoder(args, dist, local)
+        if world > 1:
+            dist.barrier()
+            dist.dist.destroy_process_group()
+        return
+    if args.workload == "gemm":
+        if rank == 0:
+            run_gemm(args)
         if world > 1:
             dist.barrier()
             dist.dist.destroy_process_group()
