@@ -103,17 +103,28 @@ __device__ __forceinline__ bool flag_wait_bounded(const int32_t* flag, int32_t w
 }
 
 // ------------------------------------------------------- bulk tensor copies
+// L2 policy for operands that one launch streams exactly once (cache pages,
+// projection weights): their lines are the first to be evicted, so the small
+// data every launch re-reads (page tables, scales, queries, activations,
+// counters) stays resident in the L2 from one launch to the next.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t policy;
+  asm("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+  return policy;
+}
+
 // 3-D tiled TMA load into this CTA's shared memory, completion signalled on
-// an mbarrier by transaction bytes.  No multicast: every CTA fetches its own
-// tiles from this GPU's memory.
-__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map,
-                                            int c0, int c1, int c2,
-                                            uint64_t* bar) {
+// an mbarrier by transaction bytes, with an L2 cache policy
+// (l2_evict_first_policy for streams).  No multicast: every CTA fetches its
+// own tiles from this GPU's memory.
+__device__ __forceinline__ void tma_load_3d_hint(void* dst, const CUtensorMap* map,
+                                                 int c0, int c1, int c2,
+                                                 uint64_t* bar, uint64_t policy) {
   asm volatile(
       "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_"
-      "tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_addr(dst)),
+      "tx::bytes.L2::cache_hint [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_addr(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2),
-      "r"(smem_addr(bar))
+      "r"(smem_addr(bar)), "l"(policy)
       : "memory");
 }
 
@@ -237,6 +248,16 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
           "r"(smem_addr(dst)),
       "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// bulk_load with an L2 cache policy.
+__device__ __forceinline__ void bulk_load_hint(void* dst, const void* src, uint32_t bytes,
+                                               uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1], %2, [%3], %4;" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
       : "memory");
 }
 

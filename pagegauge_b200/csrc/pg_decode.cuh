@@ -556,11 +556,12 @@ __device__ __forceinline__ void issue_page_fp16(const CUtensorMap* tk, const CUt
                                                 int h) {
   uint8_t* dst = ring + stage * 8192;
   uint64_t* bar = bars + stage;
+  const uint64_t pol = l2_evict_first_policy();
   mbar_arrive_expect_tx(bar, 8192);
-  tma_load_3d(dst, tk, 0, 2 * h, id * kPage, bar);
-  tma_load_3d(dst + 2048, tk, 0, 2 * h + 1, id * kPage, bar);
-  tma_load_3d(dst + 4096, tv, 0, 2 * h, id * kPage, bar);
-  tma_load_3d(dst + 6144, tv, 0, 2 * h + 1, id * kPage, bar);
+  tma_load_3d_hint(dst, tk, 0, 2 * h, id * kPage, bar, pol);
+  tma_load_3d_hint(dst + 2048, tk, 0, 2 * h + 1, id * kPage, bar, pol);
+  tma_load_3d_hint(dst + 4096, tv, 0, 2 * h, id * kPage, bar, pol);
+  tma_load_3d_hint(dst + 6144, tv, 0, 2 * h + 1, id * kPage, bar, pol);
 }
 
 // INT8 pages of one warp, two at a time.  The 4-stage ring is used as two
@@ -573,12 +574,13 @@ __device__ __forceinline__ void issue_page_fp16(const CUtensorMap* tk, const CUt
 __device__ __forceinline__ void issue_pair_int8(const CUtensorMap* tk, const CUtensorMap* tv,
                                                 uint8_t* dst, uint64_t* bar, int n, int id0,
                                                 int id1, int h) {
+  const uint64_t pol = l2_evict_first_policy();
   mbar_arrive_expect_tx(bar, n * 4096);
-  tma_load_3d(dst, tk, 0, h, id0 * kPage, bar);
-  tma_load_3d(dst + 2048, tv, 0, h, id0 * kPage, bar);
+  tma_load_3d_hint(dst, tk, 0, h, id0 * kPage, bar, pol);
+  tma_load_3d_hint(dst + 2048, tv, 0, h, id0 * kPage, bar, pol);
   if (n == 2) {
-    tma_load_3d(dst + 4096, tk, 0, h, id1 * kPage, bar);
-    tma_load_3d(dst + 6144, tv, 0, h, id1 * kPage, bar);
+    tma_load_3d_hint(dst + 4096, tk, 0, h, id1 * kPage, bar, pol);
+    tma_load_3d_hint(dst + 6144, tv, 0, h, id1 * kPage, bar, pol);
   }
 }
 
@@ -942,11 +944,12 @@ __device__ __forceinline__ void issue_pair_affine(const DecodeParams& p, const C
                                                   const CUtensorMap* tv, uint8_t* dst,
                                                   uint8_t* meta, uint64_t* bar, int n, int id0,
                                                   int id1, int h) {
+  const uint64_t pol = l2_evict_first_policy();
   mbar_arrive_expect_tx(bar, n * (4096 + kAffineMetaBytes));
   for (int j = 0; j < n; ++j) {
     const int id = j == 0 ? id0 : id1;
-    tma_load_3d(dst + 4096 * j, tk, 0, h, id * kPage, bar);
-    tma_load_3d(dst + 4096 * j + 2048, tv, 0, h, id * kPage, bar);
+    tma_load_3d_hint(dst + 4096 * j, tk, 0, h, id * kPage, bar, pol);
+    tma_load_3d_hint(dst + 4096 * j + 2048, tv, 0, h, id * kPage, bar, pol);
     const int64_t mo = (static_cast<int64_t>(id) * p.hkv + h) * 8;
     uint8_t* m = meta + kAffineMetaBytes * j;
     bulk_load(m, p.seg[0].k_scale + mo, 16, bar);

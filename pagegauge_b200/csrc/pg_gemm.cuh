@@ -141,7 +141,7 @@ __device__ __forceinline__ void gemm_issue_w(const __half* wp, const GemmParams&
                                              uint8_t* stage, uint64_t* bar, int tile, int kb) {
   mbar_arrive_expect_tx(bar, gemm_stage_bytes(NT));
   const __half* src = wp + (static_cast<int64_t>(tile) * p.kblocks + kb) * (kGemmTileRows * kGemmBK);
-  bulk_load(stage, src, kGemmTileRows * 128, bar);
+  bulk_load_hint(stage, src, kGemmTileRows * 128, bar, l2_evict_first_policy());
 }
 
 template <int NT>
