@@ -831,7 +831,7 @@ def measure_decoder(dist: Dist, batch: int, context: int = 16384, steps: int = 1
         "roofline_frac": round(achieved / peak, 4), "prefill_s": round(prefill_s, 2),
         "replans_in_timing": 0, "params": cfg.parameter_count(), "gemm": dec.gemm_impl,
         "exact_policy": policy,
-        "tp_reduce": (None if world == 1 or dec.gemm_impl != "pg" else tp_reduce),
+        "tp_reduce": (None if world == 1 else ("peer" if dec.tpx is not None else "nccl")),
         "device_guard": read_device_error(),
     }
     dec.close()

@@ -84,6 +84,16 @@ int32_t pg_tp_exchange_open(const void* ipc_handle, void** buffer_out);
 int32_t pg_tp_exchange_close(void* peer_buffer);
 int32_t pg_tp_exchange_destroy(void* buffer);
 
+/* Publish this rank's partial product computed by another GEMM (FP16
+ * src [batch, tiles * 64], e.g. cuBLAS's row-parallel o_proj / down_proj
+ * output) to every rank's exchange buffer (peers[r] = rank r's buffer as
+ * mapped here) in the format a tensor-parallel pg_skinny_gemm publishes,
+ * so that pg_tp_reduce replaces the all-reduce (and the residual add +
+ * RMSNorm after it).  Every rank must launch the same sequence.           */
+int32_t pg_tp_publish(void* const* peers, int32_t world, int32_t rank, int32_t tiles_cap,
+                      int32_t tiles, int32_t batch, const void* src, int64_t src_stride,
+                      void* stream);
+
 /* Consume a tensor-parallel GEMM's published tiles on this rank: wait
  * (about a second at most, then PG_DEV_WAIT_TIMEOUT) until all `world`
  * ranks' tiles of the `tiles` output tiles have arrived in this rank's

@@ -226,7 +226,7 @@ extern "C" {
 
 const char* pg_last_error(void) { return g_last_error.c_str(); }
 
-int32_t pg_abi_version(void) { return 105; }
+int32_t pg_abi_version(void) { return 106; }
 
 int64_t pg_tp_exchange_bytes(int32_t tiles_cap) {
   return tiles_cap > 0 ? pg::tp_exchange_bytes(tiles_cap) : -1;
@@ -1286,6 +1286,33 @@ int32_t pg_skinny_gemm(const pg_gemm_args* a, void* stream) {
     e = norm ? cudaLaunchKernelEx(&cfg, pg::pg_skinny_gemm_kernel<4, true>, wp, tx, p)
              : cudaLaunchKernelEx(&cfg, pg::pg_skinny_gemm_kernel<4, false>, wp, tx, p);
   return cuda_check(e, "skinny gemm launch");
+}
+
+int32_t pg_tp_publish(void* const* peers, int32_t world, int32_t rank, int32_t tiles_cap,
+                      int32_t tiles, int32_t batch, const void* src, int64_t src_stride,
+                      void* stream) {
+  PG_REQUIRE(peers != nullptr, "the ranks' exchange buffers are required");
+  PG_REQUIRE(world >= 2 && world <= pg::kGemmMaxTp && rank >= 0 && rank < world,
+             "world must be 2..8 with 0 <= rank < world");
+  PG_REQUIRE(tiles >= 1 && tiles <= tiles_cap, "tiles must be 1..tiles_cap");
+  PG_REQUIRE(batch >= 1 && batch <= pg::kGemmMaxXR, "batch must be 1..32");
+  PG_REQUIRE(src != nullptr && aligned(src, 4) && src_stride >= int64_t(tiles) * 64 &&
+                 src_stride % 2 == 0,
+             "src must be fp16 [batch, tiles * 64] with 4-byte aligned rows");
+  pg::TpPublishParams p{};
+  for (int r = 0; r < world; ++r) {
+    PG_REQUIRE(peers[r] != nullptr && aligned(peers[r], 256),
+               "every rank's exchange buffer is required");
+    p.peers[r] = static_cast<uint8_t*>(peers[r]);
+  }
+  p.world = world;
+  p.rank = rank;
+  p.cap = tiles_cap;
+  p.batch = batch;
+  p.src = static_cast<const __half*>(src);
+  p.src_stride = src_stride;
+  return launch_pdl(pg::pg_tp_publish_kernel, dim3(tiles), dim3(pg::kTpPublishThreads), 0,
+                    static_cast<cudaStream_t>(stream), "tp publish launch", p);
 }
 
 int32_t pg_tp_reduce(const void* exchange, int32_t world, int32_t tiles_cap, int32_t tiles,

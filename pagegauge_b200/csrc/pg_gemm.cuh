@@ -515,6 +515,50 @@ __global__ void __launch_bounds__(kGemmWarps * 32)
   gemm_flush<NT>(p, acc, cur, seg_kb0, ckb, seg, s_tile, &s_last, s_seg);
 }
 
+// Publication of a partial product computed elsewhere (a library GEMM's
+// FP16 output [batch, tiles * 64]) in the exchange format of
+// gemm_tp_push: one CTA per output tile stores the tile's values, each
+// paired with the tile's exchange count, into every rank's exchange buffer
+// (this rank's own included), then advances the count.  pg_tp_reduce then
+// sums the ranks' tiles exactly as after a publishing skinny GEMM.
+struct TpPublishParams {
+  uint8_t* peers[kGemmMaxTp];
+  int32_t world, rank, cap, batch;
+  const __half* src;
+  int64_t src_stride;
+};
+
+constexpr int kTpPublishThreads = 256;
+
+__global__ void __launch_bounds__(kTpPublishThreads)
+    pg_tp_publish_kernel(const __grid_constant__ TpPublishParams p) {
+  __shared__ int32_t s_seq;
+  const int tile = blockIdx.x;
+  const int cap = p.cap;
+  int32_t* my_seq = reinterpret_cast<int32_t*>(p.peers[p.rank] + tp_seq_offset(cap));
+  pdl_launch_dependents();
+  pdl_wait_primary();  // the GEMM that wrote src; this rank's previous reduce
+  if (threadIdx.x == 0) s_seq = my_seq[tile] + 1;
+  __syncthreads();
+  const int32_t seq = s_seq;
+  const int64_t slot = (static_cast<int64_t>(seq & 1) * kGemmMaxTp + p.rank) * cap + tile;
+  // Two values per 16-byte store: 32 pairs of columns per row.
+  const int n2 = kGemmTileRows / 2 * p.batch;
+  for (int i = threadIdx.x; i < n2; i += blockDim.x) {
+    const int b = i / (kGemmTileRows / 2), j = 2 * (i - b * (kGemmTileRows / 2));
+    const __half2 v = *reinterpret_cast<const __half2*>(p.src + b * p.src_stride +
+                                                        tile * kGemmTileRows + j);
+    const float2 f = __half22float2(v);
+    for (int dst = 0; dst < p.world; ++dst) {
+      uint2* out = reinterpret_cast<uint2*>(p.peers[dst] + tp_recv_offset(cap)) +
+                   slot * tp_slot_pairs();
+      st_pairs2_relaxed_sys(out + b * kGemmTileRows + j, f.x, f.y, seq);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) my_seq[tile] = seq;
+}
+
 // Consumer of a tensor-parallel GEMM's published tiles: one CTA of 512
 // threads per batch row b.  It waits (bounded) until every rank's tile of
 // every output tile has arrived, sums them in rank order in FP32 and then

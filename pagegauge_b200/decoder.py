@@ -252,9 +252,11 @@ class PageGaugeDecoder:
     """Greedy decoding with PageGauge attention on this rank's shard.
 
     ``process_group``: the tensor-parallel group (NCCL) or None for one GPU.
-    ``tp_reduce`` (tensor parallelism with the streaming GEMMs): "peer" sums
-    the row-parallel projections' tiles through NVLink peer memory (the GEMM
-    publishes, the next kernel reduces), "nccl" uses NCCL all-reduces.
+    ``tp_reduce`` (tensor parallelism, up to 32 rows): "peer" sums the
+    row-parallel projections' partials through NVLink peer memory (the
+    streaming GEMM publishes its tiles, or a small kernel publishes cuBLAS's
+    output; the next kernel reduces and adds the residual + RMSNorm),
+    "nccl" uses NCCL all-reduces.
     ``fuse_norm`` (one GPU, streaming GEMMs): compute the RMSNorms inside the
     qkv, gate/up and LM-head GEMMs instead of separate launches; measured
     slower on B200 (4.1-4.4 ms against 3.6-3.9 ms per B=1 step), so off by
@@ -329,6 +331,14 @@ class PageGaugeDecoder:
             gemm = "pg" if batch <= 8 else "cublas"
         self.gemm_impl = gemm
         self.sk = SkinnyGemm(dev)
+        # Row-parallel o_proj / down_proj under tensor parallelism: "peer"
+        # sums the ranks' partials through NVLink peer memory (the streaming
+        # GEMM publishes its tiles; cuBLAS's output is published by a small
+        # kernel) and adds the residual + RMSNorm in the same launch.
+        if tp_reduce not in ("peer", "nccl"):
+            raise ValueError("tp_reduce must be 'peer' or 'nccl'")
+        if process_group is not None and tp_reduce == "peer" and batch <= 32:
+            self.tpx = TpExchange(process_group, cfg.hidden // 64, dev)
         self.packed = []
         if gemm == "pg":
             # Weights in the streaming kernels' tiled layout (the row-major
@@ -341,11 +351,7 @@ class PageGaugeDecoder:
             # o_proj / down_proj add into the residual in their epilogue; under
             # tensor parallelism they first sum the ranks' tiles through peer
             # memory (no NCCL all-reduce).
-            if tp_reduce not in ("peer", "nccl"):
-                raise ValueError("tp_reduce must be 'peer' or 'nccl'")
             tp = process_group is not None
-            if tp and tp_reduce == "peer":
-                self.tpx = TpExchange(process_group, cfg.hidden // 64, dev)
             self.sk.reserve(qkv_w, cfg.hidden, B, STORE)
             self.sk.reserve(cfg.hidden, self.hq * HEAD_DIM, B, STORE if tp else RESIDUAL)
             self.sk.reserve(2 * self.inter, cfg.hidden, B, SILU_MUL)
@@ -581,14 +587,24 @@ class PageGaugeDecoder:
                 delta = None
                 continue
             self._linear(self.attn.view(B, -1), lw.o, self.o, pk.get("o"))
-            self._all_reduce(self.o)
-            self._norm(self.residual, self.o, lw.mlp_norm, self.normed)
+            if tpx is not None:
+                # cuBLAS partials through peer memory: publish, then sum +
+                # residual + RMSNorm in one launch.
+                tpx.publish(self.o)
+                tpx.reduce(B, self.residual, lw.mlp_norm, eps, self.normed)
+            else:
+                self._all_reduce(self.o)
+                self._norm(self.residual, self.o, lw.mlp_norm, self.normed)
             if self.gemm_impl == "pg":
                 self.sk(self.normed, pk["gate_up"], out=self.act, mode=SILU_MUL)
             else:
                 torch.matmul(self.normed, lw.gate_up.t(), out=self.gate_up)
                 self._silu_mul(self.gate_up, self.act)
             self._linear(self.act, lw.down, self.down, pk.get("down"))
+            if tpx is not None:
+                tpx.publish(self.down)
+                pending = True
+                continue
             self._all_reduce(self.down)
             delta = self.down
         if fuse_norm:
@@ -629,6 +645,11 @@ class PageGaugeDecoder:
             # reduction), norm, gate_up (+SiLU), down (+residual, same) per
             # layer; the final norm, LM head, argmax and position update.
             return self.cfg.layers * (7 + attn) + 4
+        if self.tpx is not None:
+            # cuBLAS projections with the peer-memory reduction: norm (or
+            # reduce), append, attention, publish o, reduce (+residual,
+            # RMSNorm), SiLU*up, publish down per layer.
+            return self.cfg.layers * (6 + attn) + 3
         return self.cfg.layers * (4 + attn) + 3
 
     def _capture(self, entry: dict) -> None:

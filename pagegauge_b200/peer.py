@@ -5,12 +5,13 @@ parallelism, scripts/benchmark_page_gauge_transformer.py:2754-2804) end in
 an all-reduce of a [B, hidden] partial product.  Here no collective library
 is involved: the projection GEMM publishes every finished FP32 output tile
 into every rank's exchange buffer as soon as the tile is done (plain peer
-stores over NVLink plus a per-tile arrival flag, so the transfer overlaps
-the rest of the GEMM), and the next kernel on each rank waits (bounded) for
-all ranks' tiles, sums them in rank order and applies the residual add and
-RMSNorm (``reduce``).  This module allocates one exchange buffer per rank
-(CUDA IPC), shares the handles over the process group and maps the other
-ranks' buffers.
+stores over NVLink, every value tagged with the exchange count, so the
+transfer overlaps the rest of the GEMM), or ``publish`` does the same for a
+partial another GEMM (cuBLAS) wrote; the next kernel on each rank waits
+(bounded) for all ranks' tiles, sums them in rank order and applies the
+residual add and RMSNorm (``reduce``).  This module allocates one
+exchange buffer per rank (CUDA IPC), shares the handles over the process
+group and maps the other ranks' buffers.
 """
 
 from __future__ import annotations
@@ -71,6 +72,20 @@ class TpExchange:
         args.tp_world, args.tp_rank, args.tp_tiles_cap = self.world, self.rank, self.tiles_cap
         for r, ptr in enumerate(self.peers):
             args.tp_peers[r] = ptr
+
+    def publish(self, src: torch.Tensor) -> None:
+        """Publish this rank's partial product computed by another GEMM
+        (float16 [batch, tiles * 64], e.g. cuBLAS's row-parallel output) to
+        every rank, as a tensor-parallel streaming GEMM publishes its tiles;
+        the next ``reduce`` sums the ranks' partials."""
+        if src.dtype != torch.float16 or src.dim() != 2 or src.stride(1) != 1:
+            raise ValueError("src must be a float16 [batch, n] tensor with contiguous rows")
+        if src.shape[1] % 64 or src.shape[1] // 64 > self.tiles_cap:
+            raise ValueError(f"src columns must be a multiple of 64, at most {self.tiles_cap * 64}")
+        peers = (ctypes.c_void_p * self.world)(*self.peers)
+        _lib.check(_lib.load().pg_tp_publish(
+            peers, self.world, self.rank, self.tiles_cap, src.shape[1] // 64, src.shape[0],
+            src.data_ptr(), src.stride(0), torch.cuda.current_stream(src.device).cuda_stream))
 
     def reduce(self, batch: int, residual: torch.Tensor | None, norm_weight: torch.Tensor | None,
                eps: float, out: torch.Tensor, tiles: int | None = None) -> torch.Tensor:

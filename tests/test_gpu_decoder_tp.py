@@ -1,9 +1,10 @@
 """Tensor-parallel PageGauge decoder on two GPUs: each rank holds half of
 the KV heads, FFN columns and vocabulary; the gathered logits of the
 prefill and of graph-captured decode steps must match the single-model
-CPU oracle.  The streaming-GEMM decoder reduces o_proj / down_proj through
-peer memory inside the GEMM; the cuBLAS decoder uses NCCL all-reduces.
-Skipped unless two GPUs are visible."""
+CPU oracle.  o_proj / down_proj are reduced through peer memory (the
+streaming GEMM publishes its tiles; cuBLAS's output goes through the
+publish kernel) or with NCCL all-reduces.  Skipped unless two GPUs are
+visible."""
 
 from __future__ import annotations
 
@@ -27,7 +28,7 @@ def _cfg():
     return DecoderConfig(layers=2, hidden=512, heads=8, kv_heads=2, intermediate=1024, vocab=512)
 
 
-def _rank(rank, port, prompt, result, gemm):
+def _rank(rank, port, prompt, result, gemm, reduce):
     import torch.distributed as dist
 
     from pagegauge_b200.decoder import PageGaugeDecoder, TensorParallel, random_decoder_weights
@@ -42,8 +43,8 @@ def _rank(rank, port, prompt, result, gemm):
         w = random_decoder_weights(cfg, 41, device="cuda", gen_device="cpu",
                                    tp=TensorParallel.of(cfg, rank, WORLD))
         dec = PageGaugeDecoder(w, batch=prompt.shape[0], max_context=512,
-                               process_group=dist.group.WORLD, gemm=gemm)
-        assert (dec.tpx is not None) == (gemm == "pg")
+                               process_group=dist.group.WORLD, gemm=gemm, tp_reduce=reduce)
+        assert (dec.tpx is not None) == (reduce == "peer")
         logits = [dec.prefill(prompt.cuda()).float()]
         tokens = [dec.tokens.clone()]
         # This rank's caches after the prefill (its KV heads), for the oracle.
@@ -80,8 +81,8 @@ def _rank(rank, port, prompt, result, gemm):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs two GPUs")
-@pytest.mark.parametrize("gemm", ["pg", "cublas"])
-def test_two_gpu_tensor_parallel_decoder_matches_oracle(cuda_lib, tmp_path, gemm):
+@pytest.mark.parametrize("gemm,reduce", [("pg", "peer"), ("cublas", "peer"), ("cublas", "nccl")])
+def test_two_gpu_tensor_parallel_decoder_matches_oracle(cuda_lib, tmp_path, gemm, reduce):
     from oracle import decoder_oracle as D
     from oracle import pagegauge_oracle as O
 
@@ -93,7 +94,7 @@ def test_two_gpu_tensor_parallel_decoder_matches_oracle(cuda_lib, tmp_path, gemm
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
     path = str(tmp_path / "tp.npz")
-    mp.spawn(_rank, args=(port, prompt, path, gemm), nprocs=WORLD, join=True)
+    mp.spawn(_rank, args=(port, prompt, path, gemm, reduce), nprocs=WORLD, join=True)
     got = np.load(path)
     logits, tokens = got["logits"], got["tokens"]
     w, ocfg = oracle_weights(cfg, seed=41), oracle_cfg(cfg)
