@@ -160,6 +160,15 @@ def sweep(batch: int, context: int, repeats: int = 30, seeds=(20261001, 20261002
     return p50
 
 
+def refinements(best: int, measured) -> list[int]:
+    """Split sizes within +-20 % of the coarse winner not yet measured (the
+    coarse candidates are num_splits steps, up to 15 % apart)."""
+    if best <= 0:
+        return []
+    out = {max(1, round(best * f)) for f in (0.8, 0.85, 0.9, 0.95, 1.05, 1.1, 1.15, 1.2)}
+    return sorted(out - set(measured))
+
+
 def _sweep_steady(batch, context, repeats, seeds, write, path, lengths, layers):
     import torch
 
@@ -170,8 +179,8 @@ def _sweep_steady(batch, context, repeats, seeds, write, path, lengths, layers):
     batch, context = len(lengths), max(lengths)
     ws = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     stream = torch.cuda.Stream()
-    results: dict[int, list[float]] = {}
     chunk = 8 * layers
+    setups = []  # per seed: (q, layer caches, page tables)
     for seed in seeds:
         caches = []
         for layer in range(layers):
@@ -179,9 +188,13 @@ def _sweep_steady(batch, context, repeats, seeds, write, path, lengths, layers):
             cache, tables = build_gauge_cache(dk, dv, lengths)
             del dk, dv
             caches.append(cache)
-        out = torch.empty_like(q)
-        old_pages = max(t // PAGE for t in tables.old_tokens)
-        for split in candidates(old_pages):
+        setups.append((q, caches, tables))
+    out = torch.empty_like(setups[0][0])
+    old_pages = max(t // PAGE for t in setups[0][2].old_tokens)
+
+    def measure(split: int) -> float:
+        per_seed = []
+        for q, caches, tables in setups:
             dec = PageGaugeDecode(ws)
             dec.plan(tables.old_indptr, tables.old_indices, tables.exact_indptr,
                      tables.exact_indices, tables.exact_last_page_len, 32, 8,
@@ -210,15 +223,20 @@ def _sweep_steady(batch, context, repeats, seeds, write, path, lengths, layers):
                     times.append(s.elapsed_time(e) * 1e3 / chunk)
             torch.cuda.synchronize()
             del graph
-            results.setdefault(split, []).append(statistics.median(times))
-        del caches
-    p50 = {k: statistics.fmean(v) for k, v in results.items()}
+            per_seed.append(statistics.median(times))
+        return statistics.fmean(per_seed)
+
+    p50 = {split: measure(split) for split in candidates(old_pages)}
+    for split in refinements(min(p50, key=p50.get), p50):
+        p50[split] = measure(split)
+    del setups
     if write:
         record(batch, context, p50, path=path,
                meta={"gpu": torch.cuda.get_device_name(), "repeats": repeats,
                      "seeds": list(seeds), "lengths": lengths, "layers": layers,
                      "mode": (f"steady: CUDA graph of {chunk} back-to-back decode steps "
-                              f"(split + merge) cycling {layers} caches")})
+                              f"(split + merge) cycling {layers} caches; coarse num_splits "
+                              f"candidates, then +-20 % around the winner")})
     return p50
 
 

@@ -42,3 +42,12 @@ def test_candidates_span_one_to_64_splits():
     c = S.candidates(3056)
     assert c[0] == 0 and 3056 in c and 48 in c and 64 in c
     assert all(-(-3056 // s) <= 64 for s in c if s)
+
+
+def test_refinements_surround_the_coarse_winner():
+    from pagegauge_b200.scheduler import refinements
+
+    assert refinements(0, [0, 64]) == []
+    r = refinements(64, [0, 48, 55, 64, 77])
+    assert r == [51, 54, 58, 61, 67, 70, 74]
+    assert 77 not in r and 64 not in r
