@@ -4,10 +4,10 @@
 A step is one PageGauge decode attention over one layer's cache: INT8
 page-affine old pages + the 256-token exact FP16 tail + LSE merge + value-
 centre restore, 32 Q / 8 KV heads, head_dim 128, page 16.  The headline
-workload is BASELINE configs[1] (B=1, context 49,152); several layers'
+workload is B1/49K (B=1, context 49,152); several layers'
 caches (more bytes than the 126 MB L2) are cycled so every step streams its
 cache from HBM.  The same line carries, under ``workloads``, the B8 ragged
-decode and the fused append step measured in the
+decode and the fused append step (B=8, 32 layers) measured in the
 same run (``--only`` skips them).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
@@ -228,8 +228,8 @@ def cpu_baseline(lengths, seconds_budget: float = 15.0) -> dict:
 
 def decoder_cpu_baseline(context: int = 16384, seed: int = 20261004) -> dict:
     """The decoder oracle on the host cores, bounded sample: one decode step
-    (B=1, position ``context``) of a one-layer model of the configs[4]
-    shape on a PageGauge cache of ``context`` tokens, plus the LM head alone;
+    (B=1, position ``context``) of a one-layer model of the benchmark
+    decoder's shape on a PageGauge cache of ``context`` tokens, plus the LM head alone;
     a 32-layer step is 32 layers + one head."""
     from oracle import decoder_oracle as D
     from oracle import pagegauge_oracle as O
@@ -276,7 +276,7 @@ def decoder_cpu_baseline(context: int = 16384, seed: int = 20261004) -> dict:
     t_head = time.perf_counter() - t0
     t_step = cfg.layers * max(t_one - t_head, 0.0) + t_head
     return {"value": 1.0 / t_step, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
-            "sample": f"one decode step of a 1-layer configs[4]-shaped model at ctx {context} "
+            "sample": f"one decode step of a 1-layer Mistral-7B-shaped model at ctx {context} "
                       f"(numpy oracle, {torch.get_num_threads()} threads): {t_one:.2f} s, LM head "
                       f"{t_head:.2f} s; 32-layer step = 32 layers + head = {t_step:.1f} s"}
 
@@ -630,7 +630,7 @@ class _Null:
 
 # ------------------------------------------------------------ append bench
 def measure_append(dist: Dist, batch: int = 8, layers: int = 32, samples: int = 100) -> dict:
-    """one decode step's fused RoPE + centred append +
+    """The fused-append benchmark: one decode step's fused RoPE + centred append +
     page finalisation for B=8 requests in each of 32 layers (one launch per
     layer), half of the requests at the last token of a page (position %
     16 == 15, so their page is finalised to INT8 in the same launch), the
@@ -770,7 +770,7 @@ def parse_policy(text: str) -> tuple[int, int, int]:
 def measure_decoder(dist: Dist, batch: int, context: int = 16384, steps: int = 16,
                     seed: int = 20261004, gemm: str = "auto", policy: str = "S0/A0/T256",
                     tp_reduce: str = "peer") -> dict:
-    """Mistral-7B-shaped random-init FP16 decoder,
+    """The benchmark decoder: Mistral-7B-shaped random-init FP16 decoder,
     prompt of ``context`` random tokens prefilled into PageGauge caches, one
     eager warm-up decode step, then ``steps`` greedy decode steps (CUDA
     graphs prepared beforehand), tensor-parallel over the ranks."""
@@ -878,7 +878,7 @@ def run_decoder(args, dist: Dist, local: int) -> None:
 
 # ------------------------------------------------------------ projections
 def run_gemm(args) -> None:
-    """The decoder's projection GEMMs alone at its one-row shapes (configs[4]
+    """The decoder's projection GEMMs alone at its one-row shapes (Mistral-7B
     layer: qkv, o + residual, gate|up + SiLU*up, down + residual; the LM
     head), each streamed from enough weight copies to exceed the L2 and
     replayed back to back in a CUDA graph (PDL between launches); a

@@ -165,7 +165,7 @@ def build_gauge_cache(dense_k: torch.Tensor, dense_v: torch.Tensor, lengths: lis
 def synthetic_dense_cache(lengths: list[int], hkv: int = 8, seed: int = 20261001,
                           device: torch.device | str = "cpu", theta: float = 1.0e6,
                           key_mean_var: float = 2.0, group: int = 4):
-    """BASELINE synthetic decode inputs: K = RoPE(N(mu_c, 1)) with
+    """The benchmark's synthetic decode inputs: K = RoPE(N(mu_c, 1)) with
     mu_c ~ N(0, key_mean_var) per (head, channel), V ~ N(0, 1), Q ~ N(0, 1),
     request-major pages (the tail of a partial last page is zero-padded).
     Returns (q [B,group*hkv,128], dense_k, dense_v) as FP16 on ``device``."""

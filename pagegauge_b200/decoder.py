@@ -1,5 +1,5 @@
 """Mistral-shaped decoder whose attention is the PageGauge decode path
-random-init FP16 weights, a prompt prefill that
+(the Mistral-7B-shaped benchmark decoder): random-init FP16 weights, a prompt prefill that
 builds the page-gauge caches, then greedy decode steps captured in CUDA
 graphs, optionally tensor-parallel over the GPUs of one box.
 
@@ -23,7 +23,7 @@ Tensor parallelism shards by KV head (Megatron column-parallel qkv and
 gate/up, row-parallel o and down, vocabulary-parallel LM head): rank t of T
 holds KV heads [t*Hkv/T, (t+1)*Hkv/T) and their query heads, so every rank
 runs the same PageGauge kernels on its own heads and caches.  The reference
-is single-GPU; the sharding follows BASELINE configs[4].
+is single-GPU; the sharding is this build's (tokens/s at 1/2/4/8 GPUs).
 
 The caches follow build_caches (:1156-1259): per (layer, request, KV head)
 centres are the FP32 mean of the prompt, every prompt page is quantised
@@ -67,7 +67,7 @@ class DecoderConfig:
 
     @classmethod
     def mistral_7b_shaped(cls) -> "DecoderConfig":
-        """32 layers, hidden 4096, 32/8 heads, FFN
+        """The benchmark decoder: 32 layers, hidden 4096, 32/8 heads, FFN
         14336, vocab 32768, RoPE theta 1e6."""
         return cls()
 

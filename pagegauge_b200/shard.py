@@ -21,7 +21,7 @@ HEAD_DIM = 128
 
 
 def ragged_lengths(batch: int, seed: int, low: int = 4096, high: int = 32768) -> list[int]:
-    """Context lengths drawn uniform in [low, high]."""
+    """Context lengths drawn uniform in [low, high] (the B8 ragged benchmark workload)."""
     rng = np.random.default_rng(seed)
     return [int(x) for x in rng.integers(low, high + 1, size=batch)]
 

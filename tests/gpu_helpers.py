@@ -10,7 +10,7 @@ import torch
 from oracle import pagegauge_oracle as O
 from pagegauge_b200.cache import build_gauge_cache, synthetic_dense_cache
 
-ATOL = 2e-3        # max-abs 2e-3 in FP16 ...
+ATOL = 2e-3        # parity bar: max-abs 2e-3 in FP16 ...
 MIN_COSINE = 0.9999  # ... and cosine >= 0.9999
 
 

@@ -15,9 +15,9 @@ import bench  # noqa: E402
 
 
 def test_algorithmic_bytes_known_answers():
-    # configs[1] B1/49K: 3,056 old pages + 256 exact tokens.
+    # B1/49K: 3,056 old pages + 256 exact tokens.
     assert bench.algorithmic_bytes([3056 * 16], [256]) == 101_285_376
-    # configs[0] B1/4K: 240 old pages + 256 exact tokens.
+    # B1/4K: 240 old pages + 256 exact tokens.
     assert bench.algorithmic_bytes([240 * 16], [256]) == 8_920_576
     # Per request the terms add: codes (K+V), scales (K+V), FP16 exact K+V.
     one = bench.algorithmic_bytes([16], [1])

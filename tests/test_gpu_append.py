@@ -114,7 +114,7 @@ def test_append_page_gauge_bit_exact_vs_oracle(cuda_lib, batch, logical_pages, p
 def test_batched_positions_bit_exact_vs_oracle(cuda_lib, shared_center):
     """Per-request positions (ragged serving batch): requests start at
     staggered in-page phases, so every step closes pages for some requests
-    only (configs[3]'s mixed close pattern)."""
+    only (the append benchmark's mixed close pattern)."""
     batch = 1 if shared_center else 8
     exact_ppr, code_ppr, steps = 3, 8, 40
     g = torch.Generator().manual_seed(20261011 + batch)

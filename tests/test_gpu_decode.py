@@ -1,6 +1,6 @@
 """GPU parity of the split-KV page-affine decode path against the CPU oracle.
 
-Tolerance: FP16 outputs within max-abs 2e-3 and
+Tolerance (the parity bar): FP16 outputs within max-abs 2e-3 and
 cosine >= 0.9999 of the float64 oracle; LSE within 2e-4 (the reference's
 tail-merge test, tests/test_page_gauge_append_extension.py:671-676)."""
 
@@ -46,7 +46,7 @@ def run_fused(q, cache, tables, split_old=0, split_exact=0, warps=4, with_center
 
 @pytest.mark.parametrize("split", [0, 1, 7, 64, 1 << 20])
 def test_b1_4k_configs0_all_splits(cuda_lib, split):
-    """B=1, 4096 tokens = 240 INT8 pages + 16 FP16 tail pages."""
+    """B1/4K: B=1, 4096 tokens = 240 INT8 pages + 16 FP16 tail pages."""
     lengths = [4096]
     q, dk, dv, cache, tables = make_case(lengths)
     if split == 0:
@@ -388,7 +388,7 @@ def test_zero_copy_host_inputs_and_output(cuda_lib):
 
 
 def test_b1_49k_full_size(cuda_lib):
-    """configs[1] at its full size (3,056 INT8 pages + the 16-page tail,
+    """B1/49K at its full size (3,056 INT8 pages + the 16-page tail,
     the benchmark's measured split): two KV heads' query rows against the
     float64 oracle, and a size-independent property -- storing the INT8
     pages in a different physical order (page table permuted to match)
@@ -429,7 +429,7 @@ def test_b1_49k_full_size(cuda_lib):
 
 
 def test_b8_ragged_full_size_and_shards(cuda_lib):
-    """configs[2] at its full size: every request's first KV head against
+    """B8 ragged at its full size: every request's first KV head against
     the float64 oracle, and the per-rank shards of a 2-GPU run (decoded here
     one after the other on one GPU, each its own batch over the same pages)
     reproduce the whole batch's outputs within the tolerance after the host

@@ -1,4 +1,4 @@
-"""GPU parity of the PageGauge decoder (configs[4] path at a small size)
+"""GPU parity of the PageGauge decoder (the benchmark decoder path at a small size)
 against the CPU decoder oracle: the prefill's last-position logits, the
 caches it builds, and the logits of greedy decode steps (CUDA graphs)
 across page boundaries, step by step from the same cache."""

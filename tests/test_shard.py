@@ -36,7 +36,7 @@ def _bench_bytes(lengths, tail_pages=16):
 def test_ragged_lengths_prefix_is_the_b8_config():
     b8 = ragged_lengths(8, 20261001)
     assert all(4096 <= n <= 32768 for n in b8)
-    assert ragged_lengths(32, 20261001)[:8] == b8  # weak scaling keeps configs[2]
+    assert ragged_lengths(32, 20261001)[:8] == b8  # weak scaling keeps the first 8 (B8 ragged)
 
 
 @pytest.mark.parametrize("lengths", [[49152], [1, 15, 16, 17, 255, 256, 257, 4097],
