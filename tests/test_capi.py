@@ -99,3 +99,16 @@ def test_error_message_roundtrip_without_gpu(lib):
     rc = lib.pg_merge_state_in_place(None, None, None, None, -1, 128, 128, None)
     assert rc == 1
     assert b"non-negative" in lib.pg_last_error()
+
+
+def test_tp_publish_validation_without_gpu(lib):
+    peers = (ctypes.c_void_p * 2)(0x10000, 0x20000)
+    src = ctypes.c_void_p(0x30000)
+    assert lib.pg_tp_publish(peers, 1, 0, 64, 64, 1, src, 4096, None) == 1
+    assert b"world must be 2..8" in lib.pg_last_error()
+    assert lib.pg_tp_publish(peers, 2, 0, 64, 65, 1, src, 4160, None) == 1
+    assert b"tiles must be 1..tiles_cap" in lib.pg_last_error()
+    assert lib.pg_tp_publish(peers, 2, 0, 64, 64, 33, src, 4096, None) == 1
+    assert b"batch must be 1..32" in lib.pg_last_error()
+    assert lib.pg_tp_publish(peers, 2, 0, 64, 64, 1, src, 4000, None) == 1
+    assert b"src must be fp16" in lib.pg_last_error()
