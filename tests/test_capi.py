@@ -112,3 +112,51 @@ def test_tp_publish_validation_without_gpu(lib):
     assert b"batch must be 1..32" in lib.pg_last_error()
     assert lib.pg_tp_publish(peers, 2, 0, 64, 64, 1, src, 4000, None) == 1
     assert b"src must be fp16" in lib.pg_last_error()
+
+
+def _decode_items(items):
+    it = items.reshape(-1, 4)
+    return [(int(r), int(hs & 0xFFFF), int(hs >> 16), int(b), int(c & 0x7FFFFFFF), int((c >> 31) & 1))
+            for r, hs, b, c in it]
+
+
+def test_planner_every_page_exactly_once_ragged(lib):
+    """Ragged requests (some without old or exact pages): per (request,
+    head) the items of each segment tile its page range exactly once, in
+    order, and the item ranges partition the list."""
+    rng = np.random.default_rng(3)
+    for batch in (1, 3, 8):
+        old = rng.integers(0, 300, batch)
+        old[0] = 0
+        exact = rng.integers(0, 17, batch)
+        if batch > 1:
+            exact[1] = 0
+        exact[0] = max(int(exact[0]), 1)  # every request has at least one page
+        i0 = np.concatenate([[0], np.cumsum(old)]).astype(np.int32)
+        i1 = np.concatenate([[0], np.cumsum(exact)]).astype(np.int32)
+        for split0 in (0, 7, 64):
+            items, off, info = plan_items(batch, 8, i0, i1, split0, 0, 148)
+            decoded = _decode_items(items)
+            assert off[0] == 0 and off[-1] == info.num_items == len(decoded)
+            for r in range(batch):
+                for h in range(8):
+                    rh = r * 8 + h
+                    mine = decoded[off[rh]:off[rh + 1]]
+                    assert all(x[0] == r and x[1] == h for x in mine)
+                    for seg, (lo, hi) in enumerate(((i0[r], i0[r + 1]), (i1[r], i1[r + 1]))):
+                        runs = [(b, c, last) for _, _, s, b, c, last in mine if s == seg]
+                        pos = lo
+                        for b, c, last in runs:
+                            assert b == pos and c > 0
+                            pos += c
+                        assert pos == hi
+                        if runs:  # the last run of a segment carries the flag
+                            assert [x[2] for x in runs] == [0] * (len(runs) - 1) + [1]
+
+
+def test_planner_fixed_split_sizes_items(lib):
+    indptr = np.array([0, 100], np.int32)
+    items, off, info = plan_items(1, 8, indptr, None, 30, 0, 148)
+    counts = [c for *_, c, _ in _decode_items(items)[:off[1]]]
+    assert counts == [30, 30, 30, 10]
+    assert info.split_pages[0] == 30
