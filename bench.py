@@ -223,7 +223,8 @@ def cpu_baseline(lengths, seconds_budget: float = 15.0) -> dict:
     nbytes = algorithmic_bytes([len(old) * PAGE], [exact_tokens])
     return {"value": nbytes / dt / 1e9, "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
             "sample": f"{steps} full decode steps of one request, ctx {n} (float64 numpy "
-                      f"oracle, {torch.get_num_threads()} threads), {dt * 1e3:.1f} ms/step"}
+                      f"oracle, {torch.get_num_threads()} threads), {dt * 1e3:.1f} ms/step",
+            "ms_per_step": dt * 1e3}
 
 
 def decoder_cpu_baseline(context: int = 16384, seed: int = 20261004) -> dict:
@@ -304,7 +305,7 @@ def run_reference(args) -> None:
     line = {
         "impl": "reference", "metric": f"decode-attn HBM GB/s ({args.workload})",
         "value": base["value"], "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
+        "warmup": args.warmup, "ms_per_step": base["ms_per_step"], "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int8/fp16 storage, f64 math",
         "data": "synthetic", "config": {"workload": args.workload, "lengths": lengths[:1]},
         "cpu_baseline": base,
