@@ -82,24 +82,12 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar,
   return false;
 }
 
-// ------------------------------------------------ cross-GPU flags (NVLink)
-// System-scope release store / acquire load of a 32-bit flag that another
-// GPU writes or reads through peer memory.
-__device__ __forceinline__ void st_release_sys(int32_t* p, int32_t v) {
-  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ int32_t ld_acquire_sys(const int32_t* p) {
-  int32_t v;
-  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-// Wait until *flag >= want, about a second at most (then false).
-__device__ __forceinline__ bool flag_wait_bounded(const int32_t* flag, int32_t want) {
-  for (uint32_t i = 0; i < (1u << 24); ++i) {
-    if (ld_acquire_sys(flag) >= want) return true;
-    __nanosleep(64);
-  }
-  return false;
+// ------------------------------------------------------------ wall clock
+// The GPU's global nanosecond timer (bounds waits in time, not iterations).
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
 }
 
 // ------------------------------------------------------- bulk tensor copies

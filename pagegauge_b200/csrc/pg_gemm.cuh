@@ -578,12 +578,14 @@ struct TpReduceParams {
 };
 
 constexpr int kTpReduceThreads = 512;
+constexpr uint64_t kTpWaitNs = 1000000000ull;  // a peer's tiles: wait about a second
 
 __global__ void __launch_bounds__(kTpReduceThreads)
     pg_tp_reduce_kernel(const __grid_constant__ TpReduceParams p) {
   __shared__ float part[kTpReduceThreads / 32];
   pdl_launch_dependents();
   pdl_wait_primary();  // the producer GEMM's own pushes and counters
+  const uint64_t t0 = globaltimer_ns();
   const int b = blockIdx.x;
   const int cap = p.cap;
   const int32_t* seq = reinterpret_cast<const int32_t*>(p.exchange + tp_seq_offset(cap));
@@ -617,7 +619,9 @@ __global__ void __launch_bounds__(kTpReduceThreads)
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         for (uint32_t spin = 0; ok && static_cast<int32_t>(v[e].y) != want; ++spin) {
-          if (spin == (1u << 24)) {
+          // About a second from the kernel's start (2^26 polls as a backstop).
+          if (spin == (1u << 26) ||
+              ((spin & 255u) == 255u && globaltimer_ns() - t0 > kTpWaitNs)) {
             ok = false;
             break;
           }
