@@ -4,20 +4,27 @@
 A step is one PageGauge decode attention over one layer's cache: INT8
 page-affine old pages + the 256-token exact FP16 tail + LSE merge + value-
 centre restore, 32 Q / 8 KV heads, head_dim 128, page 16.  The headline
-workload is B1/49K (B=1, context 49,152); several layers'
-caches (more bytes than the 126 MB L2) are cycled so every step streams its
-cache from HBM.  The same line carries, under ``workloads``, the B8 ragged
-decode and the fused append step (B=8, 32 layers) measured in the
-same run (``--only`` skips them).
+workload is B1/49K (B=1, context 49,152); several layers' caches (more
+bytes than the 126 MB L2, values drawn from the three benchmark seeds) are
+cycled so every step streams its cache from HBM.  The same line carries,
+under ``workloads``, measured in the same run (``--only`` skips them):
+
+* ``b8_ragged``: the 8 ragged requests (lengths and values from each of
+  the three seeds), sharded over the ranks (strong scaling);
+* ``append_b8_32l``: the fused append step (B=8, 32 layers);
+* ``affine_group16_*``: the alternative page representation;
+* ``decoder_b1`` / ``decoder_b32``: the Mistral-7B-shaped decoder's
+  tokens/s at context 16K, tensor-parallel over the ranks (strong).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload b1_49k|b8_ragged|b1_4k] [--split PAGES] [--only]
+                    [--workload b1_49k|b8_ragged|b1_4k|decoder|gemm] [--split PAGES] [--only]
 
-Multi-GPU (torchrun, one process per GPU, no data-path collective):
-B1/49K and B1/4K run one replica per rank; B8 ragged is weak-scaled, a
-global batch of 8*N ragged requests drawn from the seed and split across
-ranks by longest-first bin packing on decode bytes.  ``value`` is the
-whole-job bytes/s: all ranks' bytes over the max-over-ranks device time.
+Multi-GPU (torchrun, one process per GPU): B1/49K and B1/4K run one replica
+per rank (weak scaling, no data-path collective); B8 ragged shards its 8
+requests over the ranks by longest-first bin packing on decode bytes (strong
+scaling, no data-path collective); the decoder is tensor-parallel by KV head.
+``value`` is the whole-job bytes/s: all ranks' bytes over the max-over-ranks
+device time.
 """
 
 from __future__ import annotations
@@ -40,14 +47,16 @@ PAGE = 16
 DIM = 128
 HQ, HKV = 32, 8
 SEED = 20261001
+SEEDS = (20261001, 20261002, 20261003)  # the benchmark configs' three seeds
 TAIL_PAGES = 16
+L2_BYTES = 126 << 20
 
 
 def parse_args():
     p = argparse.ArgumentParser(description=__doc__)
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=20000)
-    p.add_argument("--warmup", type=int, default=50)
+    p.add_argument("--steps", type=int, default=2000)
+    p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--workload", choices=("b1_49k", "b8_ragged", "b1_4k", "decoder", "gemm"),
                    default="b1_49k")
@@ -83,17 +92,58 @@ def algorithmic_bytes(old_tokens, exact_tokens, hkv=HKV) -> int:
     return total
 
 
-def workload_lengths(name: str, world: int = 1, rank: int = 0):
-    """(this rank's request lengths, global lengths, shards)."""
-    from pagegauge_b200.shard import ragged_lengths, shard_requests
+def global_lengths(name: str, seed: int = SEED) -> list[int]:
+    """Request lengths of a workload (all ranks together)."""
+    from pagegauge_b200.shard import ragged_lengths
 
     if name == "b1_49k":
-        return [49152], [49152] * world, None
+        return [49152]
     if name == "b1_4k":
-        return [4096], [4096] * world, None
-    glob = ragged_lengths(8 * world, SEED)
+        return [4096]
+    return ragged_lengths(8, seed)
+
+
+def workload_bytes(lengths) -> int:
+    """Algorithmic bytes of one decode step over ``lengths`` (the last
+    TAIL_PAGES pages of each request exact FP16, the rest INT8)."""
+    old, exact = [], []
+    for n in lengths:
+        pages = -(-n // PAGE)
+        n_old = max(pages - TAIL_PAGES, 0)
+        old.append(n_old * PAGE)
+        exact.append(n - n_old * PAGE)
+    return algorithmic_bytes(old, exact)
+
+
+def workload_lengths(name: str, world: int = 1, rank: int = 0, seed: int = SEED):
+    """(this rank's request lengths, global lengths, shards or None).
+    B1 workloads are replicas (every rank runs the whole request); B8
+    ragged shards its 8 requests over the ranks."""
+    from pagegauge_b200.shard import shard_requests
+
+    glob = global_lengths(name, seed)
+    if name in ("b1_49k", "b1_4k"):
+        return list(glob), glob, None
     shards = shard_requests(glob, world)
     return [glob[i] for i in shards[rank]], glob, shards
+
+
+def workload_config(args, world: int) -> dict:
+    """The ``config`` both arms print, identical for the same command line:
+    the workload's shape, seeds, how the L2 is kept out of the timing, and
+    how it is split over GPUs."""
+    lengths = global_lengths(args.workload)
+    nbytes = workload_bytes(lengths)
+    replicas = args.workload in ("b1_49k", "b1_4k")
+    return {
+        "workload": args.workload, "lengths": lengths, "hq": HQ, "hkv": HKV, "head_dim": DIM,
+        "page": PAGE, "exact_tail_tokens": TAIL_PAGES * PAGE, "seeds": list(SEEDS),
+        "l2": (f"{args.layers} layer caches cycled (values from the seeds in turn), "
+               f"{args.layers * nbytes / 1e6:.0f} MB > 126 MB L2: each step reads its cache "
+               f"from HBM"),
+        "parallelism": (f"replicas x{world} (weak)" if replicas
+                        else f"requests sharded over {world} GPU(s) (strong)"),
+    }
 
 
 class Dist:
@@ -135,7 +185,10 @@ def profile_traffic(workload: str):
 
 
 class ClockSampler:
-    """nvidia-smi sampling during the timed region."""
+    """nvidia-smi sampling (every 100 ms) across the whole measured phase:
+    the headline steps, the kernel-only graphs, the end-to-end runs and the
+    secondary workloads (a single timed region is far shorter than one
+    sampling period)."""
 
     FIELDS = "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active," \
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown," \
@@ -145,6 +198,12 @@ class ClockSampler:
         self.index = index
         self.proc = None
         self.lines: list[str] = []
+
+    def start(self):
+        return self.__enter__()
+
+    def stop(self):
+        self.__exit__(None, None, None)
 
     def __enter__(self):
         try:
@@ -194,35 +253,19 @@ def cpu_baseline(lengths, seconds_budget: float = 15.0) -> dict:
     """The CPU oracle (float64 numpy restatement) on a bounded sample: whole
     decode steps of the first request of the workload until the budget is
     used (at least one step)."""
-    from oracle import pagegauge_oracle as O
-    from pagegauge_b200.cache import synthetic_dense_cache
-
     torch.set_num_threads(os.cpu_count() or 1)
-    n = lengths[0]
-    q, dk, dv = synthetic_dense_cache([n], seed=SEED)
-    q, dk, dv = q.numpy(), dk.numpy(), dv.numpy()
-    pages = -(-n // PAGE)
-    tail = min(TAIL_PAGES, pages)
-    center_k = dk.reshape(-1, HKV, DIM)[:n].astype(np.float32).mean(0).astype(np.float16)
-    center_v = dv.reshape(-1, HKV, DIM)[:n].astype(np.float32).mean(0).astype(np.float16)
-    ck, sk = O.quantize_pages_bulk(dk, center_k)
-    cv, sv = O.quantize_pages_bulk(dv, center_v)
-    ek = (dk[pages - tail:].astype(np.float32) - center_k.astype(np.float32)).astype(np.float16)
-    ev = (dv[pages - tail:].astype(np.float32) - center_v.astype(np.float32)).astype(np.float16)
-    old = list(range(pages - tail))
-    exact_tokens = n - len(old) * PAGE
+    fn, nbytes = reference_decode_sample(lengths[:1], SEED)
     steps = 0
     t0 = time.perf_counter()
     while True:
-        O.page_gauge_decode(q[0], ck, cv, sk, sv, old, len(old) * PAGE, ek, ev, list(range(tail)),
-                            exact_tokens, center_v, 1.0 / math.sqrt(DIM))
+        fn()
         steps += 1
         if time.perf_counter() - t0 > seconds_budget or steps >= 20:
             break
     dt = (time.perf_counter() - t0) / steps
-    nbytes = algorithmic_bytes([len(old) * PAGE], [exact_tokens])
-    return {"value": nbytes / dt / 1e9, "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
-            "sample": f"{steps} full decode steps of one request, ctx {n} (float64 numpy "
+    return {"value": nbytes / dt / 1e9, "unit": "GB/s", "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"{steps} full decode steps of one request, ctx {lengths[0]} (float64 numpy "
                       f"oracle, {torch.get_num_threads()} threads), {dt * 1e3:.1f} ms/step",
             "ms_per_step": dt * 1e3}
 
@@ -282,12 +325,46 @@ def decoder_cpu_baseline(context: int = 16384, seed: int = 20261004) -> dict:
                       f"{t_head:.2f} s; 32-layer step = 32 layers + head = {t_step:.1f} s"}
 
 
+def reference_decode_sample(lengths, seed: int):
+    """One request's PageGauge cache as the CPU oracle reads it (float64
+    numpy restatement of the reference path): returns a function running
+    one whole decode step of that request, and its algorithmic bytes."""
+    from oracle import pagegauge_oracle as O
+    from pagegauge_b200.cache import synthetic_dense_cache
+
+    n = lengths[0]
+    q, dk, dv = synthetic_dense_cache([n], seed=seed)
+    q, dk, dv = q.numpy(), dk.numpy(), dv.numpy()
+    pages = -(-n // PAGE)
+    tail = min(TAIL_PAGES, pages)
+    center_k = dk.reshape(-1, HKV, DIM)[:n].astype(np.float32).mean(0).astype(np.float16)
+    center_v = dv.reshape(-1, HKV, DIM)[:n].astype(np.float32).mean(0).astype(np.float16)
+    ck, sk = O.quantize_pages_bulk(dk, center_k)
+    cv, sv = O.quantize_pages_bulk(dv, center_v)
+    ek = (dk[pages - tail:].astype(np.float32) - center_k.astype(np.float32)).astype(np.float16)
+    ev = (dv[pages - tail:].astype(np.float32) - center_v.astype(np.float32)).astype(np.float16)
+    old = list(range(pages - tail))
+    exact_tokens = n - len(old) * PAGE
+
+    def step():
+        O.page_gauge_decode(q[0], ck, cv, sk, sv, old, len(old) * PAGE, ek, ev,
+                            list(range(tail)), exact_tokens, center_v, 1.0 / math.sqrt(DIM))
+
+    return step, algorithmic_bytes([len(old) * PAGE], [exact_tokens])
+
+
 def run_reference(args) -> None:
-    """The reference arm: the CPU restatement of the reference's path (the
-    oracle port) on this box's host cores, rank 0 only."""
+    """The reference arm: the reference's path restated on the CPU (the
+    oracle port: float64 numpy, all host threads) on this box's host cores,
+    rank 0 only; ``--warmup`` untimed then exactly ``--steps`` timed steps,
+    each step one whole decode of a request of the workload (B1 workloads:
+    the request; B8 ragged: the requests in turn), same config as the GPU
+    arm."""
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
+    torch.set_num_threads(os.cpu_count() or 1)
     if args.workload == "decoder":
         base = decoder_cpu_baseline()
         print(json.dumps({
@@ -300,16 +377,33 @@ def run_reference(args) -> None:
             "e2e": {"value": base["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}), flush=True)
         return
-    lengths, _, _ = workload_lengths(args.workload)
-    base = cpu_baseline(lengths[:1], seconds_budget=10.0)
+    glob = global_lengths(args.workload)
+    samples = [reference_decode_sample([glob[i]], SEEDS[i % len(SEEDS)])
+               for i in range(len(glob))]
+    for i in range(args.warmup):
+        samples[i % len(samples)][0]()
+    total_bytes, t0 = 0, time.perf_counter()
+    for i in range(args.steps):
+        fn, nbytes = samples[i % len(samples)]
+        fn()
+        total_bytes += nbytes
+    dt = time.perf_counter() - t0
+    value = total_bytes / dt / 1e9
+    sample = (f"{args.steps} timed decode steps after {args.warmup} warm-up steps, each one whole "
+              f"request of the workload ({'the request' if len(glob) == 1 else 'the 8 requests in turn'}; "
+              f"float64 numpy oracle, {torch.get_num_threads()} threads), "
+              f"{dt / args.steps * 1e3:.1f} ms/step")
     line = {
         "impl": "reference", "metric": f"decode-attn HBM GB/s ({args.workload})",
-        "value": base["value"], "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": base["ms_per_step"], "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "int8/fp16 storage, f64 math",
-        "data": "synthetic", "config": {"workload": args.workload, "lengths": lengths[:1]},
-        "cpu_baseline": base,
-        "e2e": {"value": base["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "weak" if args.workload in ("b1_49k", "b1_4k") else "strong",
+        "vs_baseline": None, "dtype": "int8/fp16 storage, f64 math",
+        "data": "synthetic (seeded; K=RoPE(N(mu,1)), mu~N(0,2); V,Q~N(0,1))",
+        "config": workload_config(args, world),
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": torch.get_num_threads(),
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
@@ -333,7 +427,9 @@ class AttentionBench:
         self.caches = []
         self.q = self.tables = None
         for layer in range(self.layers):
-            qi, dk, dv = synthetic_dense_cache(lengths, seed=seed + layer, device="cuda")
+            # layer copies take their values from the benchmark seeds in turn
+            qi, dk, dv = synthetic_dense_cache(lengths, seed=seed + layer % len(SEEDS),
+                                               device="cuda")
             cache, tables = build_gauge_cache(dk, dv, lengths, capacity_pages=cap)
             del dk, dv
             self.caches.append(cache)
@@ -369,27 +465,38 @@ class AttentionBench:
             for layer in range(self.layers):
                 self.step(layer)
             torch.cuda.synchronize()
-            self.chunk_graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(self.chunk_graph, stream=self.stream):
-                for i in range(self.chunk):
-                    self.step(i % self.layers)
-            self.single = []
-            for layer in range(self.layers):
-                g = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(g, stream=self.stream):
-                    self.step(layer)
-                self.single.append(g)
+            self.chunk_graph = self._graph(self.chunk)
+        self.rest = {}
         torch.cuda.synchronize()
 
+    def _graph(self, n: int):
+        """A CUDA graph of n back-to-back steps cycling the layers from 0."""
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=self.stream):
+            for i in range(n):
+                self.step(i % self.layers)
+        return g
+
+    def prepare_steps(self, k: int) -> None:
+        """Capture the graph of the k % chunk remainder (outside timing)."""
+        r = k % self.chunk
+        if r and r not in self.rest:
+            with torch.cuda.stream(self.stream):
+                self.rest[r] = self._graph(r)
+            torch.cuda.synchronize()
+
     def run_steps(self, k: int) -> None:
-        """Exactly k steps cycling the layers: graphs of ``chunk`` steps,
-        then single-step graphs for the remainder."""
+        """Exactly k steps cycling the layers: graphs of ``chunk`` steps
+        (a multiple of the layer count), then one graph of the remainder,
+        so even k < chunk runs as one graph of back-to-back steps."""
         for _ in range(k // self.chunk):
             self.chunk_graph.replay()
-        for i in range(k - k % self.chunk, k):
-            self.single[i % self.layers].replay()
+        if k % self.chunk:
+            self.rest[k % self.chunk].replay()
 
     def time_steps(self, steps: int, warmup: int, dist: Dist, clocks=None) -> float:
+        self.prepare_steps(max(warmup, 3))
+        self.prepare_steps(steps)
         self.run_steps(max(warmup, 3))
         torch.cuda.synchronize()
         dist.barrier()
@@ -986,12 +1093,13 @@ def main() -> None:
         return
     peak, peak_src = peak_hbm()
     lengths, glob, shards = workload_lengths(args.workload, world, rank)
+    clocks = ClockSampler(local)
+    clocks.start()  # covers every measurement below
     bench = AttentionBench(lengths, args.layers, args.split, args.merge == "fused",
                            seed=SEED + 1000 * rank, warps=args.warps,
                            cluster=args.cluster if args.merge == "cluster" else 0)
     bench.capture()
-    clocks = ClockSampler(local)
-    ms = bench.time_steps(args.steps, args.warmup, dist, clocks)
+    ms = bench.time_steps(args.steps, args.warmup, dist)
     total_bytes = dist.reduce(float(bench.nbytes), "sum")
     value = total_bytes / (ms * 1e-3) / 1e9
     kernel_ms = dist.reduce(bench.kernel_ms(args.steps), "max")
@@ -1004,34 +1112,24 @@ def main() -> None:
         e2e_ms = e2e["zero_copy_graph_ms"]
         e2e_mode = ("CUDA graph of the public-API step, inputs read and output written in "
                     "pinned host memory by the kernels (zero copy)")
+    plan_info = {"split_pages": bench.plan.split_pages[0], "work_items": bench.plan.num_items,
+                 "launches_per_step": bench.launches_per_step}
+    del bench
+    torch.cuda.empty_cache()
 
     workloads = {}
     if not args.only and args.workload == "b1_49k":
-        b8_len, b8_glob, b8_shards = workload_lengths("b8_ragged", world, rank)
-        b8 = AttentionBench(b8_len, args.layers, -1, False, seed=SEED + 1000 * rank + 500)
-        b8.capture()
-        b8_steps = max(200, args.steps // 10)
-        b8_ms = b8.time_steps(b8_steps, args.warmup, dist)
-        b8_total = dist.reduce(float(b8.nbytes), "sum")
-        b8_kms = dist.reduce(b8.kernel_ms(b8_steps), "max")
-        workloads["b8_ragged"] = {
-            "metric": "decode-attn HBM GB/s (b8_ragged)", "unit": "GB/s",
-            "value": round(b8_total / (b8_ms * 1e-3) / 1e9, 2), "us_per_step": b8_ms * 1e3,
-            "steps": b8_steps, "kernel_us": b8_kms * 1e3,
-            "roofline_frac": round(b8.nbytes / (b8_kms * 1e-3) / 1e9 / peak, 4),
-            "algorithmic_bytes_per_step_per_rank": b8.nbytes,
-            "global_batch": len(b8_glob), "lengths_rank0": b8_len,
-            "shards": b8_shards, "split_pages": b8.plan.split_pages[0],
-            "work_items": b8.plan.num_items, "scaling": "weak",
-        }
-        attn_layer_us = b8_ms * 1e3
-        del b8
-        torch.cuda.empty_cache()
+        workloads["b8_ragged"] = measure_b8_sharded(args, dist, rank, peak)
         app = measure_append(dist)
-        app["attention_us_per_layer_b8"] = attn_layer_us
-        app["pct_of_attention_step"] = round(100 * app["us_per_layer"] / attn_layer_us, 2)
-        app["increment_pct_of_attention_step"] = round(
-            100 * app["increment_us_per_step"] / app["layers"] / attn_layer_us, 2)
+        if world == 1:
+            # The append's share of a decode step: against the B8 attention
+            # step of the same 8 requests on one GPU (first seed).
+            attn_layer_us = workloads["b8_ragged"]["per_seed"][0]["us_per_step"]
+            app["attention_us_per_layer_b8"] = attn_layer_us
+            app["pct_of_attention_step"] = round(100 * app["us_per_layer"] / attn_layer_us, 2)
+            app["increment_pct_of_attention_step"] = round(
+                100 * app["increment_us_per_step"] / app["layers"] / attn_layer_us, 2)
+        app["scaling"] = "weak (replicas)"
         workloads["append_b8_32l"] = app
         aff = AffineBench(lengths, args.layers, args.split, seed=SEED + 1000 * rank + 900,
                           warps=args.warps)
@@ -1046,40 +1144,43 @@ def main() -> None:
             "roofline_frac": round(aff.nbytes / (aff_kms * 1e-3) / 1e9 / peak, 4),
             "algorithmic_bytes_per_step_per_rank": aff.nbytes,
             "split_pages": aff.plan.split_pages[0], "work_items": aff.plan.num_items,
+            "scaling": "weak (replicas)",
             "note": "the reference's rejected representation, same kernel family; "
                     "page_gauge is the headline",
         }
         del aff
         torch.cuda.empty_cache()
+        for b in (1, 32):
+            d = measure_decoder(dist, b, steps=args.decoder_steps, gemm=args.decoder_gemm,
+                                policy=args.decoder_policy, tp_reduce=args.decoder_tp_reduce)
+            d["scaling"] = f"strong (tensor parallel over {world} GPU(s))"
+            workloads[f"decoder_b{b}"] = d
+    clocks.stop()
+    err = read_device_error()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(lengths[:1])
-    err = read_device_error()
+        if "decoder_b1" in workloads:
+            workloads["decoder_b1"]["cpu_baseline"] = decoder_cpu_baseline()
 
     if rank == 0:
-        cfg = {"workload": args.workload, "lengths": lengths, "hq": HQ, "hkv": HKV,
-               "head_dim": DIM, "page": PAGE, "exact_tail_tokens": TAIL_PAGES * PAGE,
-               "split_pages": bench.plan.split_pages[0], "work_items": bench.plan.num_items,
-               "layers_cycled": bench.layers,
-               "l2": f"{bench.layers} layer caches cycled "
-                     f"({bench.layers * bench.nbytes / 1e6:.0f} MB > 126 MB L2)",
-               "parallelism": (f"replicas x{world}" if shards is None
-                               else f"requests sharded over {world} (weak, global batch {len(glob)})")}
         line = {
             "metric": f"decode-attn HBM GB/s ({args.workload})",
             "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": max(args.warmup, 3), "ms_per_step": ms, "us_per_step": ms * 1e3,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True,
+            "scaling": "weak" if shards is None else "strong", "vs_baseline": None,
             "dtype": "int8 codes + fp16 tail, fp16 mma / fp32 softmax",
             "data": "synthetic (seeded; K=RoPE(N(mu,1)), mu~N(0,2); V,Q~N(0,1))",
-            "config": cfg,
-            "algorithmic_bytes_per_step": bench.nbytes,
+            "config": workload_config(args, world),
+            "plan": plan_info,
+            "algorithmic_bytes_per_step": workload_bytes(lengths),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "traffic": profile_traffic(args.workload), "peak_source": peak_src,
                          "kernel": "pg_decode_split_kernel", "kernel_us": kernel_ms * 1e3},
-            "gpu_launches": bench.launches_per_step * args.steps,
+            "gpu_launches": plan_info["launches_per_step"] * args.steps,
             "e2e": {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
                     "us_per_step": e2e_ms * 1e3,
@@ -1099,9 +1200,55 @@ def main() -> None:
         }
         print(json.dumps(line), flush=True)
     if world > 1:
-        del bench
         dist.barrier()
         dist.dist.destroy_process_group()
+
+
+def measure_b8_sharded(args, dist: Dist, rank: int, peak: float) -> dict:
+    """the 8 ragged requests of each seed, sharded over the ranks
+    by longest-first bin packing (strong scaling: the same 8 requests at
+    every N, no data-path collective).  Per seed: max-over-ranks step time,
+    aggregate GB/s, the kernel's roofline fraction and the per-rank byte
+    imbalance (max / mean)."""
+    from pagegauge_b200.shard import request_bytes
+
+    world = dist.world
+    steps = max(200, args.steps // 10)
+    per_seed = []
+    for seed in SEEDS:
+        mine, glob, shards = workload_lengths("b8_ragged", world, rank, seed=seed)
+        loads = [sum(request_bytes(glob[i]) for i in sh) for sh in shards]
+        if mine:
+            b8 = AttentionBench(mine, args.layers, -1, False, seed=seed)
+            b8.capture()
+            my_bytes = b8.nbytes
+            b8_ms = b8.time_steps(steps, args.warmup, dist)
+            b8_kms = dist.reduce(b8.kernel_ms(steps), "max")
+            split, items = b8.plan.split_pages[0], b8.plan.num_items
+            del b8
+            torch.cuda.empty_cache()
+        else:  # more ranks than requests: this rank only joins the collectives
+            my_bytes, split, items = 0, 0, 0
+            dist.barrier()  # the two barriers and the reduce of time_steps
+            dist.barrier()
+            b8_ms = dist.reduce(0.0, "max")
+            b8_kms = dist.reduce(0.0, "max")
+        total = dist.reduce(float(my_bytes), "sum")
+        per_seed.append({
+            "seed": seed, "lengths": glob, "shards": shards, "value_gbs": round(total / (b8_ms * 1e-3) / 1e9, 2),
+            "us_per_step": b8_ms * 1e3, "kernel_us": b8_kms * 1e3,
+            "kernel_frac_of_peak": round(max(loads) / (b8_kms * 1e-3) / 1e9 / peak, 4),
+            "algorithmic_bytes_per_step": int(total), "rank_bytes": loads,
+            "imbalance": round(max(loads) / (sum(loads) / len(loads)), 4),
+            "split_pages_rank0": split, "work_items_rank0": items,
+        })
+    tot_bytes = sum(x["algorithmic_bytes_per_step"] for x in per_seed)
+    tot_us = sum(x["us_per_step"] for x in per_seed)
+    return {"metric": "decode-attn HBM GB/s (b8_ragged, 3 seeds)", "unit": "GB/s",
+            "value": round(tot_bytes / (tot_us * 1e-6) / 1e9, 2),
+            "us_per_step_mean": tot_us / len(per_seed), "steps": steps,
+            "scaling": f"strong (the 8 requests sharded over {world} GPU(s))",
+            "per_seed": per_seed}
 
 
 if __name__ == "__main__":

@@ -95,7 +95,9 @@ int32_t pg_tp_publish(void* const* peers, int32_t world, int32_t rank, int32_t t
                       void* stream);
 
 /* Consume a tensor-parallel GEMM's published tiles on this rank: wait
- * (about a second at most, then PG_DEV_WAIT_TIMEOUT) until all `world`
+ * (about a second at most, then PG_DEV_WAIT_TIMEOUT, and a row whose tiles
+ * did not all arrive stores nothing, so residual and out keep their
+ * contents and the step can be repeated) until all `world`
  * ranks' tiles of the `tiles` output tiles have arrived in this rank's
  * `exchange` buffer, sum them in rank order (FP32; identical on every
  * rank) and, per batch row (batch = the GEMM's rows):
@@ -305,6 +307,16 @@ typedef struct pg_decode_args {
                              scripts/benchmark_flashinfer_page_affine_int8.py:166-189, :567-578 */
   const void* k_bias;
   const void* v_bias;
+  int32_t int8_after_wait; /* 0: the INT8 tiles are requested before the
+                              kernel waits for the previous kernel in the
+                              stream (programmatic dependent launch), which
+                              overlaps them with its drain; correct only if
+                              none of the kernels that may still run wrote
+                              those pages.  1: request them after that wait.
+                              Set it when a page closed by an append is read
+                              as INT8 by the next step's decode (a one-page
+                              exact ring), where the append of the previous
+                              step may still be running. */
 } pg_decode_args;
 
 int32_t pg_decode_run(const pg_decode_args* args, void* stream);
@@ -326,8 +338,10 @@ int32_t pg_decode_max_clusters(int32_t warps, int32_t cluster, int32_t* out);
  * (request, kv head) pairs, and the partial states must fit the array
  * (about 2 KiB per item at GQA group 4); larger plans fail with
  * PG_ERR_CAPACITY and a message.  No cudaMalloc/cudaFree is called.  The
- * first call on each device looks up the array's device address, so make
- * it before any stream capture.  Calls on one device share that device's
+ * first call on each device looks up the array's device address.  Each
+ * call copies its plan from host memory, so a call on a stream that is
+ * being captured is refused (PG_ERR_INVALID) before anything is enqueued.
+ * Calls on one device share that device's
  * array and it keeps the last call's contents (nothing in it has to start
  * at zero: every call rewrites what it reads); two calls that run at the
  * same time on one GPU, e.g. on two streams, race on it. */

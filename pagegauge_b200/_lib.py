@@ -50,6 +50,7 @@ class PgDecodeArgs(ctypes.Structure):
         ("value_center", c_vp), ("vc_stride_b", c_i64), ("stage_mask", c_i32),
         ("merge_sem", c_vp), ("cluster", c_i32),
         ("representation", c_i32), ("k_bias", c_vp), ("v_bias", c_vp),
+        ("int8_after_wait", c_i32),
     ]
 
 

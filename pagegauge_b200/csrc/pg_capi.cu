@@ -141,13 +141,19 @@ int32_t ensure_decode_smem() {
   std::lock_guard<std::mutex> lock(mu);
   if (!done[dev]) {
     int32_t rc = cuda_check(
-        cudaFuncSetAttribute(pg::pg_decode_split_kernel<pg::kRepGauge>,
+        cudaFuncSetAttribute(pg::pg_decode_split_kernel<pg::kRepGauge, false>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              pg::decode_smem_bytes_rep(pg::kRepGauge, pg::kMaxWarps)),
         "cudaFuncSetAttribute(decode smem)");
     if (rc != PG_OK) return rc;
     rc = cuda_check(
-        cudaFuncSetAttribute(pg::pg_decode_split_kernel<pg::kRepAffine16>,
+        cudaFuncSetAttribute(pg::pg_decode_split_kernel<pg::kRepGauge, true>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             pg::decode_smem_bytes_rep(pg::kRepGauge, pg::kMaxWarps)),
+        "cudaFuncSetAttribute(wide-group decode smem)");
+    if (rc != PG_OK) return rc;
+    rc = cuda_check(
+        cudaFuncSetAttribute(pg::pg_decode_split_kernel<pg::kRepAffine16, false>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              pg::decode_smem_bytes_rep(pg::kRepAffine16, pg::kMaxWarps)),
         "cudaFuncSetAttribute(affine decode smem)");
@@ -183,10 +189,18 @@ int32_t launch_decode(const pg::DecodeParams& p, const CUtensorMap& k8,
   cfg.numAttrs = cluster > 1 ? 2 : 1;
   if (rep == pg::kRepAffine16)
     return cuda_check(
-        cudaLaunchKernelEx(&cfg, pg::pg_decode_split_kernel<pg::kRepAffine16>, k8, v8, k16, v16, p),
+        cudaLaunchKernelEx(&cfg, pg::pg_decode_split_kernel<pg::kRepAffine16, false>, k8, v8,
+                           k16, v16, p),
         "affine decode kernel launch");
+  // GQA groups of 5-8 query rows need the second query-split MMA.
+  if (p.group > 4)
+    return cuda_check(
+        cudaLaunchKernelEx(&cfg, pg::pg_decode_split_kernel<pg::kRepGauge, true>, k8, v8, k16,
+                           v16, p),
+        "decode kernel launch");
   return cuda_check(
-      cudaLaunchKernelEx(&cfg, pg::pg_decode_split_kernel<pg::kRepGauge>, k8, v8, k16, v16, p),
+      cudaLaunchKernelEx(&cfg, pg::pg_decode_split_kernel<pg::kRepGauge, false>, k8, v8, k16,
+                         v16, p),
       "decode kernel launch");
 }
 
@@ -226,7 +240,7 @@ extern "C" {
 
 const char* pg_last_error(void) { return g_last_error.c_str(); }
 
-int32_t pg_abi_version(void) { return 106; }
+int32_t pg_abi_version(void) { return 107; }
 
 int64_t pg_tp_exchange_bytes(int32_t tiles_cap) {
   return tiles_cap > 0 ? pg::tp_exchange_bytes(tiles_cap) : -1;
@@ -855,6 +869,7 @@ int32_t pg_decode_run(const pg_decode_args* a, void* stream) {
   p.value_center = static_cast<const __half*>(a->value_center);
   p.vc_stride_b = a->vc_stride_b;
   p.implicit_pages = 0;
+  p.int8_after_wait = a->int8_after_wait != 0;
   p.error_flag = device_error_ptr();
   const bool fused = a->merge_sem != nullptr && !a->final_mode;
   p.sem = fused ? a->merge_sem : nullptr;
@@ -932,7 +947,7 @@ int32_t pg_decode_max_clusters(int32_t warps, int32_t cluster, int32_t* out) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int n = 0;
-  rc = cuda_check(cudaOccupancyMaxActiveClusters(&n, pg::pg_decode_split_kernel<pg::kRepGauge>, &cfg),
+  rc = cuda_check(cudaOccupancyMaxActiveClusters(&n, pg::pg_decode_split_kernel<pg::kRepGauge, false>, &cfg),
                   "cudaOccupancyMaxActiveClusters");
   if (rc != PG_OK) return rc;
   *out = n;
@@ -1376,6 +1391,18 @@ int32_t pg_decode_static(const pg_decode_args* args, const int32_t* indptr0,
                          const int32_t* indptr1, int32_t split_pages0,
                          int32_t split_pages1, int32_t num_sms, void* stream) {
   PG_REQUIRE(args != nullptr, "null arguments");
+  {
+    // Every call copies its plan from host memory, which a stream capture
+    // cannot record; refuse before enqueuing anything, so the caller's
+    // capture stays valid.
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    int32_t rc0 = cuda_check(cudaStreamIsCapturing(static_cast<cudaStream_t>(stream), &cs),
+                             "cudaStreamIsCapturing");
+    if (rc0 != PG_OK) return rc0;
+    PG_REQUIRE(cs == cudaStreamCaptureStatusNone,
+               "pg_decode_static cannot run while its stream is being captured: it copies "
+               "its plan from host memory on every call");
+  }
   PG_REQUIRE(static_cast<int64_t>(args->batch) * args->kv_heads <= kStaticMaxHeads,
              "pg_decode_static supports at most %lld (request, kv head) pairs",
              static_cast<long long>(kStaticMaxHeads));

@@ -353,8 +353,9 @@ __device__ __noinline__ void cluster_epilogue(const DecodeParams& p, int W, cons
 
 // 168 registers per thread at most: three 4-warp CTAs per SM (the host
 // planner's slot count assumes it).  REP selects segment 0's page
-// representation (kRepGauge or kRepAffine16).
-template <int REP>
+// representation (kRepGauge or kRepAffine16); WIDE (PageGauge only) is the
+// GQA 5-8 form of the INT8 query split.
+template <int REP, bool WIDE>
 __global__ void __maxnreg__(168)
     pg_decode_split_kernel(const __grid_constant__ CUtensorMap tm_k8,
                            const __grid_constant__ CUtensorMap tm_v8,
@@ -420,9 +421,9 @@ __global__ void __maxnreg__(168)
   bool ok;
   if (seg == 0) {
     if constexpr (REP == kRepGauge) {
-      QInt8 qi;
-      ok = run_warp_pages_int8(p, &tm_k8, &tm_v8, st, ring, bars, qi, r, h,
-                               item.idx_begin, n_pages, has_last, warp, W, lane);
+      QInt8<WIDE> qi;
+      ok = run_warp_pages_int8<WIDE>(p, &tm_k8, &tm_v8, st, ring, bars, qi, r, h,
+                                     item.idx_begin, n_pages, has_last, warp, W, lane);
       // Remove the +1152 code bias of the PV operand: O -= 1152 * sum(P'').
       const float sp0 = 1152.f * __shfl_sync(0xffffffffu, st.o1[0], t);
       const float sp1 = 1152.f * __shfl_sync(0xffffffffu, st.o1[1], t);

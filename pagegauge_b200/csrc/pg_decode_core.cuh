@@ -66,6 +66,10 @@ struct DecodeParams {
   // matching group biases.
   const __half* k_bias;
   const __half* v_bias;
+  // 1: INT8 tiles only after griddepcontrol.wait (their pages may have been
+  // written by a kernel that is still running, e.g. an append that closed
+  // a page of a one-page exact ring).
+  int32_t int8_after_wait;
 };
 
 // Page representations of segment 0 (one kernel instantiation each).
@@ -105,16 +109,24 @@ struct WarpState {
   float sref;            // reference V scale (INT8 segment)
 };
 
-// Q for the INT8 segment as two int8 parts per row, q ~ sq * (hi + lo/254)
-// with sq = max|q_row| / 127 (|error| <= sq/508).  Q is the A operand of
-// mma.m16n8k32.s8: rows 0-7 hold the hi parts of the GQA query rows, rows
-// 8-15 the lo parts, so one mma yields both partial dot products of a
-// query row in the same thread.  a[ks] = {hi dims 32t+8ks+0..3, lo same,
-// hi dims 32t+8ks+4..7, lo same} of query row g (the B operand, K, uses
-// the identical dimension order).
+// Q for the INT8 segment as three int8 parts per row,
+//   q ~ sq * (hi + lo/254 + lo2/254^2),   sq = max|q_row| / 127,
+// |error| <= sq/129032 = max|q_row|/16.4e6 per element (the FP16 input
+// itself is only exact to 2^-11 relative).  Two parts (error sq/508) lose
+// the small channels of a row that has outlier channels; the third part
+// keeps every channel of such a row within FP16 resolution of its largest.
+// Q is the A operand of mma.m16n8k32.s8 and a[ks] = {row g dims
+// 32t+8ks+0..3, row g+8 same, row g dims 32t+8ks+4..7, row g+8 same}
+// (the B operand, K, uses the identical dimension order):
+//   GQA group <= 4: rows 0-3 hi, rows 8-11 lo, rows 4-7 lo2 of query rows
+//     0-3 (rows 12-15 zero); lane g < 4 adds the lo2 products of lane g+4.
+//   GQA group 5-8 (WIDE): rows 0-7 hi, rows 8-15 lo, and a second mma
+//     whose rows 0-7 are the lo2 parts (a2 = its non-zero registers).
+template <bool WIDE>
 struct QInt8 {
   uint32_t a[4][4];
-  float c;  // sq(row g) / 254 * sm_scale * log2(e)
+  uint32_t a2[WIDE ? 4 : 1][2];
+  float c;  // sq(row g) / 254^2 * sm_scale * log2(e); 0 on lanes holding no row's hi part
 };
 
 // A page's scores may exceed the running reference max by this many log2

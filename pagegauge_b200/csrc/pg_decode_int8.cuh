@@ -1,5 +1,5 @@
 // INT8 PageGauge pages of the split-KV decode (segment 0, one FP16 scale
-// per (page, KV head)): Q split into two int8 parts for the integer MMA,
+// per (page, KV head)): Q split into three int8 parts for the integer MMA,
 // QK on IMMA with the K scale applied to the fp32 scores, the V scale
 // folded into P for an FP16 PV on biased codes, and the per-warp TMA
 // pipeline that takes the pages two at a time.
@@ -16,14 +16,19 @@ __device__ __forceinline__ uint32_t pack_s8x4(int a, int b, int c, int d) {
 
 __device__ __forceinline__ int clamp127(int v) { return v < -127 ? -127 : (v > 127 ? 127 : v); }
 
-// Two-part int8 Q for the INT8 segment (thread t owns dims [32t, 32t+32)).
+// Three-part int8 Q for the INT8 segment (thread t owns dims [32t, 32t+32)).
+// GQA <= 4: lanes g and g+4 both split query row g & 3; lane g packs its
+// (hi, lo), lane g+4 its (lo2, 0).  WIDE: lane g splits query row g.
+template <bool WIDE>
 __device__ __forceinline__ void load_q_int8(const DecodeParams& p, int r, int h,
-                                            int g, int t, QInt8& qi) {
+                                            int g, int t, QInt8<WIDE>& qi) {
   float qv[32];
-  if (g < p.group) {
+  const int row = WIDE ? g : (g & 3);
+  const bool second = !WIDE && g >= 4;  // this lane holds row's lo2 part
+  if (row < p.group) {
     const __half2* q2 = reinterpret_cast<const __half2*>(
         p.q + static_cast<int64_t>(r) * p.q_stride_b +
-        static_cast<int64_t>(h * p.group + g) * p.q_stride_h + 32 * t);
+        static_cast<int64_t>(h * p.group + row) * p.q_stride_h + 32 * t);
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
       const float2 f = __half22float2(q2[i]);
@@ -42,24 +47,38 @@ __device__ __forceinline__ void load_q_int8(const DecodeParams& p, int r, int h,
   const float sq = amax > 0.f ? amax / 127.f : 1.f;
   const float inv = 1.f / sq;
   const float inv_lo = 254.f / sq;
+  const float inv_lo2 = 64516.f / sq;
+  const float step_lo = sq / 254.f;
 #pragma unroll
   for (int ks = 0; ks < 4; ++ks) {
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
-      int hv[4], lv[4];
+      int hv[4], lv[4], l2[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const float x = qv[8 * ks + 4 * half + i];
         const int hi = clamp127(__float2int_rn(x * inv));
         const float rem = fmaf(-static_cast<float>(hi), sq, x);
+        const int lo = clamp127(__float2int_rn(rem * inv_lo));
+        const float rem2 = fmaf(-static_cast<float>(lo), step_lo, rem);
         hv[i] = hi;
-        lv[i] = clamp127(__float2int_rn(rem * inv_lo));
+        lv[i] = lo;
+        l2[i] = clamp127(__float2int_rn(rem2 * inv_lo2));
       }
-      qi.a[ks][2 * half] = pack_s8x4(hv[0], hv[1], hv[2], hv[3]);
-      qi.a[ks][2 * half + 1] = pack_s8x4(lv[0], lv[1], lv[2], lv[3]);
+      const uint32_t ph = pack_s8x4(hv[0], hv[1], hv[2], hv[3]);
+      const uint32_t pl = pack_s8x4(lv[0], lv[1], lv[2], lv[3]);
+      const uint32_t p2 = pack_s8x4(l2[0], l2[1], l2[2], l2[3]);
+      if constexpr (WIDE) {
+        qi.a[ks][2 * half] = ph;
+        qi.a[ks][2 * half + 1] = pl;
+        qi.a2[ks][half] = p2;
+      } else {
+        qi.a[ks][2 * half] = second ? p2 : ph;
+        qi.a[ks][2 * half + 1] = second ? 0u : pl;
+      }
     }
   }
-  qi.c = sq * (p.sm_scale_log2 / 254.f);
+  qi.c = second ? 0.f : sq * (p.sm_scale_log2 / 64516.f);
 }
 
 __device__ __forceinline__ void mma_s8_16832(int* d, const uint32_t* a,
@@ -74,9 +93,13 @@ __device__ __forceinline__ void mma_s8_16832(int* d, const uint32_t* a,
 // INT8 QK scores of one page for query row g: K tile at stage (16 rows of
 // 128 bytes, 128B-swizzled by row) is the B operand straight from shared
 // memory (n-tile 0 = tokens 0-7, n-tile 1 = tokens 8-15); the accumulator
-// rows g / g+8 carry the hi / lo parts.  s[] = tokens 2t, 2t+1, 8+2t, 9+2t
-// in log2 units (masked tokens -inf).
-__device__ __forceinline__ void qk_int8(const uint8_t* stage, const QInt8& qi,
+// rows g / g+8 carry the hi / lo parts and the lo2 part comes from lane
+// g+4 (GQA <= 4) or from the second mma (WIDE).  s[] = tokens 2t, 2t+1,
+// 8+2t, 9+2t in log2 units (masked tokens -inf); 0 on lanes that hold no
+// query row.  The int32 sums are exact; (hi*254 + lo) stays below 2^30 and
+// its FP32 product with 254 rounds at 2^-24 relative.
+template <bool WIDE>
+__device__ __forceinline__ void qk_int8(const uint8_t* stage, const QInt8<WIDE>& qi,
                                         float sk, int valid, int g, int t,
                                         float* s) {
   const uint32_t rg = g * 128;
@@ -96,11 +119,36 @@ __device__ __forceinline__ void qk_int8(const uint8_t* stage, const QInt8& qi,
   mma_s8_16832(c_hi, qi.a[2], kh1.x, kh1.y);
   mma_s8_16832(c_lo, qi.a[3], kg1.z, kg1.w);
   mma_s8_16832(c_hi, qi.a[3], kh1.z, kh1.w);
+  int x[4];  // lo2 products of tokens 2t, 2t+1, 8+2t, 9+2t
+  if constexpr (WIDE) {
+    int d_lo[4] = {0, 0, 0, 0}, d_hi[4] = {0, 0, 0, 0};
+    uint32_t a2[4];
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      a2[0] = qi.a2[ks][0];
+      a2[1] = 0u;
+      a2[2] = qi.a2[ks][1];
+      a2[3] = 0u;
+      const uint4& kg = ks < 2 ? kg0 : kg1;
+      const uint4& kh = ks < 2 ? kh0 : kh1;
+      mma_s8_16832(d_lo, a2, (ks & 1) ? kg.z : kg.x, (ks & 1) ? kg.w : kg.y);
+      mma_s8_16832(d_hi, a2, (ks & 1) ? kh.z : kh.x, (ks & 1) ? kh.w : kh.y);
+    }
+    x[0] = d_lo[0];
+    x[1] = d_lo[1];
+    x[2] = d_hi[0];
+    x[3] = d_hi[1];
+  } else {
+    x[0] = __shfl_down_sync(0xffffffffu, c_lo[0], 16);
+    x[1] = __shfl_down_sync(0xffffffffu, c_lo[1], 16);
+    x[2] = __shfl_down_sync(0xffffffffu, c_hi[0], 16);
+    x[3] = __shfl_down_sync(0xffffffffu, c_hi[1], 16);
+  }
   const float e = qi.c * sk;
-  s[0] = static_cast<float>(c_lo[0] * 254 + c_lo[2]) * e;
-  s[1] = static_cast<float>(c_lo[1] * 254 + c_lo[3]) * e;
-  s[2] = static_cast<float>(c_hi[0] * 254 + c_hi[2]) * e;
-  s[3] = static_cast<float>(c_hi[1] * 254 + c_hi[3]) * e;
+  s[0] = fmaf(static_cast<float>(c_lo[0] * 254 + c_lo[2]), 254.f, static_cast<float>(x[0])) * e;
+  s[1] = fmaf(static_cast<float>(c_lo[1] * 254 + c_lo[3]), 254.f, static_cast<float>(x[1])) * e;
+  s[2] = fmaf(static_cast<float>(c_hi[0] * 254 + c_hi[2]), 254.f, static_cast<float>(x[2])) * e;
+  s[3] = fmaf(static_cast<float>(c_hi[1] * 254 + c_hi[3]), 254.f, static_cast<float>(x[3])) * e;
   if (valid < kPage) {
     if (2 * t >= valid) s[0] = kNegInf;
     if (2 * t + 1 >= valid) s[1] = kNegInf;
@@ -189,10 +237,10 @@ __device__ __forceinline__ void pv_int8(WarpState& st, const uint8_t* stage,
 // NP INT8 pages at once: the pages' QK chains, softmax work and PV chains
 // are independent, which gives each warp the instruction-level parallelism
 // that a single page's dependency chain lacks.
-template <int NP>
+template <int NP, bool WIDE>
 __device__ __forceinline__ void pages_int8(WarpState& st,
                                            const uint8_t* const* stages,
-                                           const QInt8& qi, const float* sk,
+                                           const QInt8<WIDE>& qi, const float* sk,
                                            const float* r, const int* valid,
                                            int g, int t, const uint32_t* vaddr) {
   float s[4 * NP];
@@ -224,9 +272,10 @@ __device__ __forceinline__ void issue_pair_int8(const CUtensorMap* tk, const CUt
   }
 }
 
+template <bool WIDE>
 __device__ __forceinline__ bool run_warp_pages_int8(
     const DecodeParams& p, const CUtensorMap* tk, const CUtensorMap* tv,
-    WarpState& st, uint8_t* ring, uint64_t* bars, QInt8& qi, int r,
+    WarpState& st, uint8_t* ring, uint64_t* bars, QInt8<WIDE>& qi, int r,
     int h, int idx_begin, int n_pages, bool has_last, int warp, int W,
     int lane) {
   const int g = lane >> 2, t = lane & 3;
@@ -247,6 +296,10 @@ __device__ __forceinline__ bool run_warp_pages_int8(
     load_window_set<1>(p, sd, idx_begin, warp, W, n_w, h, 32, lane, win.id_b, win.sk_b,
                        win.sv_b);
 
+  // The page ids come from the plan.  With p.int8_after_wait the pages'
+  // codes and scales (written by an append that may still be running) are
+  // read only after the previous kernel in the stream has completed.
+  if (p.int8_after_wait) pdl_wait_primary();
   // Prologue: pairs 0 and 1 (pages 0-3).
 #pragma unroll
   for (int q = 0; q < 2; ++q) {
@@ -335,9 +388,9 @@ __device__ __forceinline__ bool run_warp_pages_int8(
         valid[0] = last_valid;
     }
     if (two)
-      pages_int8<2>(st, stg, qi, sk, rr, valid, g, t, vaddr);
+      pages_int8<2, WIDE>(st, stg, qi, sk, rr, valid, g, t, vaddr);
     else
-      pages_int8<1>(st, stg, qi, sk, rr, valid, g, t, vaddr);
+      pages_int8<1, WIDE>(st, stg, qi, sk, rr, valid, g, t, vaddr);
     __syncwarp();
     // Refill this pair slot with pair q + 2.
     const int nq = q + 2;

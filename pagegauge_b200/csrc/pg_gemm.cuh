@@ -642,7 +642,6 @@ __global__ void __launch_bounds__(kTpReduceThreads)
                                    __floats2half2_rn(d[2 * e], d[2 * e + 1]));
         xw[e] = *reinterpret_cast<const uint32_t*>(&s2);
       }
-      *reinterpret_cast<uint4*>(res) = x[c];
     } else {
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -658,6 +657,18 @@ __global__ void __launch_bounds__(kTpReduceThreads)
     }
   }
   if (!ok) record_error(p.error_flag, kDevWaitTimeout);
+  // A row whose tiles did not all arrive in time stores nothing: residual
+  // and out keep their contents, so a caller that reads the guard word can
+  // repeat the step.
+  if (!__syncthreads_and(ok)) return;
+  if (p.residual != nullptr) {
+#pragma unroll
+    for (int c = 0; c < kMaxChunks; ++c) {
+      const int col = (c * kTpReduceThreads + threadIdx.x) * 8;
+      if (col >= n) break;
+      *reinterpret_cast<uint4*>(p.residual + b * p.residual_stride + col) = x[c];
+    }
+  }
   float inv = 1.f;
   if (p.norm_w != nullptr) {
 #pragma unroll

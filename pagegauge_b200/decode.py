@@ -74,14 +74,20 @@ class PageGaugeDecode:
             exact_key, exact_value, value_center: torch.Tensor | None,
             out: torch.Tensor | None = None, lse: torch.Tensor | None = None,
             sm_scale: float | None = None, fused_merge: bool = False,
-            cluster: int = 0, affine_bias=None) -> torch.Tensor:
+            cluster: int = 0, affine_bias=None, int8_after_wait: bool = False) -> torch.Tensor:
         """``cluster`` = 2..8 runs the decode as one launch whose CTAs merge
         in thread-block clusters (the single-launch ABI of the reference's
         heterogeneous path); ``fused_merge`` merges in the last CTA of each
         head; otherwise a merge kernel follows the split kernel.
         ``affine_bias = (k_bias, v_bias)`` selects the affine_group16
         representation for the INT8 pages: key/value_scales and the biases
-        are then [pages, Hkv, 8] (one pair per 16-dim group)."""
+        are then [pages, Hkv, 8] (one pair per 16-dim group).
+        ``int8_after_wait`` must be set when an append launched just before
+        this decode may have closed a page that this decode reads as INT8 --
+        a one-page exact ring, where the page closed at one step is INT8 at
+        the next.  The INT8 tiles are then requested only after the previous
+        kernel in the stream completes (otherwise they are requested while it
+        drains, because every kernel here lets its successor start early)."""
         plan = self.work_plan
         key = None
         if out is not None:
@@ -90,7 +96,7 @@ class PageGaugeDecode:
                    exact_key.data_ptr(), exact_key.shape, exact_value.data_ptr(),
                    None if value_center is None else (value_center.data_ptr(), value_center.shape),
                    out.data_ptr(), out.shape, out.stride(), None if lse is None else lse.data_ptr(),
-                   sm_scale, fused_merge, cluster, q.dtype, out.dtype,
+                   sm_scale, fused_merge, cluster, q.dtype, out.dtype, int8_after_wait,
                    None if affine_bias is None else (affine_bias[0].data_ptr(),
                                                      affine_bias[1].data_ptr()))
             if key == self._last_key:
@@ -121,7 +127,8 @@ class PageGaugeDecode:
                                      f"[pages,{self._num_kv_heads},8] float16")
         args = launch_decode(plan, q, segs, self.sm_scale if sm_scale is None else sm_scale, out,
                              lse, value_center=value_center, fused_merge=fused_merge,
-                             cluster=cluster, affine_bias=affine_bias)
+                             cluster=cluster, affine_bias=affine_bias,
+                             int8_after_wait=int8_after_wait)
         if key is not None:
             self._last_key, self._last_args = key, args
             self._last_args_ref = ctypes.byref(args)

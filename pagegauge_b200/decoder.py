@@ -560,8 +560,11 @@ class PageGaugeDecoder:
                 q, k, v, self.cos, self.sin, self.positions, c.key_center, c.value_center,
                 self.rq, c.exact_key, c.exact_value, c.key_codes, c.value_codes, c.key_scales,
                 c.value_scales, self.fixed_pages)
+            # With a one-page ring the page this step's append closes is
+            # INT8 at the next step, whose decode must then wait for it.
             dec.run(self.rq, c.key_codes, c.value_codes, c.key_scales, c.value_scales,
-                    c.exact_key, c.exact_value, c.value_center, out=self.attn)
+                    c.exact_key, c.exact_value, c.value_center, out=self.attn,
+                    int8_after_wait=self.ring_pages == 1)
             if fused and tpx is not None:
                 # Row-parallel projections publish their tiles through peer
                 # memory; the next kernel sums the ranks' tiles into the

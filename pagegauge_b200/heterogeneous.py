@@ -87,7 +87,10 @@ class HeterogeneousDecodeWrapper:
         self._old_key = key
 
     def run(self, q, paged_kv_cache, k_page_scale, v_page_scale, exact_k_cache, exact_v_cache,
-            old_kv_len, value_center, sm_scale=None, out=None, lse=None, return_lse=False, **_ignored):
+            old_kv_len, value_center, sm_scale=None, out=None, lse=None, return_lse=False,
+            int8_after_wait=False, **_ignored):
+        """``int8_after_wait``: see PageGaugeDecode.run (a page closed by the
+        append just before this call is read here as INT8)."""
         if self._indptr_host is None:
             raise RuntimeError("plan() must be called before run()")
         if self._old_key is None:
@@ -100,7 +103,7 @@ class HeterogeneousDecodeWrapper:
         segs = (_segment(old_k, old_v, self._old_idx, self._full, k_page_scale, v_page_scale),
                 _segment(exact_k_cache, exact_v_cache, self._ex_idx, self._last))
         launch_decode(self._plan, q, segs, 1.0 / math.sqrt(DIM) if sm_scale is None else sm_scale,
-                      out, lse, value_center=value_center)
+                      out, lse, value_center=value_center, int8_after_wait=int8_after_wait)
         return (out, lse) if return_lse else out
 
 

@@ -596,6 +596,9 @@ class ServedPool:
                   self.positions.data_ptr(), self.token_slots.data_ptr(),
                   self.exact_slots.data_ptr(), self.center_rows.data_ptr(), cos.stride(0),
                   cos.shape[0], _stream(q))
+        # A one-page tail ring makes the page closed by this append INT8 at
+        # the next step: that decode must wait for the append to complete.
         return self.decoder.run(rotated_q, pool['key_codes'], pool['value_codes'],
                                 pool['key_scales'], pool['value_scales'], ek, ev,
-                                self.center_out, out=out, lse=lse)
+                                self.center_out, out=out, lse=lse,
+                                int8_after_wait=self.layout.policy.tail_pages == 1)

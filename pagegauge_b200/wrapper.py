@@ -150,9 +150,12 @@ def launch_decode(plan: PagedDecodePlan, q: torch.Tensor, segments, sm_scale: fl
                   out: torch.Tensor, lse: torch.Tensor | None, extra=None,
                   value_center: torch.Tensor | None = None, final_ok: bool = True,
                   fused_merge: bool = False, cluster: int = 0,
-                  affine_bias=None) -> "_lib.PgDecodeArgs":
+                  affine_bias=None, int8_after_wait: bool = False) -> "_lib.PgDecodeArgs":
     """Fill the C argument block and launch split decode (+ merge); returns
-    the argument block so a caller may relaunch it unchanged."""
+    the argument block so a caller may relaunch it unchanged.
+    ``int8_after_wait``: the INT8 pages may have been written by a kernel
+    launched just before (an append that closed a page of a one-page exact
+    ring), so the decode reads them only after that kernel completes."""
     if q.dtype != torch.float16 or q.dim() != 3 or q.stride(2) != 1:
         raise ValueError("q must be float16 [B,Hq,128] with a contiguous last dimension")
     a = _lib.PgDecodeArgs()
@@ -194,6 +197,7 @@ def launch_decode(plan: PagedDecodePlan, q: torch.Tensor, segments, sm_scale: fl
         a.representation = 1
         a.k_bias = affine_bias[0].data_ptr()
         a.v_bias = affine_bias[1].data_ptr()
+    a.int8_after_wait = 1 if int8_after_wait else 0
     _lib.check(_lib.load().pg_decode_run(ctypes.byref(a), _stream(q)))
     return a
 

@@ -58,3 +58,28 @@ def assert_close_decode(out, expected, atol=ATOL):
     cos = O.cosine(got, expected)
     assert err <= atol and cos >= MIN_COSINE, f"max-abs {err:.3e}, cosine {cos:.6f}"
     return err, cos
+
+
+def check_all_heads(q, cache, tables, out, lse, request, group, lse_rtol=0.0):
+    """Every KV head's query rows of ``request`` against the float64 oracle
+    (one head at a time, so long contexts stay small on the host):
+    outputs at the parity bar, base-2 LSE within 2e-4 (+ lse_rtol)."""
+    ck, cv = cpu(cache.key_codes), cpu(cache.value_codes)
+    sk, sv = cpu(cache.key_scales), cpu(cache.value_scales)
+    ek, ev = cpu(cache.exact_key), cpu(cache.exact_value)
+    o_ptr, e_ptr = cpu(tables.old_indptr), cpu(tables.exact_indptr)
+    old_ids = cpu(tables.old_indices)[o_ptr[request]:o_ptr[request + 1]]
+    ex_ids = cpu(tables.exact_indices)[e_ptr[request]:e_ptr[request + 1]]
+    worst = 0.0
+    for h in range(ck.shape[2]):
+        hs = slice(h, h + 1)
+        rows = slice(group * h, group * h + group)
+        exp, exp_lse = O.page_gauge_decode(
+            cpu(q[request, rows]), ck[:, :, hs], cv[:, :, hs], sk[:, hs], sv[:, hs], old_ids,
+            tables.old_tokens[request], ek[:, :, hs], ev[:, :, hs], ex_ids,
+            tables.exact_tokens[request], cpu(cache.value_center[request, hs]), 128 ** -0.5)
+        err, _ = assert_close_decode(out[request, rows], exp)
+        worst = max(worst, err)
+        if lse is not None:
+            np.testing.assert_allclose(cpu(lse[request, rows]), exp_lse, atol=2e-4, rtol=lse_rtol)
+    return worst

@@ -83,10 +83,11 @@ def test_decoder_prefill_and_decode_match_oracle(cuda_lib, batch, prompt_len, ge
     assert read_device_error() == 0
 
 
-@pytest.mark.parametrize("sink,suffix,ring", [(1, 2, 4), (4, 0, 6)])
+@pytest.mark.parametrize("sink,suffix,ring", [(1, 2, 4), (4, 0, 6), (0, 0, 1)])
 def test_decoder_exact_page_policies_match_oracle(cuda_lib, sink, suffix, ring):
     """Exact prefix (sink) pages, a static exact suffix of the prompt and a
-    tail ring of `ring` pages (the paper's S/A/T policies)."""
+    tail ring of `ring` pages (the paper's S/A/T policies); ring 1 makes the
+    page an append closes INT8 at the very next step."""
     batch, prompt_len = 2, 256
     weights = random_decoder_weights(CFG, SEED, device="cuda", gen_device="cpu")
     dec = PageGaugeDecoder(weights, batch=batch, max_context=512, ring_pages=ring,

@@ -90,3 +90,31 @@ def test_static_scratch_rejects_plans_beyond_its_maximum(cuda_lib):
                                       torch.cuda.current_stream().cuda_stream)
     assert rc == 1
     assert b"at most" in _lib.load().pg_last_error()
+
+
+def test_static_scratch_refuses_a_capturing_stream(cuda_lib):
+    """Each call copies its plan from host memory, which a stream capture
+    cannot record: the call is refused before anything is enqueued, and the
+    caller's capture stays usable."""
+    q, dk, dv, cache, tables = make_case([1024], seed=37)
+    dec = PageGaugeDecode(torch.empty(8 << 20, dtype=torch.uint8, device="cuda"))
+    dec.plan(tables.old_indptr, tables.old_indices, tables.exact_indptr, tables.exact_indices,
+             tables.exact_last_page_len, 32, 8)
+    out = torch.empty_like(q)
+    lse = torch.empty(1, 32, device="cuda", dtype=torch.float32)
+    a = _args(q, cache, tables, dec, out, lse)
+    ind0 = host_indptr(tables.old_indptr)
+    ind1 = host_indptr(tables.exact_indptr)
+    lib = _lib.load()
+    x = torch.zeros(16, device="cuda")
+    stream = torch.cuda.Stream()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        rc = lib.pg_decode_static(ctypes.byref(a), ind0.ctypes.data, ind1.ctypes.data, 0, 0,
+                                  num_sms(q.device), stream.cuda_stream)
+        x.add_(1)
+    assert rc == 1
+    assert b"being captured" in lib.pg_last_error()
+    graph.replay()
+    torch.cuda.synchronize()
+    assert float(x[0]) == 1.0
