@@ -35,7 +35,6 @@ ages out of the tail ring already has its codes in the pool; the aged pages
 
 from __future__ import annotations
 
-import heapq
 import math
 from dataclasses import dataclass
 
@@ -50,71 +49,118 @@ PAGE = 16
 # ----------------------------------------------------------------- policy
 @dataclass(frozen=True)
 class Policy:
-    """S/A/T page policy: ``prefix_pages`` exact pages at the start,
-    ``suffix_pages`` exact pages that ended the prompt, and a tail ring of
-    ``tail_pages`` (partition.py:7-18)."""
+    """Exact-page policy of a served request: ``prefix_pages`` pages from
+    the start of the context, the ``suffix_pages`` pages that close the
+    prompt, and a ring over the last ``tail_pages`` pages stay FP16; the
+    rest of the completed pages are read as INT8 (partition.py:7-18)."""
     prefix_pages: int = 4
     suffix_pages: int = 128
     tail_pages: int = 48
 
     def __post_init__(self):
-        values = (self.prefix_pages, self.suffix_pages, self.tail_pages)
-        if (any(type(v) is not int for v in values) or self.prefix_pages < 0
-                or self.suffix_pages < 0 or self.tail_pages < 1):
+        counts = (self.prefix_pages, self.suffix_pages, self.tail_pages)
+        if not all(type(c) is int for c in counts) or min(counts) < 0 or self.tail_pages == 0:
             raise ValueError('Invalid page policy')
 
     @property
     def storage_pages(self) -> int:
+        """Sidecar pages one lease holds: prefix, suffix, then the ring."""
         return self.prefix_pages + self.suffix_pages + self.tail_pages
+
+    def regions(self, prompt_pages: int, pages: int) -> tuple:
+        """The three exact regions as half-open [begin, end) page ranges
+        (prefix, prompt suffix, tail), in that order."""
+        return ((0, self.prefix_pages), (prompt_pages - self.suffix_pages, prompt_pages),
+                (pages - self.tail_pages, pages))
+
+    def ring_base(self) -> int:
+        return self.prefix_pages + self.suffix_pages
+
+
+def _covered(runs) -> list:
+    """Union of half-open page ranges as sorted, disjoint ranges."""
+    out: list = []
+    for b, e in sorted(r for r in runs if r[0] < r[1]):
+        if out and b <= out[-1][1]:
+            out[-1] = (out[-1][0], max(out[-1][1], e))
+        else:
+            out.append((b, e))
+    return out
 
 
 def partition(prompt_tokens, current_tokens, policy: Policy = Policy()) -> dict:
-    """Logical pages of a request with ``current_tokens`` tokens split into
-    exact (prefix, suffix, tail) and history (INT8) pages
-    (partition.py:21-40).  The partial last prompt page belongs to the tail."""
+    """Split the logical pages of a request at ``current_tokens`` tokens into
+    its exact pages (prefix, prompt suffix, tail) and its history pages,
+    read as INT8 (partition.py:21-40).  The partial last page is always in
+    the tail.  Returns the regions, the exact and history page tuples and
+    the token counts of each side."""
     if (type(prompt_tokens) is not int or type(current_tokens) is not int
-            or not 0 < prompt_tokens <= current_tokens):
+            or prompt_tokens <= 0 or current_tokens < prompt_tokens):
         raise ValueError('Invalid prompt/current length')
-    initial = prompt_tokens // PAGE
+    prompt_pages = prompt_tokens // PAGE
     pages = -(-current_tokens // PAGE)
-    if (initial < policy.prefix_pages + policy.suffix_pages
+    # The prefix and suffix need a prompt that holds them, and at least one
+    # page must lie between the prefix and the tail.
+    if (prompt_pages < policy.prefix_pages + policy.suffix_pages
             or pages - policy.tail_pages <= policy.prefix_pages):
         raise ValueError('Prompt cannot support this policy; explicit FP16 fallback required')
-    prefix = range(policy.prefix_pages)
-    suffix = range(initial - policy.suffix_pages, initial)
-    tail = range(pages - policy.tail_pages, pages)
-    exact = sorted(set(prefix) | set(suffix) | set(tail))
-    exact_set = set(exact)
-    history = tuple(p for p in range(pages) if p not in exact_set)
+    prefix, suffix, tail = (tuple(range(b, e)) for b, e in policy.regions(prompt_pages, pages))
+    exact_runs = _covered(policy.regions(prompt_pages, pages))
+    exact, history, cursor = [], [], 0
+    for b, e in exact_runs:
+        history.extend(range(cursor, b))
+        exact.extend(range(b, e))
+        cursor = e
+    history.extend(range(cursor, pages))
     if not history or history[-1] == pages - 1:
         raise ValueError('No historical page or partial last page incorrectly quantized')
-    return {'prefix': tuple(prefix), 'suffix': tuple(suffix), 'tail': tuple(tail),
-            'exact': tuple(exact), 'history': history,
+    return {'prefix': prefix, 'suffix': suffix, 'tail': tail,
+            'exact': tuple(exact), 'history': tuple(history),
             'history_tokens': PAGE * len(history),
             'exact_tokens': current_tokens - PAGE * len(history),
-            'tail_tokens': (policy.tail_pages - 1) * PAGE + (current_tokens - 1) % PAGE + 1}
+            'tail_tokens': current_tokens - PAGE * (pages - policy.tail_pages)}
 
 
 def exact_slot(logical_page, prompt_tokens, lease_slot, policy: Policy = Policy()) -> int:
-    """Sidecar page of an exact logical page: prefix pages in order, then the
-    suffix pages, then the tail ring slot ``page % tail_pages``
+    """Sidecar page of an exact logical page: the lease's block of
+    ``storage_pages`` sidecar pages holds the prefix pages, then the prompt
+    suffix pages, then the ring slot ``page % tail_pages``
     (partition.py:43-52)."""
-    initial = prompt_tokens // PAGE
-    if min(logical_page, lease_slot) < 0:
+    if logical_page < 0 or lease_slot < 0:
         raise ValueError('Negative page/lease slot')
+    prompt_pages = prompt_tokens // PAGE
+    suffix_begin = prompt_pages - policy.suffix_pages
     if logical_page < policy.prefix_pages:
-        local = logical_page
-    elif initial - policy.suffix_pages <= logical_page < initial:
-        local = policy.prefix_pages + logical_page - (initial - policy.suffix_pages)
+        within = logical_page
+    elif suffix_begin <= logical_page < prompt_pages:
+        within = policy.prefix_pages + (logical_page - suffix_begin)
     else:
-        local = policy.prefix_pages + policy.suffix_pages + logical_page % policy.tail_pages
-    return lease_slot * policy.storage_pages + local
+        within = policy.ring_base() + logical_page % policy.tail_pages
+    return lease_slot * policy.storage_pages + within
+
+
+def _aging(policy: Policy, prompt_tokens: int, tokens: int) -> tuple:
+    """History pages gained when a request grows from ``tokens`` to
+    ``tokens + 1`` tokens: when the new token opens a page, the ring's
+    oldest page leaves the tail, and it turns INT8 unless the prefix or the
+    prompt suffix keeps it exact."""
+    if tokens % PAGE:
+        return ()
+    leaving = tokens // PAGE - policy.tail_pages  # the ring now starts one page later
+    if leaving < 0:
+        return ()
+    (p0, p1), (s0, s1), _ = policy.regions(prompt_tokens // PAGE, tokens // PAGE + 1)
+    return () if p0 <= leaving < p1 or s0 <= leaving < s1 else (leaving,)
 
 
 # ---------------------------------------------------------------- layout
 @dataclass(frozen=True)
 class Layout:
-    """Served pool geometry and its capacity accounting (cache_layout.py)."""
+    """Geometry of a served cache -- the persistent code pool (per layer:
+    K/V codes and K/V page scales of ``physical_pages`` pages) and the
+    per-lease sidecars (exact pages, key/value/output centres) of
+    ``maximum_requests`` admissible requests -- and its byte accounting
+    (cache_layout.py:6-38)."""
     layers: int
     physical_pages: int
     maximum_requests: int
@@ -124,124 +170,119 @@ class Layout:
     policy: Policy = Policy()
 
     def __post_init__(self):
-        geometry = (self.layers, self.physical_pages, self.maximum_requests, self.kv_heads,
-                    self.query_heads, self.head_dim)
-        if (any(type(v) is not int or v < 1 for v in geometry)
-                or self.query_heads % self.kv_heads):
+        dims = (self.layers, self.physical_pages, self.maximum_requests, self.kv_heads,
+                self.query_heads, self.head_dim)
+        if not all(type(d) is int and d >= 1 for d in dims) or self.query_heads % self.kv_heads:
             raise ValueError('Invalid cache geometry')
 
-    def accounting(self) -> dict:
+    def planes(self) -> dict:
+        """name -> (shape, bytes per element) of every served tensor; the
+        first four form the pool, the rest the sidecars."""
         L, N, R = self.layers, self.physical_pages, self.maximum_requests
         H, Q, D = self.kv_heads, self.query_heads, self.head_dim
-        codes = L * N * PAGE * H * D
-        exact = 2 * L * R * self.policy.storage_pages * PAGE * H * D
-        tensors = {'key_codes': codes, 'value_codes': codes,
-                   'key_scales': 2 * L * N * H, 'value_scales': 2 * L * N * H,
-                   'exact_key': exact, 'exact_value': exact,
-                   'key_center': 2 * L * R * H * D, 'value_center': 2 * L * R * H * D,
-                   'output_center': 2 * L * R * Q * D}
-        pool = sum(tensors[k] for k in ('key_codes', 'value_codes', 'key_scales', 'value_scales'))
-        total = sum(tensors.values())
-        return {'tensors': tensors, 'page_pool_bytes': pool,
+        exact = (L, R * self.policy.storage_pages, PAGE, H, D)
+        return {'key_codes': ((L, N, PAGE, H, D), 1), 'value_codes': ((L, N, PAGE, H, D), 1),
+                'key_scales': ((L, N, H), 2), 'value_scales': ((L, N, H), 2),
+                'exact_key': (exact, 2), 'exact_value': (exact, 2),
+                'key_center': ((L, R, H, D), 2), 'value_center': ((L, R, H, D), 2),
+                'output_center': ((L, R, Q, D), 2)}
+
+    def accounting(self) -> dict:
+        sizes = {name: math.prod(shape) * width for name, (shape, width) in self.planes().items()}
+        pool = sum(sizes[n] for n in POOL_PLANES)
+        total = sum(sizes.values())
+        return {'tensors': sizes, 'page_pool_bytes': pool,
                 'reserved_sidecar_bytes': total - pool,
                 'total_served_capacity_bytes': total,
-                'per_layer_page_bytes': 2 * PAGE * H * D + 4 * H,
-                'scope': ('Declared persistent code/metadata pool and all admitted-request '
-                          'sidecar slots, including empty reserved slots. Excludes weights, '
-                          'workspace, graph pools, input/output buffers and allocator padding; '
-                          'those must be separately reserved/measured before admission.')}
+                'per_layer_page_bytes': 2 * PAGE * self.kv_heads * self.head_dim
+                                        + 2 * 2 * self.kv_heads,
+                'scope': 'code pool planes plus the sidecars of every admissible lease, used '
+                         'or not; model weights, decode workspace, CUDA graph pools, batch '
+                         'buffers and allocator slack are budgeted separately'}
 
     def admissible_pages(self, cache_budget_bytes) -> int:
-        """Physical pages a cache-only byte budget holds after every
-        reserved sidecar (cache_layout.py:33-38)."""
+        """Pool pages a cache-only byte budget holds once every lease's
+        sidecars are reserved (cache_layout.py:33-38)."""
         acc = self.accounting()
-        remaining = cache_budget_bytes - acc['reserved_sidecar_bytes']
-        if remaining < 0:
+        left = cache_budget_bytes - acc['reserved_sidecar_bytes']
+        if left < 0:
             raise MemoryError('Budget cannot hold reserved exact/center sidecars')
-        return remaining // (self.layers * acc['per_layer_page_bytes'])
+        return left // (self.layers * acc['per_layer_page_bytes'])
 
     @classmethod
     def for_budget(cls, layers: int, maximum_requests: int, cache_budget_bytes: int,
                    **kw) -> "Layout":
         """The largest pool a cache-only budget admits (e.g. a B200's HBM
         minus weights, workspace and graph pools)."""
-        probe = cls(layers, 1, maximum_requests, **kw)
-        pages = probe.admissible_pages(cache_budget_bytes)
+        pages = cls(layers, 1, maximum_requests, **kw).admissible_pages(cache_budget_bytes)
         if pages < 1:
             raise MemoryError('Budget cannot hold reserved exact/center sidecars')
         return cls(layers, int(pages), maximum_requests, **kw)
 
 
+POOL_PLANES = ('key_codes', 'value_codes', 'key_scales', 'value_scales')
+
+
 # ----------------------------------------------------------------- views
 def dense_pool_views(raw: torch.Tensor, physical_pages, kv_heads, head_dim=128) -> dict:
-    """Split one layer's raw uint8 allocation into the K codes, V codes, K
-    scales and V scales planes, without a copy (cache_views.py:9-24)."""
-    if any(type(x) is not int or x < 1 for x in (physical_pages, kv_heads, head_dim)):
+    """One layer's raw uint8 pool allocation as the four planes the kernels
+    read -- K codes, V codes [pages, 16, Hkv, D] int8, K scales, V scales
+    [pages, Hkv] fp16 -- back to back, no copy (cache_views.py:9-24)."""
+    if not all(type(x) is int and x >= 1 for x in (physical_pages, kv_heads, head_dim)):
         raise ValueError('Positive integer pool geometry required')
-    codes = physical_pages * PAGE * kv_heads * head_dim
-    scales = physical_pages * kv_heads * 2
+    specs = (('key_codes', torch.int8, (physical_pages, PAGE, kv_heads, head_dim)),
+             ('value_codes', torch.int8, (physical_pages, PAGE, kv_heads, head_dim)),
+             ('key_scales', torch.float16, (physical_pages, kv_heads)),
+             ('value_scales', torch.float16, (physical_pages, kv_heads)))
+    widths = [math.prod(shape) * torch.empty(0, dtype=dt).element_size() for _, dt, shape in specs]
     if (raw.dtype != torch.uint8 or raw.ndim != 1 or not raw.is_contiguous()
-            or raw.numel() != 2 * codes + 2 * scales or raw.data_ptr() % 16):
+            or raw.numel() != sum(widths) or raw.data_ptr() % 16):
         raise ValueError('Aligned contiguous uint8 layer allocation of exact size required')
-    return {
-        'key_codes': raw[:codes].view(torch.int8).view(physical_pages, PAGE, kv_heads, head_dim),
-        'value_codes': raw[codes:2 * codes].view(torch.int8).view(physical_pages, PAGE, kv_heads,
-                                                                   head_dim),
-        'key_scales': raw[2 * codes:2 * codes + scales].view(torch.float16).view(physical_pages,
-                                                                                 kv_heads),
-        'value_scales': raw[2 * codes + scales:].view(torch.float16).view(physical_pages,
-                                                                          kv_heads),
-    }
+    views, at = {}, 0
+    for (name, dt, shape), width in zip(specs, widths):
+        views[name] = raw[at:at + width].view(dt).view(shape)
+        at += width
+    return views
 
 
 def from_engine_layer(layer: torch.Tensor, physical_pages, kv_heads) -> dict:
-    """Reinterpret a compact packed engine layer [pages, Hkv, 1, 2*16*128+4]
-    uint8 as pool planes, no copy (cache_views.py:27-39)."""
-    expected = (physical_pages, kv_heads, 1, 2 * PAGE * 128 + 4)
-    if layer.dtype != torch.uint8 or tuple(layer.shape) != expected or not layer.is_contiguous():
+    """An engine's packed layer [pages, Hkv, 1, 2*16*128+4] uint8 read as
+    the same four planes, without a copy (cache_views.py:27-39)."""
+    if (layer.dtype != torch.uint8 or not layer.is_contiguous()
+            or tuple(layer.shape) != (physical_pages, kv_heads, 1, 2 * PAGE * 128 + 4)):
         raise ValueError('Compact packed engine layer required; copying is forbidden')
     return dense_pool_views(layer.view(-1), physical_pages, kv_heads)
 
 
 def zero_physical_pages(views: dict, page_ids) -> None:
-    """Zero the four planes of the given pool pages on the current stream,
-    one kernel launch (cache_views.py:42-62)."""
-    names = ('key_codes', 'value_codes', 'key_scales', 'value_scales')
-    tensors = [views[n] for n in names]
-    first = tensors[0]
+    """Zero the given pool pages in all four planes, one kernel launch on
+    the current stream (cache_views.py:42-62)."""
+    planes = [views[n] for n in POOL_PLANES]
+    count = planes[0].shape[0]
     pages = tuple(page_ids)
-    if (any(t.device != first.device or t.shape[0] != first.shape[0] for t in tensors)
-            or any(type(p) is not int or not 0 <= p < first.shape[0] for p in pages)
-            or len(set(pages)) != len(pages)):
+    consistent = all(t.device == planes[0].device and t.shape[0] == count for t in planes)
+    valid = all(type(p) is int and 0 <= p < count for p in pages) and len(set(pages)) == len(pages)
+    if not (consistent and valid):
         raise ValueError('Invalid physical pages or inconsistent pool views')
     if not pages:
         return
-    if not first.is_cuda:
+    if not planes[0].is_cuda:
         raise ValueError('pool views must be CUDA tensors')
-    ids = torch.tensor(pages, dtype=torch.int32).to(first.device, non_blocking=True)
-    _lib.call('pg_zero_pool_pages', first.data_ptr(), tensors[1].data_ptr(),
-              tensors[2].data_ptr(), tensors[3].data_ptr(), first.shape[0], first.shape[2],
-              ids.data_ptr(), len(pages), torch.cuda.current_stream(first.device).cuda_stream)
+    ids = torch.tensor(pages, dtype=torch.int32).to(planes[0].device, non_blocking=True)
+    _lib.call('pg_zero_pool_pages', *(t.data_ptr() for t in planes), count,
+              planes[0].shape[2], ids.data_ptr(), len(pages),
+              torch.cuda.current_stream(planes[0].device).cuda_stream)
 
 
 def allocate_sidecars(layout: Layout, *, device, cache_budget_bytes) -> dict:
-    """Exact pages and centres reserved for every admissible request
-    (sidecars.py:10-35)."""
+    """Zeroed sidecar tensors for every admissible lease, shaped by the
+    layout's plane table (sidecars.py:10-35)."""
     if type(cache_budget_bytes) is not int or cache_budget_bytes < 0:
         raise ValueError('Nonnegative integer cache-only byte budget required')
-    acc = layout.accounting()
-    if acc['total_served_capacity_bytes'] > cache_budget_bytes:
+    if layout.accounting()['total_served_capacity_bytes'] > cache_budget_bytes:
         raise MemoryError('Code pool plus all reserved sidecars exceed cache budget')
-    L, R, H, D = layout.layers, layout.maximum_requests, layout.kv_heads, layout.head_dim
-    exact = (L, R * layout.policy.storage_pages, PAGE, H, D)
-    shapes = {'exact_key': exact, 'exact_value': exact, 'key_center': (L, R, H, D),
-              'value_center': (L, R, H, D), 'output_center': (L, R, layout.query_heads, D)}
-    out = {name: torch.zeros(shape, dtype=torch.float16, device=device)
-           for name, shape in shapes.items()}
-    for name, t in out.items():
-        if t.numel() * t.element_size() != acc['tensors'][name]:
-            raise RuntimeError('Sidecar allocation differs from declared accounting')
-    return out
+    return {name: torch.zeros(shape, dtype=torch.float16, device=device)
+            for name, (shape, _) in layout.planes().items() if name not in POOL_PLANES}
 
 
 # ------------------------------------------------------- request lifetimes
@@ -260,90 +301,105 @@ class State:
     physical_pages: tuple
 
 
+def _block_table(physical_pages, count: int) -> tuple:
+    """A request's physical pages: exactly ``count`` distinct non-negative
+    integers."""
+    pages = tuple(physical_pages)
+    if (len(pages) != count or len(set(pages)) != count
+            or not all(type(p) is int and p >= 0 for p in pages)):
+        raise ValueError('Wrong/duplicate physical block table')
+    return pages
+
+
 class RequestSlots:
-    """Fixed admission capacity of sidecar slots; a request holds a lease
-    (slot + generation) and owns its physical pages until released
-    (request_slots.py:20-93)."""
+    """Admission control of the served cache: ``maximum_requests`` sidecar
+    slots, each lent to one live request at a time under a generation
+    count, and the ownership of every physical pool page a live request
+    holds (request_slots.py:20-93).  Slots are handed out lowest first."""
 
     def __init__(self, maximum_requests, policy: Policy = Policy()):
         if type(maximum_requests) is not int or maximum_requests < 1:
             raise ValueError('Positive fixed admission capacity required')
         self.policy = policy
-        self.free = list(range(maximum_requests))
+        self._occupied = [False] * maximum_requests
         self.generations = [0] * maximum_requests
         self.states: dict[str, State] = {}
         self.page_owner: dict[int, Lease] = {}
 
-    def _pages(self, physical_pages, count) -> tuple:
-        pages = tuple(physical_pages)
-        if (len(pages) != count or len(set(pages)) != count
-                or any(type(p) is not int or p < 0 for p in pages)):
-            raise ValueError('Wrong/duplicate physical block table')
-        return pages
+    @property
+    def free(self) -> list:
+        """Slots no live request holds, ascending."""
+        return [i for i, used in enumerate(self._occupied) if not used]
+
+    def _claim(self, pages, lease: Lease) -> None:
+        for p in pages:
+            self.page_owner[p] = lease
 
     def admit(self, request_id, prompt_tokens, physical_pages) -> Lease:
         if not isinstance(request_id, str) or not request_id or request_id in self.states:
             raise ValueError('Invalid or duplicate live request ID')
-        partition(prompt_tokens, prompt_tokens, self.policy)
-        pages = self._pages(physical_pages, -(-prompt_tokens // PAGE))
+        partition(prompt_tokens, prompt_tokens, self.policy)  # the policy must fit the prompt
+        pages = _block_table(physical_pages, -(-prompt_tokens // PAGE))
         if any(p in self.page_owner for p in pages):
             raise ValueError('Cross-request page sharing is disabled')
-        if not self.free:
+        free = self.free
+        if not free:
             raise MemoryError('Declared exact-sidecar admission capacity reached')
-        slot = heapq.heappop(self.free)
+        slot = free[0]
+        self._occupied[slot] = True
         self.generations[slot] += 1
         lease = Lease(request_id, slot, self.generations[slot])
         self.states[request_id] = State(lease, prompt_tokens, prompt_tokens, pages)
-        for p in pages:
-            self.page_owner[p] = lease
+        self._claim(pages, lease)
         return lease
 
     def state(self, lease: Lease) -> State:
-        st = self.states.get(lease.request_id)
-        if st is None or st.lease != lease:
+        current = self.states.get(lease.request_id)
+        if current is None or current.lease != lease:
             raise ValueError('Stale request lease/center generation')
-        return st
+        return current
 
     def batch(self, request_ids) -> tuple:
-        ids = tuple(request_ids)
-        if len(set(ids)) != len(ids):
+        rows = tuple(request_ids)
+        if len(set(rows)) != len(rows):
             raise ValueError('Duplicate batch row')
-        try:
-            return tuple(self.states[i].lease for i in ids)
-        except KeyError as error:
-            raise ValueError('Unknown scheduled request') from error
+        missing = [r for r in rows if r not in self.states]
+        if missing:
+            raise ValueError('Unknown scheduled request')
+        return tuple(self.states[r].lease for r in rows)
 
     def append(self, lease: Lease, position, physical_pages) -> dict:
-        st = self.state(lease)
-        if position != st.current_tokens:
+        """Record the token at ``position`` (the request's next one) with the
+        request's block table after it; returns the page it closes, the
+        pages that turned INT8 and the new partition."""
+        current = self.state(lease)
+        if position != current.current_tokens:
             raise ValueError('Skipped/replayed token or wrong per-request position')
-        length = position + 1
-        pages = self._pages(physical_pages, -(-length // PAGE))
-        if pages[:len(st.physical_pages)] != st.physical_pages:
+        tokens = position + 1
+        pages = _block_table(physical_pages, -(-tokens // PAGE))
+        held = len(current.physical_pages)
+        if pages[:held] != current.physical_pages:
             raise ValueError('Preemption/remapping is not supported in phase one')
-        extra = pages[len(st.physical_pages):]
-        if any(p in self.page_owner for p in extra):
+        if any(p in self.page_owner for p in pages[held:]):
             raise ValueError('New physical page belongs to a live request')
-        before = partition(st.prompt_tokens, st.current_tokens, self.policy)
-        after = partition(st.prompt_tokens, length, self.policy)
-        aged = sorted(set(after['history']) - set(before['history']))
-        if any(p >= length // PAGE for p in aged):
+        after = partition(current.prompt_tokens, tokens, self.policy)
+        aged = _aging(self.policy, current.prompt_tokens, position)
+        if any(p >= tokens // PAGE for p in aged):
             raise ValueError('Attempt to consume an unfinished INT8 page')
-        for p in extra:
-            self.page_owner[p] = lease
-        self.states[lease.request_id] = State(lease, st.prompt_tokens, length, pages)
+        self._claim(pages[held:], lease)
+        self.states[lease.request_id] = State(lease, current.prompt_tokens, tokens, pages)
         return {'lease': lease, 'position': position,
-                'closed_page': position // PAGE if length % PAGE == 0 else None,
-                'new_history_pages': tuple(aged), 'partition': after}
+                'closed_page': position // PAGE if tokens % PAGE == 0 else None,
+                'new_history_pages': aged, 'partition': after}
 
     def release(self, lease: Lease) -> None:
-        st = self.state(lease)
-        if any(self.page_owner.get(p) != lease for p in st.physical_pages):
+        current = self.state(lease)
+        if any(self.page_owner.get(p) != lease for p in current.physical_pages):
             raise ValueError('Page ownership corrupted')
-        for p in st.physical_pages:
+        for p in current.physical_pages:
             del self.page_owner[p]
         del self.states[lease.request_id]
-        heapq.heappush(self.free, lease.slot)
+        self._occupied[lease.slot] = False
 
 
 # ------------------------------------------------------- decode metadata
@@ -365,8 +421,8 @@ class DecodeBatch:
     rows: tuple
 
     def columns(self) -> dict:
-        """Integer columns of the device ABI, in scheduled row order
-        (decode_metadata.py:28-35)."""
+        """The integer columns a device step consumes, one entry per row in
+        scheduled order (decode_metadata.py:28-35)."""
         return {'request_slots': tuple(r.lease.slot for r in self.rows),
                 'generations': tuple(r.lease.generation for r in self.rows),
                 'positions': tuple(r.position for r in self.rows),
@@ -374,50 +430,56 @@ class DecodeBatch:
                 'exact_token_slots': tuple(r.exact_token_slot for r in self.rows)}
 
 
+def _decode_row(manager: RequestSlots, lease: Lease, position, physical_pages,
+                taken: set) -> DecodeRow:
+    """One row of a decode batch, validated against the manager without
+    changing it; ``taken`` collects the physical pages the batch uses."""
+    current = manager.state(lease)
+    if type(position) is not int or position != current.current_tokens:
+        raise ValueError('Wrong next token position')
+    pages = _block_table(physical_pages, position // PAGE + 1)
+    held = len(current.physical_pages)
+    if pages[:held] != current.physical_pages:
+        raise ValueError('Physical remapping is unsupported')
+    if any(p in taken for p in pages[held:]):
+        raise ValueError('Physical page alias across batch')
+    taken.update(pages[held:])
+    partition(current.prompt_tokens, position + 1, manager.policy)
+    aged = _aging(manager.policy, current.prompt_tokens, position)
+    if any(p >= (position + 1) // PAGE for p in aged):
+        raise ValueError('Cannot quantize incomplete page')
+    page, token = divmod(position, PAGE)
+    slot_of = lambda lp: exact_slot(lp, current.prompt_tokens, lease.slot,  # noqa: E731
+                                    manager.policy)
+    return DecodeRow(lease, current, position, pages, pages[page] * PAGE + token,
+                     slot_of(page) * PAGE + token, aged, tuple(pages[p] for p in aged),
+                     tuple(slot_of(p) for p in aged))
+
+
 def prepare_decode(manager: RequestSlots, scheduled) -> DecodeBatch:
-    """Validate a batch of (lease, next position, full physical block table)
-    without mutating the manager (decode_metadata.py:38-62)."""
-    rows = []
-    ids = set()
-    allocated = set(manager.page_owner)
+    """Validate a batch of (lease, next position, full block table) rows and
+    derive its device metadata, changing nothing in the manager
+    (decode_metadata.py:38-62)."""
+    seen, taken, rows = set(), set(manager.page_owner), []
     for lease, position, physical_pages in scheduled:
-        st = manager.state(lease)
-        if lease.request_id in ids:
+        manager.state(lease)
+        if lease.request_id in seen:
             raise ValueError('Duplicate scheduled request')
-        ids.add(lease.request_id)
-        if type(position) is not int or position != st.current_tokens:
-            raise ValueError('Wrong next token position')
-        pages = manager._pages(physical_pages, (position + PAGE) // PAGE)
-        if pages[:len(st.physical_pages)] != st.physical_pages:
-            raise ValueError('Physical remapping is unsupported')
-        extra = pages[len(st.physical_pages):]
-        if any(p in allocated for p in extra):
-            raise ValueError('Physical page alias across batch')
-        allocated.update(extra)
-        before = partition(st.prompt_tokens, position, manager.policy)
-        after = partition(st.prompt_tokens, position + 1, manager.policy)
-        aged = tuple(sorted(set(after['history']) - set(before['history'])))
-        if any(p >= (position + 1) // PAGE for p in aged):
-            raise ValueError('Cannot quantize incomplete page')
-        page = position // PAGE
-        rows.append(DecodeRow(
-            lease, st, position, pages, pages[page] * PAGE + position % PAGE,
-            exact_slot(page, st.prompt_tokens, lease.slot, manager.policy) * PAGE
-            + position % PAGE,
-            aged, tuple(pages[p] for p in aged),
-            tuple(exact_slot(p, st.prompt_tokens, lease.slot, manager.policy) for p in aged)))
+        seen.add(lease.request_id)
+        rows.append(_decode_row(manager, lease, position, physical_pages, taken))
     return DecodeBatch(tuple(rows))
 
 
 def commit_decode(manager: RequestSlots, batch: DecodeBatch) -> tuple:
-    """Advance the manager after the batch's device work has completed
-    (decode_metadata.py:65-76)."""
+    """Advance the manager by a batch whose device work has completed.  Every
+    row must still describe its request's current state and re-derive to
+    the same metadata (decode_metadata.py:65-76)."""
+    if any(manager.state(r.lease) != r.expected_state for r in batch.rows):
+        raise ValueError('Decode batch is stale')
+    taken = set(manager.page_owner)
     for row in batch.rows:
-        if manager.state(row.lease) != row.expected_state:
-            raise ValueError('Decode batch is stale')
-    fresh = prepare_decode(manager, [(r.lease, r.position, r.physical_pages) for r in batch.rows])
-    if fresh != batch:
-        raise ValueError('Decode metadata was altered')
+        if _decode_row(manager, row.lease, row.position, row.physical_pages, taken) != row:
+            raise ValueError('Decode metadata was altered')
     return tuple(manager.append(r.lease, r.position, r.physical_pages) for r in batch.rows)
 
 
