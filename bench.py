@@ -146,6 +146,19 @@ def workload_config(args, world: int) -> dict:
     }
 
 
+def upload_graph(graph) -> None:
+    """Upload a captured CUDA graph to the device (cuGraphUpload) so that its
+    first replay -- which may be the timed one -- launches like any later
+    replay instead of paying the one-time upload."""
+    handle = graph.raw_cuda_graph_exec()
+    stream = torch.cuda.current_stream().cuda_stream
+    rc = ctypes.CDLL("libcuda.so.1").cuGraphUpload(ctypes.c_void_p(int(handle)),
+                                                    ctypes.c_void_p(stream))
+    if rc != 0:
+        raise RuntimeError(f"cuGraphUpload failed ({rc})")
+    torch.cuda.synchronize()
+
+
 class Dist:
     """Barrier / max / sum over ranks (no-ops for one process)."""
 
@@ -470,11 +483,13 @@ class AttentionBench:
         torch.cuda.synchronize()
 
     def _graph(self, n: int):
-        """A CUDA graph of n back-to-back steps cycling the layers from 0."""
+        """A CUDA graph of n back-to-back steps cycling the layers from 0,
+        uploaded to the device."""
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=self.stream):
             for i in range(n):
                 self.step(i % self.layers)
+        upload_graph(g)
         return g
 
     def prepare_steps(self, k: int) -> None:
@@ -1095,30 +1110,12 @@ def main() -> None:
     lengths, glob, shards = workload_lengths(args.workload, world, rank)
     clocks = ClockSampler(local)
     clocks.start()  # covers every measurement below
-    bench = AttentionBench(lengths, args.layers, args.split, args.merge == "fused",
-                           seed=SEED + 1000 * rank, warps=args.warps,
-                           cluster=args.cluster if args.merge == "cluster" else 0)
-    bench.capture()
-    ms = bench.time_steps(args.steps, args.warmup, dist)
-    total_bytes = dist.reduce(float(bench.nbytes), "sum")
-    value = total_bytes / (ms * 1e-3) / 1e9
-    kernel_ms = dist.reduce(bench.kernel_ms(args.steps), "max")
-    achieved = bench.nbytes / (kernel_ms * 1e-3) / 1e9
-    e2e = bench.e2e(max(10, args.steps // 4), dist)
-    e2e_ms = e2e["graph_ms"] if e2e["graph_ms"] is not None else e2e["eager_ms"]
-    e2e_mode = ("CUDA graph of the public-API step" if e2e["graph_ms"] is not None
-                else "eager public-API calls")
-    if e2e["zero_copy_equal"] and e2e["zero_copy_graph_ms"] < e2e_ms:
-        e2e_ms = e2e["zero_copy_graph_ms"]
-        e2e_mode = ("CUDA graph of the public-API step, inputs read and output written in "
-                    "pinned host memory by the kernels (zero copy)")
-    plan_info = {"split_pages": bench.plan.split_pages[0], "work_items": bench.plan.num_items,
-                 "launches_per_step": bench.launches_per_step}
-    del bench
-    torch.cuda.empty_cache()
-
+    secondary = not args.only and args.workload == "b1_49k"
     workloads = {}
-    if not args.only and args.workload == "b1_49k":
+    # The memory-bound secondary workloads run first: the headline's timed
+    # steps then find the GPU at its working clocks rather than ramping up
+    # from idle (a 20-step run lasts well under a millisecond).
+    if secondary:
         workloads["b8_ragged"] = measure_b8_sharded(args, dist, rank, peak)
         app = measure_append(dist)
         if world == 1:
@@ -1150,6 +1147,30 @@ def main() -> None:
         }
         del aff
         torch.cuda.empty_cache()
+
+    bench = AttentionBench(lengths, args.layers, args.split, args.merge == "fused",
+                           seed=SEED + 1000 * rank, warps=args.warps,
+                           cluster=args.cluster if args.merge == "cluster" else 0)
+    bench.capture()
+    ms = bench.time_steps(args.steps, args.warmup, dist)
+    total_bytes = dist.reduce(float(bench.nbytes), "sum")
+    value = total_bytes / (ms * 1e-3) / 1e9
+    kernel_ms = dist.reduce(bench.kernel_ms(args.steps), "max")
+    achieved = bench.nbytes / (kernel_ms * 1e-3) / 1e9
+    e2e = bench.e2e(max(10, args.steps // 4), dist)
+    e2e_ms = e2e["graph_ms"] if e2e["graph_ms"] is not None else e2e["eager_ms"]
+    e2e_mode = ("CUDA graph of the public-API step" if e2e["graph_ms"] is not None
+                else "eager public-API calls")
+    if e2e["zero_copy_equal"] and e2e["zero_copy_graph_ms"] < e2e_ms:
+        e2e_ms = e2e["zero_copy_graph_ms"]
+        e2e_mode = ("CUDA graph of the public-API step, inputs read and output written in "
+                    "pinned host memory by the kernels (zero copy)")
+    plan_info = {"split_pages": bench.plan.split_pages[0], "work_items": bench.plan.num_items,
+                 "launches_per_step": bench.launches_per_step}
+    del bench
+    torch.cuda.empty_cache()
+
+    if secondary:
         for b in (1, 32):
             d = measure_decoder(dist, b, steps=args.decoder_steps, gemm=args.decoder_gemm,
                                 policy=args.decoder_policy, tp_reduce=args.decoder_tp_reduce)

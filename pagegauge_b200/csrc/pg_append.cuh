@@ -14,9 +14,12 @@
 // that are not rounded to FP16, the same scale rule, and a selectable
 // rounding mode (half away from zero, or half to even as torch.round).
 //
-// Layout: one CTA per (request, KV head), 64 threads; thread j owns the
-// dimension pair (2j, 2j+1), so every global access is a 4-byte half2 and a
-// 64-thread row is one coalesced 256-byte (FP16) / 128-byte (INT8) line.
+// Layout: one CTA of 256 threads per (request, KV head).  For the append,
+// thread (g, j) = (t / 64, t % 64) owns the dimension pair (2j, 2j+1) of
+// one query head (g) and of the key (g = 0) or value (g = 1), so every
+// access is a 4-byte half2 and 64 threads cover one coalesced 256-byte FP16
+// row; for the page close, thread t owns 8 dimensions (16 bytes) of token
+// t / 16 of the page.
 #pragma once
 
 #include "pg_common.cuh"
@@ -319,10 +322,10 @@ __global__ void __launch_bounds__(kAppendThreads)
       record_error(p.error_flag, kDevBadPosition);
     return;
   }
-  const uint32_t c = reinterpret_cast<const uint32_t*>(cosr)[j];
-  const uint32_t s = reinterpret_cast<const uint32_t*>(sinr)[j];
-  rotate_query_heads(p, r, h, g, j, in, c, s);
-
+  // Everything the position decides is requested before any store: the
+  // RoPE row and, when this token closes the page, the page's 15 older
+  // tokens from the ring (stores before them would keep the compiler from
+  // issuing those loads early, since it cannot rule out aliasing).
   const int page = static_cast<int>(pos / kPage);
   const int token = static_cast<int>(pos % kPage);
   int64_t ring_page, code_page;
@@ -335,9 +338,6 @@ __global__ void __launch_bounds__(kAppendThreads)
     }
     ring_page = es >> 4;
     code_page = ts >> 4;
-    if (g == 1)
-      reinterpret_cast<uint32_t*>(p.center_out +
-                                  (static_cast<int64_t>(r) * p.hkv + h) * kHeadDim)[j] = center;
   } else {
     const int sink = static_cast<int>(p.exact_sink_pages);
     const int tail_pages = static_cast<int>(p.exact_pages_per_request) - sink;
@@ -357,6 +357,14 @@ __global__ void __launch_bounds__(kAppendThreads)
     kx = *reinterpret_cast<const uint4*>(kring + tk * row_stride + col);
     vx = *reinterpret_cast<const uint4*>(vring + tk * row_stride + col);
   }
+  const uint32_t c = reinterpret_cast<const uint32_t*>(cosr)[j];
+  const uint32_t s = reinterpret_cast<const uint32_t*>(sinr)[j];
+  if constexpr (SERVED) {
+    if (g == 1)
+      reinterpret_cast<uint32_t*>(p.center_out +
+                                  (static_cast<int64_t>(r) * p.hkv + h) * kHeadDim)[j] = center;
+  }
+  rotate_query_heads(p, r, h, g, j, in, c, s);
   if (g < 2) {
     const uint32_t val = g == 0 ? center_pair(rope_apply(in.x, in.partner, j, c, s), center)
                                 : center_pair(in.x, center);

@@ -93,7 +93,8 @@ class PageGaugeDecode:
         if out is not None:
             key = (q.data_ptr(), q.shape, q.stride(), key_codes.data_ptr(), key_codes.shape,
                    value_codes.data_ptr(), key_scales.data_ptr(), value_scales.data_ptr(),
-                   exact_key.data_ptr(), exact_key.shape, exact_value.data_ptr(),
+                   None if exact_key is None else (exact_key.data_ptr(), exact_key.shape,
+                                                   exact_value.data_ptr()),
                    None if value_center is None else (value_center.data_ptr(), value_center.shape),
                    out.data_ptr(), out.shape, out.stride(), None if lse is None else lse.data_ptr(),
                    sm_scale, fused_merge, cluster, q.dtype, out.dtype, int8_after_wait,
