@@ -422,7 +422,8 @@ __global__ void __maxnreg__(168)
   if (seg == 0) {
     if constexpr (REP == kRepGauge) {
       QInt8<WIDE> qi;
-      ok = run_warp_pages_int8<WIDE>(p, &tm_k8, &tm_v8, st, ring, bars, qi, r, h,
+      QFragTable* qtab = reinterpret_cast<QFragTable*>(smem + W * kRingBytes + W * kStagesI8 * 8);
+      ok = run_warp_pages_int8<WIDE>(p, &tm_k8, &tm_v8, st, ring, bars, qtab, qi, r, h,
                                      item.idx_begin, n_pages, has_last, warp, W, lane);
       // Remove the +1152 code bias of the PV operand: O -= 1152 * sum(P'').
       const float sp0 = 1152.f * __shfl_sync(0xffffffffu, st.o1[0], t);

@@ -81,8 +81,19 @@ constexpr int kRingBytes = kStagesI8 * 4096;
 constexpr int kMaxWarps = 8;
 constexpr int kCoStride = 132;  // padded row of the CTA combine buffer
 
+// The INT8 segment's query, split once per CTA (every warp of a CTA serves
+// the same request and KV head): a[lane][4*ks + i] is mma lane `lane`'s
+// A-operand register qi.a[ks][i], a2[lane] the wide form's second-MMA
+// registers, c[lane] its score factor.
+struct QFragTable {
+  uint32_t a[32][16];
+  uint32_t a2[32][8];
+  float c[32];
+};
+constexpr int kQFragBytes = static_cast<int>(sizeof(QFragTable));
+
 __host__ __device__ constexpr int decode_smem_bytes(int warps) {
-  return warps * kRingBytes + warps * kStagesI8 * 8 + 1024;
+  return warps * kRingBytes + warps * kStagesI8 * 8 + kQFragBytes + 1024;
 }
 
 // affine_group16: each page also stages its 64 bytes of group metadata

@@ -16,69 +16,96 @@ __device__ __forceinline__ uint32_t pack_s8x4(int a, int b, int c, int d) {
 
 __device__ __forceinline__ int clamp127(int v) { return v < -127 ? -127 : (v > 127 ? 127 : v); }
 
-// Three-part int8 Q for the INT8 segment (thread t owns dims [32t, 32t+32)).
-// GQA <= 4: lanes g and g+4 both split query row g & 3; lane g packs its
-// (hi, lo), lane g+4 its (lo2, 0).  WIDE: lane g splits query row g.
+// Three-part int8 Q for the INT8 segment, computed once per CTA into the
+// shared table (all warps call this after the query is final, then read
+// their fragments).  Warp w splits the row slots g = w, w + W, ... of the
+// eight mma lane groups: GQA <= 4, slots g and g + 4 both split query row
+// g & 3, slot g keeping (hi, lo) and slot g + 4 (lo2, 0); WIDE, slot g
+// splits row g into (hi, lo) and the second-MMA register lo2.  Lane l of
+// the warp owns the 4 dims 4l..4l+3 = (t, ks, half) = (l / 8, (l / 2) % 4,
+// l % 2) of the fragment order described at QInt8.
 template <bool WIDE>
-__device__ __forceinline__ void load_q_int8(const DecodeParams& p, int r, int h,
-                                            int g, int t, QInt8<WIDE>& qi) {
-  float qv[32];
-  const int row = WIDE ? g : (g & 3);
-  const bool second = !WIDE && g >= 4;  // this lane holds row's lo2 part
-  if (row < p.group) {
-    const __half2* q2 = reinterpret_cast<const __half2*>(
-        p.q + static_cast<int64_t>(r) * p.q_stride_b +
-        static_cast<int64_t>(h * p.group + row) * p.q_stride_h + 32 * t);
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const float2 f = __half22float2(q2[i]);
-      qv[2 * i] = f.x;
-      qv[2 * i + 1] = f.y;
+__device__ __forceinline__ void split_q_cta(const DecodeParams& p, int r, int h, int warp,
+                                            int W, int lane, QFragTable* tab) {
+  const int t = lane >> 3, ks = (lane >> 1) & 3, half = lane & 1;
+  for (int g = warp; g < 8; g += W) {
+    const int row = WIDE ? g : (g & 3);
+    const bool second = !WIDE && g >= 4;
+    float x[4] = {0.f, 0.f, 0.f, 0.f};
+    if (row < p.group) {
+      // Rows are 4-byte aligned (the C ABI's guarantee): half2 loads.
+      const __half2* q2 = reinterpret_cast<const __half2*>(
+          p.q + static_cast<int64_t>(r) * p.q_stride_b +
+          static_cast<int64_t>(h * p.group + row) * p.q_stride_h + 4 * lane);
+      const float2 f0 = __half22float2(q2[0]);
+      const float2 f1 = __half22float2(q2[1]);
+      x[0] = f0.x;
+      x[1] = f0.y;
+      x[2] = f1.x;
+      x[3] = f1.y;
     }
-  } else {
+    float amax = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
 #pragma unroll
-    for (int i = 0; i < 32; ++i) qv[i] = 0.f;
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float sq = amax > 0.f ? amax / 127.f : 1.f;
+    const float inv = 1.f / sq;
+    const float inv_lo = 254.f / sq;
+    const float inv_lo2 = 64516.f / sq;
+    const float step_lo = sq / 254.f;
+    int hv[4], lv[4], l2[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int hi = clamp127(__float2int_rn(x[i] * inv));
+      const float rem = fmaf(-static_cast<float>(hi), sq, x[i]);
+      const int lo = clamp127(__float2int_rn(rem * inv_lo));
+      const float rem2 = fmaf(-static_cast<float>(lo), step_lo, rem);
+      hv[i] = hi;
+      lv[i] = lo;
+      l2[i] = clamp127(__float2int_rn(rem2 * inv_lo2));
+    }
+    const uint32_t ph = pack_s8x4(hv[0], hv[1], hv[2], hv[3]);
+    const uint32_t pl = pack_s8x4(lv[0], lv[1], lv[2], lv[3]);
+    const uint32_t p2 = pack_s8x4(l2[0], l2[1], l2[2], l2[3]);
+    uint32_t* a = tab->a[4 * g + t] + 4 * ks + 2 * half;
+    if constexpr (WIDE) {
+      a[0] = ph;
+      a[1] = pl;
+      tab->a2[4 * g + t][2 * ks + half] = p2;
+    } else {
+      a[0] = second ? p2 : ph;
+      a[1] = second ? 0u : pl;
+    }
+    if ((lane & 7) == 0)
+      tab->c[4 * g + t] = (second || row >= p.group) ? 0.f : sq * (p.sm_scale_log2 / 64516.f);
   }
-  float amax = 0.f;
-#pragma unroll
-  for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(qv[i]));
-  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-  const float sq = amax > 0.f ? amax / 127.f : 1.f;
-  const float inv = 1.f / sq;
-  const float inv_lo = 254.f / sq;
-  const float inv_lo2 = 64516.f / sq;
-  const float step_lo = sq / 254.f;
+  __syncthreads();
+}
+
+// This lane's query fragments from the CTA's table.
+template <bool WIDE>
+__device__ __forceinline__ void load_q_frag(const QFragTable* tab, int lane, QInt8<WIDE>& qi) {
+  const uint4* a = reinterpret_cast<const uint4*>(tab->a[lane]);
 #pragma unroll
   for (int ks = 0; ks < 4; ++ks) {
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      int hv[4], lv[4], l2[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float x = qv[8 * ks + 4 * half + i];
-        const int hi = clamp127(__float2int_rn(x * inv));
-        const float rem = fmaf(-static_cast<float>(hi), sq, x);
-        const int lo = clamp127(__float2int_rn(rem * inv_lo));
-        const float rem2 = fmaf(-static_cast<float>(lo), step_lo, rem);
-        hv[i] = hi;
-        lv[i] = lo;
-        l2[i] = clamp127(__float2int_rn(rem2 * inv_lo2));
-      }
-      const uint32_t ph = pack_s8x4(hv[0], hv[1], hv[2], hv[3]);
-      const uint32_t pl = pack_s8x4(lv[0], lv[1], lv[2], lv[3]);
-      const uint32_t p2 = pack_s8x4(l2[0], l2[1], l2[2], l2[3]);
-      if constexpr (WIDE) {
-        qi.a[ks][2 * half] = ph;
-        qi.a[ks][2 * half + 1] = pl;
-        qi.a2[ks][half] = p2;
-      } else {
-        qi.a[ks][2 * half] = second ? p2 : ph;
-        qi.a[ks][2 * half + 1] = second ? 0u : pl;
-      }
-    }
+    const uint4 v = a[ks];
+    qi.a[ks][0] = v.x;
+    qi.a[ks][1] = v.y;
+    qi.a[ks][2] = v.z;
+    qi.a[ks][3] = v.w;
   }
-  qi.c = second ? 0.f : sq * (p.sm_scale_log2 / 64516.f);
+  if constexpr (WIDE) {
+    const uint4* a2 = reinterpret_cast<const uint4*>(tab->a2[lane]);
+    const uint4 v0 = a2[0], v1 = a2[1];
+    qi.a2[0][0] = v0.x;
+    qi.a2[0][1] = v0.y;
+    qi.a2[1][0] = v0.z;
+    qi.a2[1][1] = v0.w;
+    qi.a2[2][0] = v1.x;
+    qi.a2[2][1] = v1.y;
+    qi.a2[3][0] = v1.z;
+    qi.a2[3][1] = v1.w;
+  }
+  qi.c = tab->c[lane];
 }
 
 __device__ __forceinline__ void mma_s8_16832(int* d, const uint32_t* a,
@@ -275,13 +302,13 @@ __device__ __forceinline__ void issue_pair_int8(const CUtensorMap* tk, const CUt
 template <bool WIDE>
 __device__ __forceinline__ bool run_warp_pages_int8(
     const DecodeParams& p, const CUtensorMap* tk, const CUtensorMap* tv,
-    WarpState& st, uint8_t* ring, uint64_t* bars, QInt8<WIDE>& qi, int r,
+    WarpState& st, uint8_t* ring, uint64_t* bars, QFragTable* qtab, QInt8<WIDE>& qi, int r,
     int h, int idx_begin, int n_pages, bool has_last, int warp, int W,
     int lane) {
   const int g = lane >> 2, t = lane & 3;
   const SegmentDesc& sd = p.seg[0];
+  // A warp without pages still takes part in the CTA's query split below.
   const int n_w = n_pages > warp ? (n_pages - warp + W - 1) / W : 0;
-  if (n_w == 0) return true;
   const int n_pairs = (n_w + 1) >> 1;
 
   PageWindow win;
@@ -323,6 +350,8 @@ __device__ __forceinline__ bool run_warp_pages_int8(
     for (int k = 0; k < 4; ++k) vaddr[k] = tok * 128 + (((2 * k + (j >> 1)) ^ row) << 4);
   }
   pdl_wait_primary();
+  split_q_cta<WIDE>(p, r, h, warp, W, lane, qtab);
+  if (n_w == 0) return true;
   int last_valid = kPage;
   if (has_last) {
     const int lv = __ldg(sd.last_len + r);
@@ -330,7 +359,7 @@ __device__ __forceinline__ bool run_warp_pages_int8(
   }
   // The warp's last page is the request's last page when it is the item's.
   const bool last_here = has_last && warp + W * (n_w - 1) == n_pages - 1;
-  load_q_int8(p, r, h, g, t, qi);
+  load_q_frag<WIDE>(qtab, lane, qi);
 
   // V-scale reference and per-page ratios s_V / s_ref.
   const bool fixed_ref = n_w <= 64;
