@@ -357,7 +357,8 @@ int32_t pg_merge_state_in_place(void* v_a, float* s_a, const void* v_b,
 
 /* Bulk completed-page quantisation: fp32 centring (no FP16 rounding),
  * scale = f16(max(absmax/127, 2^-20)), rounding 0 = half away from zero
- * (prefill quantiser), 1 = half to even (torch.round).                   */
+ * (prefill quantiser), 1 = half to even (torch.round).  value,
+ * value_center, value_codes and value_scales may all be NULL: key only. */
 int32_t pg_quantize_pages(const void* key, const void* value,
                           const void* key_center, const void* value_center,
                           int64_t pages_per_center, void* key_codes,

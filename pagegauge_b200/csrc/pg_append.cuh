@@ -14,12 +14,13 @@
 // that are not rounded to FP16, the same scale rule, and a selectable
 // rounding mode (half away from zero, or half to even as torch.round).
 //
-// Layout: one CTA of 256 threads per (request, KV head).  For the append,
-// thread (g, j) = (t / 64, t % 64) owns the dimension pair (2j, 2j+1) of
-// one query head (g) and of the key (g = 0) or value (g = 1), so every
-// access is a 4-byte half2 and 64 threads cover one coalesced 256-byte FP16
-// row; for the page close, thread t owns 8 dimensions (16 bytes) of token
-// t / 16 of the page.
+// Layout: CTAs of 256 threads; thread (g, j) = (t / 64, t % 64) owns the
+// dimension pair (2j, 2j+1) of one row (a query head, the key or the
+// value), so every access is a 4-byte half2 and 64 threads cover one
+// coalesced 256-byte FP16 row; for a page close, thread t owns 8
+// dimensions (16 bytes) of token t / 16 of the page.  The FP16 comparator
+// runs one CTA per (request, KV head); the page-gauge append two (key and
+// value), each closing its own page.
 #pragma once
 
 #include "pg_common.cuh"
@@ -275,33 +276,52 @@ __device__ __forceinline__ uint2 quantize_half8(const uint4& v, float scale, flo
   return make_uint2(out[0], out[1]);
 }
 
-// One CTA of 256 threads per (request, KV head).  Append: thread (g, j)
-// rotates query head h + g*Hkv's pair j; g = 0 rotates and centres the key
-// pair, g = 1 centres the value pair, both into the ring slot.  Page close
-// (token 15): thread t owns 8 consecutive dims (16 B) of token t/16 of the
-// page for K and V; the 15 older tokens are read from the ring as soon as
-// the position is known (in parallel with the RoPE work), the new token
-// comes through shared memory; the CTA reduces the two abs-maxima, and each
-// thread quantises and writes its 8 + 8 codes (8-byte stores).
+// Two CTAs of 256 threads per (request, KV head): role 0 appends and closes
+// the key, role 1 the value, and the request's 2*Hkv CTAs share its query
+// heads (CTA c = 2h + role rotates heads c, c + 2*Hkv, ...).  Thread
+// (g, j) = (t / 64, t % 64): g = 0 rotates (key) and centres its role's
+// dimension pair j into the ring slot; g >= 1 rotates pair j of one query
+// head.  Page close (token 15): thread t owns 8 consecutive dims (16 B) of
+// token t / 16 of the role's page; the 15 older tokens are read from the
+// ring as soon as the position is known (alongside the RoPE row), the new
+// token comes through shared memory, one CTA reduction gives the abs-max,
+// and each thread quantises and writes its 8 codes (one 8-byte store).
 // SERVED: pages addressed through the served pool's per-row slots
 // (token_slots / exact_slots / center_rows) instead of the request-major
 // layout.
 template <bool SERVED>
 __global__ void __launch_bounds__(kAppendThreads)
     pg_rope_append_page_gauge_kernel(const __grid_constant__ AppendParams p) {
-  __shared__ float red[2][kAppendThreads / 32];
+  __shared__ float red[kAppendThreads / 32];
   // A dependent decode launch may start streaming completed INT8 pages now:
-  // the page this launch may close is still in the exact window, so the
-  // decode reads it from the ring, and the decode waits for this grid
-  // before reading q or the ring.  This grid waits for its own predecessor
-  // (which produced q, k, v) before reading anything.
+  // the page this launch may close is still in the exact window (or the
+  // decode was told to request its INT8 tiles only after this grid), and
+  // the decode waits for this grid before reading q or the ring.  This grid
+  // waits for its own predecessor (which produced q, k, v) before reading
+  // anything.
   pdl_launch_dependents();
   pdl_wait_primary();
-  __shared__ __align__(16) uint32_t newest[2][kHeadDim / 2];
-  const int r = blockIdx.x / p.hkv;
-  const int h = blockIdx.x % p.hkv;
+  __shared__ __align__(16) uint32_t newest[kHeadDim / 2];
+  const int per_request = 2 * p.hkv;
+  const int r = blockIdx.x / per_request;
+  const int c = blockIdx.x % per_request;
+  const int h = c >> 1, role = c & 1;
   const int g = threadIdx.x >> 6, j = threadIdx.x & 63;
-  const AppendInputs in = load_append_inputs(p, r, h, g, j);
+  // Loads that do not depend on the position.
+  uint32_t x = 0u, partner = 0u, qx = 0u, qpartner = 0u;
+  const int qh = c + (g - 1) * per_request;  // g >= 1: this thread's query head
+  if (g == 0) {
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(
+        (role == 0 ? p.k + r * p.k_stride_b : p.v + r * p.v_stride_b) +
+        static_cast<int64_t>(h) * kHeadDim);
+    x = src[j];
+    if (role == 0) partner = src[(j + 32) & 63];
+  } else if (qh < p.hq) {
+    const uint32_t* q32 = reinterpret_cast<const uint32_t*>(
+        p.q + r * p.q_stride_b + static_cast<int64_t>(qh) * kHeadDim);
+    qx = q32[j];
+    qpartner = q32[(j + 32) & 63];
+  }
   int64_t crow = r;
   if constexpr (SERVED) {
     crow = __ldg(p.center_rows + r);
@@ -311,9 +331,10 @@ __global__ void __launch_bounds__(kAppendThreads)
     }
   }
   uint32_t center = 0u;
-  if (g < 2) {
+  if (g == 0) {
     const int64_t cofs = crow * p.center_stride_b + static_cast<int64_t>(h) * kHeadDim;
-    center = reinterpret_cast<const uint32_t*>((g == 0 ? p.key_center : p.value_center) + cofs)[j];
+    center = reinterpret_cast<const uint32_t*>((role == 0 ? p.key_center : p.value_center) +
+                                               cofs)[j];
   }
   int64_t pos;
   const __half *cosr, *sinr;
@@ -346,61 +367,53 @@ __global__ void __launch_bounds__(kAppendThreads)
     code_page = r * p.code_pages_per_request + page;
   }
   const int64_t row_stride = static_cast<int64_t>(p.hkv) * kHeadDim;  // per token
-  __half* kring = p.key_pages + (ring_page * kPage * p.hkv + h) * kHeadDim;
-  __half* vring = p.value_pages + (ring_page * kPage * p.hkv + h) * kHeadDim;
+  __half* ring = (role == 0 ? p.key_pages : p.value_pages) +
+                 (ring_page * kPage * p.hkv + h) * kHeadDim;
   // The 16th token closes the page: its INT8 copy is produced now, so it is
   // ready when the page later leaves the exact window.
   const bool close = token == kPage - 1;  // uniform over the CTA
   const int tk = threadIdx.x >> 4, col = (threadIdx.x & 15) * 8;
-  uint4 kx = make_uint4(0u, 0u, 0u, 0u), vx = kx;
-  if (close && tk < kPage - 1) {
-    kx = *reinterpret_cast<const uint4*>(kring + tk * row_stride + col);
-    vx = *reinterpret_cast<const uint4*>(vring + tk * row_stride + col);
-  }
-  const uint32_t c = reinterpret_cast<const uint32_t*>(cosr)[j];
-  const uint32_t s = reinterpret_cast<const uint32_t*>(sinr)[j];
+  uint4 vals = make_uint4(0u, 0u, 0u, 0u);
+  if (close && tk < kPage - 1) vals = *reinterpret_cast<const uint4*>(ring + tk * row_stride + col);
+  const uint32_t cs = reinterpret_cast<const uint32_t*>(cosr)[j];
+  const uint32_t sn = reinterpret_cast<const uint32_t*>(sinr)[j];
   if constexpr (SERVED) {
-    if (g == 1)
+    if (g == 0 && role == 1)
       reinterpret_cast<uint32_t*>(p.center_out +
                                   (static_cast<int64_t>(r) * p.hkv + h) * kHeadDim)[j] = center;
   }
-  rotate_query_heads(p, r, h, g, j, in, c, s);
-  if (g < 2) {
-    const uint32_t val = g == 0 ? center_pair(rope_apply(in.x, in.partner, j, c, s), center)
-                                : center_pair(in.x, center);
-    reinterpret_cast<uint32_t*>((g == 0 ? kring : vring) + token * row_stride)[j] = val;
-    if (close) newest[g][j] = val;
+  if (g >= 1) {
+    __half* out = p.rotated_q + static_cast<int64_t>(r) * p.hq * kHeadDim;
+    if (qh < p.hq)
+      reinterpret_cast<uint32_t*>(out + static_cast<int64_t>(qh) * kHeadDim)[j] =
+          rope_apply(qx, qpartner, j, cs, sn);
+    // Query heads beyond three per CTA (Hq > 6 * Hkv).
+    for (int qo = qh + 3 * per_request; qo < p.hq; qo += 3 * per_request) {
+      const __half* src = p.q + r * p.q_stride_b + static_cast<int64_t>(qo) * kHeadDim;
+      reinterpret_cast<uint32_t*>(out + static_cast<int64_t>(qo) * kHeadDim)[j] =
+          rope_pair(src, j, cs, sn);
+    }
+  } else {
+    const uint32_t val = center_pair(role == 0 ? rope_apply(x, partner, j, cs, sn) : x, center);
+    reinterpret_cast<uint32_t*>(ring + token * row_stride)[j] = val;
+    if (close) newest[j] = val;
   }
   if (!close) return;
   __syncthreads();
-  if (tk == kPage - 1) {
-    kx = *reinterpret_cast<const uint4*>(&newest[0][col / 2]);
-    vx = *reinterpret_cast<const uint4*>(&newest[1][col / 2]);
-  }
-  float km = absmax_half8(kx), vm = absmax_half8(vx);
+  if (tk == kPage - 1) vals = *reinterpret_cast<const uint4*>(&newest[col / 2]);
+  float m = absmax_half8(vals);
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    km = fmaxf(km, __shfl_xor_sync(0xffffffffu, km, o));
-    vm = fmaxf(vm, __shfl_xor_sync(0xffffffffu, vm, o));
-  }
-  if ((threadIdx.x & 31) == 0) {
-    red[0][threadIdx.x >> 5] = km;
-    red[1][threadIdx.x >> 5] = vm;
-  }
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
   __syncthreads();
 #pragma unroll
-  for (int w = 0; w < kAppendThreads / 32; ++w) {
-    km = fmaxf(km, red[0][w]);
-    vm = fmaxf(vm, red[1][w]);
-  }
-  const __half ks_h = __float2half_rn(fmaxf(__fdiv_rn(km, 127.f), 0x1p-20f));
-  const __half vs_h = __float2half_rn(fmaxf(__fdiv_rn(vm, 127.f), 0x1p-20f));
-  if (threadIdx.x == 0) p.key_scales[code_page * p.hkv + h] = ks_h;
-  if (threadIdx.x == 1) p.value_scales[code_page * p.hkv + h] = vs_h;
+  for (int w = 0; w < kAppendThreads / 32; ++w) m = fmaxf(m, red[w]);
+  const __half s_h = __float2half_rn(fmaxf(__fdiv_rn(m, 127.f), 0x1p-20f));
+  if (threadIdx.x == 0) (role == 0 ? p.key_scales : p.value_scales)[code_page * p.hkv + h] = s_h;
   const int64_t cbase = (code_page * kPage * p.hkv + h) * kHeadDim + tk * row_stride + col;
-  const float ksf = __half2float(ks_h), vsf = __half2float(vs_h);
-  *reinterpret_cast<uint2*>(p.key_codes + cbase) = quantize_half8(kx, ksf, __frcp_rn(ksf));
-  *reinterpret_cast<uint2*>(p.value_codes + cbase) = quantize_half8(vx, vsf, __frcp_rn(vsf));
+  const float sf = __half2float(s_h);
+  *reinterpret_cast<uint2*>((role == 0 ? p.key_codes : p.value_codes) + cbase) =
+      quantize_half8(vals, sf, __frcp_rn(sf));
 }
 
 // Zero the four planes (K/V codes, K/V scales) of the listed pool pages:
@@ -453,8 +466,11 @@ __global__ void __launch_bounds__(64)
   const int j = threadIdx.x;
   const int64_t center = p.pages_per_center > 0 ? page / p.pages_per_center : 0;
   const int64_t cofs = (center * p.hkv + h) * kHeadDim;
+  // value == null: key pages only (one tensor to quantise).
+  const bool has_v = p.value != nullptr;
   const __half2 kc = reinterpret_cast<const __half2*>(p.key_center + cofs)[j];
-  const __half2 vc = reinterpret_cast<const __half2*>(p.value_center + cofs)[j];
+  const __half2 vc = has_v ? reinterpret_cast<const __half2*>(p.value_center + cofs)[j]
+                           : __floats2half2_rn(0.f, 0.f);
   const int64_t row_stride = static_cast<int64_t>(p.hkv) * kHeadDim;
   const int64_t base = (page * kPage * p.hkv + h) * kHeadDim;
   float2 kf[kPage], vf[kPage];
@@ -462,7 +478,9 @@ __global__ void __launch_bounds__(64)
 #pragma unroll
   for (int tk = 0; tk < kPage; ++tk) {
     const __half2 kx = reinterpret_cast<const __half2*>(p.key + base + tk * row_stride)[j];
-    const __half2 vx = reinterpret_cast<const __half2*>(p.value + base + tk * row_stride)[j];
+    const __half2 vx = has_v
+                           ? reinterpret_cast<const __half2*>(p.value + base + tk * row_stride)[j]
+                           : __floats2half2_rn(0.f, 0.f);
     kf[tk].x = __fsub_rn(__low2float(kx), __low2float(kc));
     kf[tk].y = __fsub_rn(__high2float(kx), __high2float(kc));
     vf[tk].x = __fsub_rn(__low2float(vx), __low2float(vc));
@@ -476,18 +494,21 @@ __global__ void __launch_bounds__(64)
   const __half vs_h = __float2half_rn(fmaxf(__fdiv_rn(vm, 127.f), 0x1p-20f));
   if (j == 0) {
     p.key_scales[page * p.hkv + h] = ks_h;
-    p.value_scales[page * p.hkv + h] = vs_h;
+    if (has_v) p.value_scales[page * p.hkv + h] = vs_h;
   }
   const float ksf = __half2float(ks_h), vsf = __half2float(vs_h);
 #pragma unroll
   for (int tk = 0; tk < kPage; ++tk) {
-    char2 kz, vz;
+    char2 kz;
     kz.x = quantize_one(kf[tk].x, ksf, p.half_even);
     kz.y = quantize_one(kf[tk].y, ksf, p.half_even);
-    vz.x = quantize_one(vf[tk].x, vsf, p.half_even);
-    vz.y = quantize_one(vf[tk].y, vsf, p.half_even);
     reinterpret_cast<char2*>(p.key_codes + base + tk * row_stride)[j] = kz;
-    reinterpret_cast<char2*>(p.value_codes + base + tk * row_stride)[j] = vz;
+    if (has_v) {
+      char2 vz;
+      vz.x = quantize_one(vf[tk].x, vsf, p.half_even);
+      vz.y = quantize_one(vf[tk].y, vsf, p.half_even);
+      reinterpret_cast<char2*>(p.value_codes + base + tk * row_stride)[j] = vz;
+    }
   }
 }
 

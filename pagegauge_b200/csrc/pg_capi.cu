@@ -498,7 +498,7 @@ static int32_t append_page_gauge_impl(
   p.exact_sink_pages = exact_sink_pages;
   p.code_pages_per_request = code_ppr;
   p.error_flag = device_error_ptr();
-  return launch_pdl(pg::pg_rope_append_page_gauge_kernel<false>, dim3(batch * kv_heads),
+  return launch_pdl(pg::pg_rope_append_page_gauge_kernel<false>, dim3(batch * kv_heads * 2),
                     dim3(pg::kAppendThreads), 0, static_cast<cudaStream_t>(stream),
                     "rope_append_page_gauge launch", p);
 }
@@ -591,7 +591,7 @@ int32_t pg_rope_append_page_gauge_served(
   p.num_code_pages = num_code_pages;
   p.num_exact_pages = num_exact_pages;
   p.num_centers = num_centers;
-  return launch_pdl(pg::pg_rope_append_page_gauge_kernel<true>, dim3(batch * kv_heads),
+  return launch_pdl(pg::pg_rope_append_page_gauge_kernel<true>, dim3(batch * kv_heads * 2),
                     dim3(pg::kAppendThreads), 0, static_cast<cudaStream_t>(stream),
                     "served rope_append_page_gauge launch", p);
 }
@@ -979,6 +979,13 @@ int32_t pg_quantize_pages(const void* key, const void* value,
   PG_REQUIRE(pages_per_center >= 0, "pages_per_center must be non-negative");
   if (num_pages == 0) return PG_OK;
   PG_REQUIRE(num_pages * kv_heads < (int64_t(1) << 31), "too many pages");
+  const bool key_only = value == nullptr;
+  PG_REQUIRE(!key_only || (value_center == nullptr && value_codes == nullptr &&
+                           value_scales == nullptr),
+             "value, value_center, value_codes and value_scales are all given or all NULL");
+  PG_REQUIRE(key != nullptr && key_center != nullptr && key_codes != nullptr &&
+                 key_scales != nullptr,
+             "key, key_center, key_codes and key_scales are required");
   PG_REQUIRE(aligned(key, 4) && aligned(value, 4) && aligned(key_center, 4) &&
                  aligned(value_center, 4) && aligned(key_codes, 2) && aligned(value_codes, 2),
              "tensors must be aligned");

@@ -68,13 +68,14 @@ def quantize_completed_kv_pages(key, value, key_center, value_center, key_codes,
 
 
 def _quantize_one(values: torch.Tensor, center: torch.Tensor):
+    """One tensor's pages: the bulk quantiser's key-only form, torch.round."""
+    if not values.is_cuda or values.dtype != torch.float16 or not values.is_contiguous():
+        raise ValueError("values must be contiguous CUDA [pages,16,heads,128] float16")
     codes = torch.empty_like(values, dtype=torch.int8)
     scale = torch.empty(values.shape[0], values.shape[2], device=values.device, dtype=torch.float16)
-    # K and V slots of the kernel both receive this tensor; the duplicate
-    # work is negligible next to a separate launch per role.
-    codes2 = torch.empty_like(codes)
-    scale2 = torch.empty_like(scale)
-    quantize_pages_into(values, values, center, center, codes, codes2, scale, scale2, 0, "half_even")
+    _lib.call("pg_quantize_pages", values.data_ptr(), None, center.data_ptr(), None, 0,
+              codes.data_ptr(), None, scale.data_ptr(), None, values.shape[0], values.shape[2],
+              1, _stream(values))
     return codes, scale
 
 
