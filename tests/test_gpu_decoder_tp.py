@@ -21,6 +21,10 @@ pytestmark = pytest.mark.gpu
 
 WORLD = 2
 STEPS = 6
+# Logits against the float64 oracle: the FP16 rounding floor of this small
+# model, stated in tests/test_gpu_decoder.py (its dense prefill, which uses
+# none of this library's kernels, is already 1.5e-3 from the oracle).
+LOGIT_ATOL = 2.5e-3
 
 
 def _cfg():
@@ -101,7 +105,7 @@ def test_two_gpu_tensor_parallel_decoder_matches_oracle(cuda_lib, tmp_path, gemm
     for r in range(2):
         exp, _ = D.dense_forward(w, ocfg, prompt[r].numpy())
         err = np.abs(logits[0, r] - exp).max()
-        assert err < 2e-3, err
+        assert err < LOGIT_ATOL, err
     # Greedy tokens are the argmax of the gathered logits at every step.
     assert np.array_equal(tokens, logits.argmax(-1))
     # Decode steps from the gathered post-prefill caches, teacher-forced
@@ -116,4 +120,4 @@ def test_two_gpu_tensor_parallel_decoder_matches_oracle(cuda_lib, tmp_path, gemm
     for i in range(STEPS):
         exp = D.decode_step(w, ocfg, caches, tokens[i], [200 + i] * 2, int(got["capacity"]))
         err = np.abs(logits[i + 1] - exp).max()
-        assert err < 2e-3, (i, err)
+        assert err < LOGIT_ATOL, (i, err)
