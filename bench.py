@@ -427,7 +427,7 @@ class AttentionBench:
     of the public-API decode step."""
 
     def __init__(self, lengths, layers: int, split: int, fused_merge: bool, seed: int,
-                 warps: int = 4, cluster: int = 0):
+                 warps: int = 4, cluster: int = 0, hkv: int = HKV):
         from pagegauge_b200 import scheduler
         from pagegauge_b200.cache import build_gauge_cache, rope_tables, synthetic_dense_cache
         from pagegauge_b200.decode import PageGaugeDecode
@@ -441,7 +441,7 @@ class AttentionBench:
         self.q = self.tables = None
         for layer in range(self.layers):
             # layer copies take their values from the benchmark seeds in turn
-            qi, dk, dv = synthetic_dense_cache(lengths, seed=seed + layer % len(SEEDS),
+            qi, dk, dv = synthetic_dense_cache(lengths, hkv=hkv, seed=seed + layer % len(SEEDS),
                                                device="cuda")
             cache, tables = build_gauge_cache(dk, dv, lengths, capacity_pages=cap)
             del dk, dv
@@ -452,14 +452,19 @@ class AttentionBench:
         torch.cuda.synchronize()
         if split < 0:
             split = scheduler.lookup(len(lengths), max(lengths))
+            if split and hkv < HKV:
+                # The table is measured with 8 KV heads; fewer heads split
+                # each head finer so the work list still fills one wave.
+                split = max(1, split * hkv // HKV)
         self.ws = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
         self.dec = PageGaugeDecode(self.ws, warps_per_cta=warps)
         t = self.tables
         self.dec.plan(t.old_indptr, t.old_indices, t.exact_indptr, t.exact_indices,
-                      t.exact_last_page_len, HQ, HKV, old_split_pages=split, exact_split_pages=0)
+                      t.exact_last_page_len, 4 * hkv, hkv, old_split_pages=split,
+                      exact_split_pages=0)
         self.plan = self.dec.work_plan
         self.out = torch.empty_like(self.q)
-        self.nbytes = algorithmic_bytes(t.old_tokens, t.exact_tokens)
+        self.nbytes = algorithmic_bytes(t.old_tokens, t.exact_tokens, hkv=hkv)
         self.launches_per_step = 1 if ((self.plan.single and self.plan.num_items)
                                        or fused_merge or cluster > 1) else 2
         self.rope = rope_tables(cap * PAGE, device="cuda")
@@ -1231,16 +1236,23 @@ def measure_b8_sharded(args, dist: Dist, rank: int, peak: float) -> dict:
     every N, no data-path collective).  Per seed: max-over-ranks step time,
     aggregate GB/s, the kernel's roofline fraction and the per-rank byte
     imbalance (max / mean)."""
-    from pagegauge_b200.shard import request_bytes
+    from pagegauge_b200.shard import plan_shards
 
     world = dist.world
     steps = max(200, args.steps // 10)
     per_seed = []
     for seed in SEEDS:
-        mine, glob, shards = workload_lengths("b8_ragged", world, rank, seed=seed)
-        loads = [sum(request_bytes(glob[i]) for i in sh) for sh in shards]
+        glob = global_lengths("b8_ragged", seed)
+        plan = plan_shards(glob, world, kv_heads=HKV)
+        shards, loads = plan["requests"], plan["rank_bytes"]
+        mine = [glob[i] for i in shards[rank]]
+        h0, h1 = plan["heads"][rank]
+        hkv = h1 - h0
+        sharding = ("requests (longest-first bin packing on decode bytes)"
+                    if plan["mode"] == "requests"
+                    else f"KV heads ({hkv} of {HKV} per GPU, all requests)")
         if mine:
-            b8 = AttentionBench(mine, args.layers, -1, False, seed=seed)
+            b8 = AttentionBench(mine, args.layers, -1, False, seed=seed, hkv=hkv)
             b8.capture()
             my_bytes = b8.nbytes
             b8_ms = b8.time_steps(steps, args.warmup, dist)
@@ -1259,7 +1271,7 @@ def measure_b8_sharded(args, dist: Dist, rank: int, peak: float) -> dict:
             "seed": seed, "lengths": glob, "shards": shards, "value_gbs": round(total / (b8_ms * 1e-3) / 1e9, 2),
             "us_per_step": b8_ms * 1e3, "kernel_us": b8_kms * 1e3,
             "kernel_frac_of_peak": round(max(loads) / (b8_kms * 1e-3) / 1e9 / peak, 4),
-            "algorithmic_bytes_per_step": int(total), "rank_bytes": loads,
+            "algorithmic_bytes_per_step": int(total), "rank_bytes": loads, "sharding": sharding,
             "imbalance": round(max(loads) / (sum(loads) / len(loads)), 4),
             "split_pages_rank0": split, "work_items_rank0": items,
         })
@@ -1268,7 +1280,8 @@ def measure_b8_sharded(args, dist: Dist, rank: int, peak: float) -> dict:
     return {"metric": "decode-attn HBM GB/s (b8_ragged, 3 seeds)", "unit": "GB/s",
             "value": round(tot_bytes / (tot_us * 1e-6) / 1e9, 2),
             "us_per_step_mean": tot_us / len(per_seed), "steps": steps,
-            "scaling": f"strong (the 8 requests sharded over {world} GPU(s))",
+            "scaling": f"strong (the same 8 requests over {world} GPU(s), sharded by request "
+                       f"or by KV head, whichever balances the bytes)",
             "per_seed": per_seed}
 
 

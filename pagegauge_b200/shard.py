@@ -1,13 +1,21 @@
-"""Request sharding across the GPUs of one box (no data-path collective).
+"""Sharding a decode batch across the GPUs of one box (no data-path
+collective).
 
-Requests of a ragged decode batch are independent, so a batch is split
-across ranks by greedy longest-first bin packing on each request's decode
-bytes (INT8 old pages + scales + the FP16 exact tail); each rank decodes
-its own requests with its own cache and the outputs are gathered on the
-host afterwards.  The reference runs one GPU only; the per-request byte
-model is the one its B8 ragged accounting uses
-(scripts/benchmark_flashinfer_page_affine_int8.py:392-420 splits old and
-exact pages per request).
+Requests of a ragged decode batch are independent, and so are the KV heads
+of a request, so a batch splits across ranks either way:
+
+* by request: greedy longest-first bin packing on each request's decode
+  bytes (INT8 old pages + scales + the FP16 exact tail); each rank decodes
+  its own requests with its own cache;
+* by KV head: every rank decodes every request over Hkv/N of its KV heads
+  (and their query heads); each rank's bytes are exactly 1/N of the batch.
+
+``plan_shards`` takes request shards when they balance the bytes to within
+a tolerance and KV-head shards otherwise (a few long requests on many
+GPUs).  Outputs are gathered on the host afterwards.  The reference runs
+one GPU only; the per-request byte model is the one its B8 ragged
+accounting uses (scripts/benchmark_flashinfer_page_affine_int8.py:392-420
+splits old and exact pages per request).
 """
 
 from __future__ import annotations
@@ -67,3 +75,36 @@ def gather_outputs(shards, outputs, batch: int):
         for row, i in enumerate(idx):
             full[i] = out[row]
     return full
+
+
+def head_range(kv_heads: int, world: int, rank: int) -> tuple[int, int]:
+    """KV heads [h0, h1) of ``rank`` when ``world`` ranks split ``kv_heads``."""
+    if world < 1 or kv_heads % world:
+        raise ValueError("KV heads must divide evenly across the ranks")
+    per = kv_heads // world
+    return rank * per, (rank + 1) * per
+
+
+def plan_shards(lengths, world: int, kv_heads: int = 8, tolerance: float = 1.02) -> dict:
+    """Choose how ``world`` ranks split a ragged batch: request shards when
+    the largest rank's bytes are within ``tolerance`` of the mean (or the
+    heads cannot be split evenly), else KV-head shards.  Returns
+    {"mode": "requests" | "heads", "requests": [[request ids] per rank],
+    "heads": [(h0, h1) per rank], "rank_bytes": [...]}."""
+    shards = shard_requests(lengths, world, kv_heads=kv_heads)
+    loads = shard_loads(lengths, shards, kv_heads=kv_heads)
+    mean = sum(loads) / world
+    if world == 1 or kv_heads % world or max(loads) <= mean * tolerance:
+        return {"mode": "requests", "requests": shards,
+                "heads": [(0, kv_heads)] * world, "rank_bytes": loads}
+    per = kv_heads // world
+    every = list(range(len(lengths)))
+    return {"mode": "heads", "requests": [every] * world,
+            "heads": [head_range(kv_heads, world, r) for r in range(world)],
+            "rank_bytes": [sum(request_bytes(n, kv_heads=per) for n in lengths)] * world}
+
+
+def gather_head_outputs(outputs, group: int):
+    """Concatenate per-rank outputs [B, group * (Hkv/N), 128] of KV-head
+    shards (rank order = head order) into [B, Hq, 128]."""
+    return np.concatenate(list(outputs), axis=1)

@@ -454,3 +454,25 @@ def test_b8_ragged_full_size_and_shards(cuda_lib, seed):
     assert read_device_error() == 0
     full = gather_outputs(shards, parts, len(lengths))
     assert O.max_abs(full.astype(np.float64), cpu(out).astype(np.float64)) <= 2e-3
+    if seed != 20261001:
+        return
+    # KV-head shards (each rank: every request over 8/N heads) gathered
+    # along the head axis reproduce the whole batch as well.
+    from pagegauge_b200.shard import gather_head_outputs, head_range
+
+    for world in (2, 4, 8):
+        parts = []
+        for rank in range(world):
+            h0, h1 = head_range(8, world, rank)
+            sub = lambda t: t[:, :, h0:h1].contiguous()  # noqa: E731
+            dec = PageGaugeDecode(workspace())
+            dec.plan(tables.old_indptr, tables.old_indices, tables.exact_indptr,
+                     tables.exact_indices, tables.exact_last_page_len, 4 * (h1 - h0), h1 - h0)
+            part = dec.run(q[:, 4 * h0:4 * h1].contiguous(), sub(cache.key_codes),
+                           sub(cache.value_codes), cache.key_scales[:, h0:h1].contiguous(),
+                           cache.value_scales[:, h0:h1].contiguous(), sub(cache.exact_key),
+                           sub(cache.exact_value), cache.value_center[:, h0:h1].contiguous())
+            torch.cuda.synchronize()
+            parts.append(cpu(part))
+        full = gather_head_outputs(parts, 4)
+        assert O.max_abs(full.astype(np.float64), cpu(out).astype(np.float64)) <= 2e-3

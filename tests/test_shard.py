@@ -117,3 +117,33 @@ def test_two_rank_gloo_shard_and_gather_matches_single_process(tmp_path):
     ref = _decode_requests(lengths, list(range(len(lengths))), seed)
     assert full.shape == ref.shape
     assert np.array_equal(full, ref)
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_plan_shards_balances_bytes(world):
+    from pagegauge_b200.shard import plan_shards, ragged_lengths, request_bytes
+
+    for seed in (20261001, 20261002, 20261003):
+        lengths = ragged_lengths(8, seed)
+        total = sum(request_bytes(n) for n in lengths)
+        plan = plan_shards(lengths, world)
+        assert sum(plan["rank_bytes"]) == total or plan["mode"] == "heads"
+        if plan["mode"] == "requests":
+            assert max(plan["rank_bytes"]) <= total / world * 1.02
+            assert sorted(sum(plan["requests"], [])) == list(range(8))
+        else:
+            # every rank: all requests over its own 8/world heads, 1/world of the bytes
+            assert plan["heads"] == [(r * 8 // world, (r + 1) * 8 // world) for r in range(world)]
+            assert all(req == list(range(8)) for req in plan["requests"])
+            assert sum(plan["rank_bytes"]) == total
+    # one long request among short ones on 8 GPUs: heads
+    assert plan_shards([32768] + [4096] * 7, 8)["mode"] == "heads"
+    assert plan_shards([4096] * 8, 8)["mode"] == "requests"
+
+
+def test_head_shards_gather_to_the_whole_batch():
+    from pagegauge_b200.shard import gather_head_outputs
+
+    full = np.random.default_rng(0).standard_normal((8, 32, 128))
+    parts = [full[:, 8 * r:8 * (r + 1)] for r in range(4)]  # 2 KV heads x group 4 each
+    assert np.array_equal(gather_head_outputs(parts, 4), full)
