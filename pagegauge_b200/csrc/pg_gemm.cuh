@@ -607,28 +607,43 @@ __global__ void __launch_bounds__(kTpReduceThreads)
     float d[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) d[e] = 0.f;
-    for (int src = 0; src < p.world; ++src) {
-      const uint2* slot = recv + ((static_cast<int64_t>(par) * kGemmMaxTp + src) * cap + t) *
-                                     tp_slot_pairs();
-      // All eight loads in flight, then re-read only values whose tag is not
-      // yet this exchange's count (not arrived), for about a second at most.
-      const uint2* row = slot + b * kGemmTileRows + j0;  // 8 contiguous pairs (64 B)
-      uint2 v[8];
+    // Ranks in batches of kSrcBatch: every load of a batch is in flight
+    // before the first tag is checked (one memory round trip per batch, not
+    // per rank), then only values whose tag is not yet this exchange's
+    // count (not arrived) are re-read, for about a second at most.  The
+    // sum runs in rank order, identical on every rank.
+    constexpr int kSrcBatch = 4;
+    for (int s0 = 0; s0 < p.world; s0 += kSrcBatch) {
+      uint2 v[kSrcBatch][8];
+      const uint2* rows[kSrcBatch];
 #pragma unroll
-      for (int e = 0; e < 8; e += 2) ld_pairs2_relaxed_sys(row + e, v[e], v[e + 1]);
+      for (int k = 0; k < kSrcBatch; ++k) {
+        const int src = s0 + k;
+        rows[k] = recv + ((static_cast<int64_t>(par) * kGemmMaxTp + src) * cap + t) *
+                             tp_slot_pairs() +
+                  b * kGemmTileRows + j0;  // 8 contiguous pairs (64 B)
+        if (src < p.world) {
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        for (uint32_t spin = 0; ok && static_cast<int32_t>(v[e].y) != want; ++spin) {
-          // About a second from the kernel's start (2^26 polls as a backstop).
-          if (spin == (1u << 26) ||
-              ((spin & 255u) == 255u && globaltimer_ns() - t0 > kTpWaitNs)) {
-            ok = false;
-            break;
-          }
-          __nanosleep(32);
-          v[e] = ld_pair_relaxed_sys(row + e);
+          for (int e = 0; e < 8; e += 2) ld_pairs2_relaxed_sys(rows[k] + e, v[k][e], v[k][e + 1]);
         }
-        d[e] += __uint_as_float(v[e].x);
+      }
+#pragma unroll
+      for (int k = 0; k < kSrcBatch; ++k) {
+        if (s0 + k >= p.world) break;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          for (uint32_t spin = 0; ok && static_cast<int32_t>(v[k][e].y) != want; ++spin) {
+            // About a second from the kernel's start (2^26 polls as a backstop).
+            if (spin == (1u << 26) ||
+                ((spin & 255u) == 255u && globaltimer_ns() - t0 > kTpWaitNs)) {
+              ok = false;
+              break;
+            }
+            __nanosleep(32);
+            v[k][e] = ld_pair_relaxed_sys(rows[k] + e);
+          }
+          d[e] += __uint_as_float(v[k][e].x);
+        }
       }
     }
     uint32_t* xw = reinterpret_cast<uint32_t*>(&x[c]);
