@@ -451,11 +451,7 @@ class AttentionBench:
         self.capacity_pages = cap
         torch.cuda.synchronize()
         if split < 0:
-            split = scheduler.lookup(len(lengths), max(lengths))
-            if split and hkv < HKV:
-                # The table is measured with 8 KV heads; fewer heads split
-                # each head finer so the work list still fills one wave.
-                split = max(1, split * hkv // HKV)
+            split = scheduler.lookup(len(lengths), max(lengths), kv_heads=hkv)
         self.ws = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
         self.dec = PageGaugeDecode(self.ws, warps_per_cta=warps)
         t = self.tables

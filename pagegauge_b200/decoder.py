@@ -513,11 +513,7 @@ class PageGaugeDecoder:
         old_idx = torch.from_numpy(o_idx).to(dev)
         ex_idx = torch.from_numpy(e_idx).to(dev)
         has_old = bool(o_ptr[-1] > 0)
-        split = scheduler.lookup(self.batch, int(max(positions)) + 1)
-        if split and self.hkv < 8:
-            # The table is measured with 8 KV heads; a rank holding fewer
-            # splits each head finer so the work list still fills one wave.
-            split = max(1, split * self.hkv // 8)
+        split = scheduler.lookup(self.batch, int(max(positions)) + 1, kv_heads=self.hkv)
         dec.plan(torch.from_numpy(o_ptr) if has_old else None, old_idx if has_old else None,
                  torch.from_numpy(e_ptr), ex_idx, self.last_len, self.hq, self.hkv,
                  old_split_pages=split, old_last_page_len=self._old_last if has_old else None)

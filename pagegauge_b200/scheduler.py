@@ -10,7 +10,7 @@ back over caches larger than the L2; ``--mode burst`` times single decodes
 behind a 256 MiB scrub instead), and the argmin is stored per (batch,
 half-octave context) bucket in ``split_table.json`` next to this file.
 
-    python -m pagegauge_b200.scheduler --sweep [--batch 1 --context 49152]
+    python -m pagegauge_b200.scheduler --sweep [--batch 1 --context 49152] [--kv-heads 8 1]
 """
 
 from __future__ import annotations
@@ -25,15 +25,16 @@ TABLE_PATH = Path(__file__).resolve().parent / "split_table.json"
 PAGE = 16
 
 
-def bucket(batch: int, context: int) -> str:
+def bucket(batch: int, context: int, kv_heads: int = 8) -> str:
     """Batch exact, context rounded down to a half octave (2^k or 1.5 * 2^k,
     >= 1024): bucket 2^k covers [2^k, 1.5 * 2^k), bucket 1.5 * 2^k covers
-    [1.5 * 2^k, 2^(k+1))."""
+    [1.5 * 2^k, 2^(k+1)); KV heads other than 8 (a tensor-parallel or
+    head-sharded rank) get their own entries."""
     k = max(10, int(math.floor(math.log2(max(context, 1)))))
     c = 1 << k
     if k >= 11 and context >= c + c // 2:
         c += c // 2
-    return f"b{batch}_c{c}"
+    return f"b{batch}_c{c}" + ("" if kv_heads == 8 else f"_h{kv_heads}")
 
 
 def load_table(path: Path = TABLE_PATH) -> dict:
@@ -42,11 +43,19 @@ def load_table(path: Path = TABLE_PATH) -> dict:
     return {"entries": {}}
 
 
-def lookup(batch: int, context: int, path: Path = TABLE_PATH) -> int:
+def lookup(batch: int, context: int, path: Path = TABLE_PATH, kv_heads: int = 8) -> int:
     """Pages per work item for this shape; 0 (the one-wave heuristic) when
-    the bucket was never measured."""
-    entry = load_table(path)["entries"].get(bucket(batch, context))
-    return int(entry["split_pages"]) if entry else 0
+    the bucket was never measured.  With fewer than 8 KV heads and no entry
+    of its own, the 8-head entry scaled by kv_heads / 8 (each head split
+    finer, so the work list still fills about one wave)."""
+    entries = load_table(path)["entries"]
+    entry = entries.get(bucket(batch, context, kv_heads))
+    if entry:
+        return int(entry["split_pages"])
+    entry = entries.get(bucket(batch, context))
+    if not entry:
+        return 0
+    return max(1, int(entry["split_pages"]) * kv_heads // 8)
 
 
 def candidates(old_pages_per_request: int) -> list[int]:
@@ -59,11 +68,11 @@ def candidates(old_pages_per_request: int) -> list[int]:
 
 
 def record(batch: int, context: int, results: dict[int, float], path: Path = TABLE_PATH,
-           meta: dict | None = None) -> int:
+           meta: dict | None = None, kv_heads: int = 8) -> int:
     """Store the argmin of {split_pages: p50 microseconds}."""
     best = min(results, key=results.get)
     table = load_table(path)
-    table["entries"][bucket(batch, context)] = {
+    table["entries"][bucket(batch, context, kv_heads)] = {
         "split_pages": int(best), "p50_us": results[best],
         "candidates_us": {str(k): v for k, v in sorted(results.items())}, **(meta or {})}
     path.write_text(json.dumps(table, indent=1, sort_keys=True) + "\n")
@@ -72,7 +81,8 @@ def record(batch: int, context: int, results: dict[int, float], path: Path = TAB
 
 def sweep(batch: int, context: int, repeats: int = 30, seeds=(20261001, 20261002, 20261003),
           write: bool = True, path: Path = TABLE_PATH, lengths: list[int] | None = None,
-          burst: int = 16, mode: str = "steady", layers: int = 4) -> dict[int, float]:
+          burst: int = 16, mode: str = "steady", layers: int = 4,
+          kv_heads: int = 8) -> dict[int, float]:
     """Time every candidate split on the current GPU and record the winner.
 
     ``mode="steady"`` (the default): ``layers`` caches of the shape (more
@@ -89,7 +99,10 @@ def sweep(batch: int, context: int, repeats: int = 30, seeds=(20261001, 20261002
     import torch
 
     if mode == "steady":
-        return _sweep_steady(batch, context, repeats, seeds, write, path, lengths, layers)
+        return _sweep_steady(batch, context, repeats, seeds, write, path, lengths, layers,
+                             kv_heads)
+    if kv_heads != 8:
+        raise ValueError("the burst mode sweeps 8 KV heads only")
     from .cache import build_gauge_cache, synthetic_dense_cache
     from .decode import PageGaugeDecode
 
@@ -169,7 +182,7 @@ def refinements(best: int, measured) -> list[int]:
     return sorted(out - set(measured))
 
 
-def _sweep_steady(batch, context, repeats, seeds, write, path, lengths, layers):
+def _sweep_steady(batch, context, repeats, seeds, write, path, lengths, layers, kv_heads=8):
     import torch
 
     from .cache import build_gauge_cache, synthetic_dense_cache
@@ -184,7 +197,8 @@ def _sweep_steady(batch, context, repeats, seeds, write, path, lengths, layers):
     for seed in seeds:
         caches = []
         for layer in range(layers):
-            q, dk, dv = synthetic_dense_cache(lengths, seed=seed + 7919 * layer, device="cuda")
+            q, dk, dv = synthetic_dense_cache(lengths, hkv=kv_heads, seed=seed + 7919 * layer,
+                                              device="cuda")
             cache, tables = build_gauge_cache(dk, dv, lengths)
             del dk, dv
             caches.append(cache)
@@ -197,7 +211,7 @@ def _sweep_steady(batch, context, repeats, seeds, write, path, lengths, layers):
         for q, caches, tables in setups:
             dec = PageGaugeDecode(ws)
             dec.plan(tables.old_indptr, tables.old_indices, tables.exact_indptr,
-                     tables.exact_indices, tables.exact_last_page_len, 32, 8,
+                     tables.exact_indices, tables.exact_last_page_len, 4 * kv_heads, kv_heads,
                      old_split_pages=split)
 
             def run(c):
@@ -231,9 +245,10 @@ def _sweep_steady(batch, context, repeats, seeds, write, path, lengths, layers):
         p50[split] = measure(split)
     del setups
     if write:
-        record(batch, context, p50, path=path,
+        record(batch, context, p50, path=path, kv_heads=kv_heads,
                meta={"gpu": torch.cuda.get_device_name(), "repeats": repeats,
                      "seeds": list(seeds), "lengths": lengths, "layers": layers,
+                     "kv_heads": kv_heads,
                      "mode": (f"steady: CUDA graph of {chunk} back-to-back decode steps "
                               f"(split + merge) cycling {layers} caches; coarse num_splits "
                               f"candidates, then +-20 % around the winner")})
@@ -250,6 +265,8 @@ def main() -> None:
                         help="also sweep a ragged batch of this size (contexts U[4096, 32768])")
     parser.add_argument("--table", type=Path, default=TABLE_PATH)
     parser.add_argument("--mode", choices=("steady", "burst"), default="steady")
+    parser.add_argument("--kv-heads", type=int, nargs="*", default=[8],
+                        help="KV heads per GPU (8 / tensor-parallel or head-shard degree)")
     parser.add_argument("--reset", action="store_true", help="start from an empty table")
     args = parser.parse_args()
     if args.reset and args.sweep:
@@ -257,15 +274,17 @@ def main() -> None:
     if not args.sweep:
         print(json.dumps(load_table(args.table), indent=1))
         return
-    for b in args.batch:
-        for c in args.context:
-            print(b, c, json.dumps(sweep(b, c, args.repeats, path=args.table, mode=args.mode)),
-                  flush=True)
-    if args.ragged:
-        from .shard import ragged_lengths
-        lengths = ragged_lengths(args.ragged, 20261001)
-        print("ragged", lengths, json.dumps(sweep(0, 0, args.repeats, path=args.table,
-                                                  lengths=lengths, mode=args.mode)), flush=True)
+    for h in args.kv_heads:
+        for b in args.batch:
+            for c in args.context:
+                print(b, c, h, json.dumps(sweep(b, c, args.repeats, path=args.table,
+                                                mode=args.mode, kv_heads=h)), flush=True)
+        if args.ragged:
+            from .shard import ragged_lengths
+            lengths = ragged_lengths(args.ragged, 20261001)
+            print("ragged", lengths, h, json.dumps(sweep(0, 0, args.repeats, path=args.table,
+                                                         lengths=lengths, mode=args.mode,
+                                                         kv_heads=h)), flush=True)
 
 
 if __name__ == "__main__":

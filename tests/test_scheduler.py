@@ -51,3 +51,16 @@ def test_refinements_surround_the_coarse_winner():
     r = refinements(64, [0, 48, 55, 64, 77])
     assert r == [51, 54, 58, 61, 67, 70, 74]
     assert 77 not in r and 64 not in r
+
+
+def test_kv_head_entries_and_fallback(tmp_path):
+    path = tmp_path / "t.json"
+    S.record(1, 16384, {24: 13.0, 48: 14.0}, path=path)
+    # no entry of its own: the 8-head split scaled by kv_heads / 8
+    assert S.lookup(1, 16384, path=path, kv_heads=2) == 6
+    assert S.lookup(1, 16384, path=path, kv_heads=1) == 3
+    # a measured entry for one head wins over the scaled fallback
+    S.record(1, 16384, {3: 9.0, 12: 7.5}, path=path, kv_heads=1)
+    assert S.lookup(1, 16384, path=path, kv_heads=1) == 12
+    assert S.lookup(1, 16384, path=path) == 24
+    assert S.bucket(1, 16384, 1) == "b1_c16384_h1" and S.bucket(1, 16384) == "b1_c16384"
