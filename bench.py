@@ -58,7 +58,8 @@ def parse_args():
     p.add_argument("--steps", type=int, default=2000)
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    p.add_argument("--workload", choices=("b1_49k", "b8_ragged", "b1_4k", "decoder", "gemm"),
+    p.add_argument("--workload",
+                   choices=("b1_49k", "b8_ragged", "b1_4k", "decoder", "gemm", "append"),
                    default="b1_49k")
     p.add_argument("--split", type=int, default=-1,
                    help="pages per work item (-1: measured scheduler table, 0: heuristic)")
@@ -1096,6 +1097,21 @@ def main() -> None:
 
     if args.workload == "decoder":
         run_decoder(args, dist, local)
+        if world > 1:
+            dist.barrier()
+            dist.dist.destroy_process_group()
+        return
+    if args.workload == "append":
+        # configs[3] alone: the fused append step (B=8, 32 layers) and the
+        # FP16 comparator, as in the default line's workloads.
+        app = measure_append(dist)
+        if rank == 0:
+            print(json.dumps({
+                "metric": "fused append step us (B=8, 32 layers)", "value": app["us_per_step"],
+                "unit": "us", "n_gpus": world, "higher_is_better": False,
+                "dtype": "fp16 RoPE, fp32 centring, int8 codes", "data": "synthetic",
+                "config": {"workload": "append", "batch": 8, "layers": 32},
+                "workloads": {"append_b8_32l": app}}), flush=True)
         if world > 1:
             dist.barrier()
             dist.dist.destroy_process_group()
