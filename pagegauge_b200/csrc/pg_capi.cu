@@ -716,6 +716,10 @@ int32_t pg_decode_plan(int32_t batch, int32_t kv_heads, const int32_t* indptr0,
     }
   }
   int split[2] = {split_pages0, split_pages1};
+  // A given INT8 split with an automatic FP16 split: FP16 items of the same
+  // bytes (an FP16 page moves twice an INT8 page's), so the tail does not
+  // break into many short items that push the plan past one wave.
+  if (split[0] > 0 && split[1] == 0) split[1] = std::max(1, split[0] / 2);
   if (split[0] == 0 || split[1] == 0) {
     // Automatic: minimise the estimated makespan
     //   ceil(items / resident_slots) * (pages per item + startup overhead)
