@@ -719,7 +719,7 @@ class AffineBench(AttentionBench):
             self.q = qi if self.q is None else self.q
         torch.cuda.synchronize()
         if split < 0:
-            split = scheduler.lookup(len(lengths), max(lengths))
+            split = scheduler.lookup(len(lengths), max(lengths), representation="affine_group16")
         last = torch.tensor([(n - 1) % PAGE + 1 for n in lengths], dtype=torch.int32, device="cuda")
         self.ws = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
         self.dec = PageGaugeDecode(self.ws, warps_per_cta=warps)

@@ -12,8 +12,12 @@ Public surface (mirrors the reference's operator surface):
   decode.PageGaugeDecode              fused old-INT8 + exact-FP16 + merge + c_V
   heterogeneous.run_decode()          the single-page-table ABI
   quantize.quantize_page_gauge() / quantize_completed_kv_pages()
+  quantize.quantize_pages()           the affine_group16 representation
   page_table.*                        request-major page-table helpers
-  scheduler.SplitScheduler            measured num_splits selection
+  serving.*                           paged serving pool (vLLM-side layout)
+  decoder.PageGaugeDecoder            Mistral-shaped decoder on these kernels
+  scheduler.lookup()                  measured pages per work item
+  shard.plan_shards()                 request or KV-head shards per GPU
 """
 
 __version__ = "0.1.0"

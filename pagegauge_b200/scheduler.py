@@ -11,6 +11,7 @@ behind a 256 MiB scrub instead), and the argmin is stored per (batch,
 half-octave context) bucket in ``split_table.json`` next to this file.
 
     python -m pagegauge_b200.scheduler --sweep [--batch 1 --context 49152] [--kv-heads 8 1]
+        [--representation affine_group16]
 """
 
 from __future__ import annotations
@@ -25,16 +26,24 @@ TABLE_PATH = Path(__file__).resolve().parent / "split_table.json"
 PAGE = 16
 
 
-def bucket(batch: int, context: int, kv_heads: int = 8) -> str:
+REPRESENTATIONS = ("page_gauge", "affine_group16")
+
+
+def bucket(batch: int, context: int, kv_heads: int = 8,
+           representation: str = "page_gauge") -> str:
     """Batch exact, context rounded down to a half octave (2^k or 1.5 * 2^k,
     >= 1024): bucket 2^k covers [2^k, 1.5 * 2^k), bucket 1.5 * 2^k covers
     [1.5 * 2^k, 2^(k+1)); KV heads other than 8 (a tensor-parallel or
-    head-sharded rank) get their own entries."""
+    head-sharded rank) and the affine_group16 representation (a different
+    kernel instantiation) get their own entries."""
+    if representation not in REPRESENTATIONS:
+        raise ValueError(f"unknown representation {representation!r}")
     k = max(10, int(math.floor(math.log2(max(context, 1)))))
     c = 1 << k
     if k >= 11 and context >= c + c // 2:
         c += c // 2
-    return f"b{batch}_c{c}" + ("" if kv_heads == 8 else f"_h{kv_heads}")
+    return (f"b{batch}_c{c}" + ("" if kv_heads == 8 else f"_h{kv_heads}")
+            + ("" if representation == "page_gauge" else "_affine"))
 
 
 def load_table(path: Path = TABLE_PATH) -> dict:
@@ -43,36 +52,44 @@ def load_table(path: Path = TABLE_PATH) -> dict:
     return {"entries": {}}
 
 
-def lookup(batch: int, context: int, path: Path = TABLE_PATH, kv_heads: int = 8) -> int:
+def lookup(batch: int, context: int, path: Path = TABLE_PATH, kv_heads: int = 8,
+           representation: str = "page_gauge") -> int:
     """Pages per work item for this shape; 0 (the one-wave heuristic) when
     the bucket was never measured.  With fewer than 8 KV heads and no entry
     of its own, the 8-head entry scaled by kv_heads / 8 (each head split
-    finer, so the work list still fills about one wave)."""
+    finer, so the work list still fills about one wave); affine_group16
+    without an entry of its own takes the page_gauge entry."""
     entries = load_table(path)["entries"]
-    entry = entries.get(bucket(batch, context, kv_heads))
-    if entry:
-        return int(entry["split_pages"])
-    entry = entries.get(bucket(batch, context))
-    if not entry:
-        return 0
-    return max(1, int(entry["split_pages"]) * kv_heads // 8)
+    for rep in dict.fromkeys((representation, "page_gauge")):
+        entry = entries.get(bucket(batch, context, kv_heads, rep))
+        if entry:
+            return int(entry["split_pages"])
+        entry = entries.get(bucket(batch, context, 8, rep))
+        if entry:
+            return max(1, int(entry["split_pages"]) * kv_heads // 8)
+    return 0
 
 
-def candidates(old_pages_per_request: int) -> list[int]:
+MAX_SPLIT_PAGES = 128  # the planner's cap: 32 pages per warp at 4 warps per CTA
+
+
+def candidates(old_pages_per_request: int, max_split: int = MAX_SPLIT_PAGES) -> list[int]:
     """Split sizes giving num_splits in 1..64 per (request, head), plus 0
-    for the one-wave heuristic."""
+    for the one-wave heuristic; sizes above the planner's cap would all
+    run as the cap, so the cap stands for them."""
     out = {0}
     for splits in (1, 2, 4, 8, 12, 16, 24, 32, 40, 48, 56, 64):
-        out.add(max(1, math.ceil(old_pages_per_request / splits)))
+        out.add(min(max_split, max(1, math.ceil(old_pages_per_request / splits))))
     return sorted(out)
 
 
 def record(batch: int, context: int, results: dict[int, float], path: Path = TABLE_PATH,
-           meta: dict | None = None, kv_heads: int = 8) -> int:
+           meta: dict | None = None, kv_heads: int = 8,
+           representation: str = "page_gauge") -> int:
     """Store the argmin of {split_pages: p50 microseconds}."""
     best = min(results, key=results.get)
     table = load_table(path)
-    table["entries"][bucket(batch, context, kv_heads)] = {
+    table["entries"][bucket(batch, context, kv_heads, representation)] = {
         "split_pages": int(best), "p50_us": results[best],
         "candidates_us": {str(k): v for k, v in sorted(results.items())}, **(meta or {})}
     path.write_text(json.dumps(table, indent=1, sort_keys=True) + "\n")
@@ -82,7 +99,7 @@ def record(batch: int, context: int, results: dict[int, float], path: Path = TAB
 def sweep(batch: int, context: int, repeats: int = 30, seeds=(20261001, 20261002, 20261003),
           write: bool = True, path: Path = TABLE_PATH, lengths: list[int] | None = None,
           burst: int = 16, mode: str = "steady", layers: int = 4,
-          kv_heads: int = 8) -> dict[int, float]:
+          kv_heads: int = 8, representation: str = "page_gauge") -> dict[int, float]:
     """Time every candidate split on the current GPU and record the winner.
 
     ``mode="steady"`` (the default): ``layers`` caches of the shape (more
@@ -100,9 +117,9 @@ def sweep(batch: int, context: int, repeats: int = 30, seeds=(20261001, 20261002
 
     if mode == "steady":
         return _sweep_steady(batch, context, repeats, seeds, write, path, lengths, layers,
-                             kv_heads)
-    if kv_heads != 8:
-        raise ValueError("the burst mode sweeps 8 KV heads only")
+                             kv_heads, representation)
+    if kv_heads != 8 or representation != "page_gauge":
+        raise ValueError("the burst mode sweeps 8-head page_gauge caches only")
     from .cache import build_gauge_cache, synthetic_dense_cache
     from .decode import PageGaugeDecode
 
@@ -182,10 +199,42 @@ def refinements(best: int, measured) -> list[int]:
     return sorted(out - set(measured))
 
 
-def _sweep_steady(batch, context, repeats, seeds, write, path, lengths, layers, kv_heads=8):
+def _layer_setup(lengths, seed: int, kv_heads: int, representation: str):
+    """One layer's cache for the steady sweep: (q, decode.run arguments,
+    run keywords, plan tables (old_indptr, old_indices, exact_indptr,
+    exact_indices, exact_last_page_len)).  page_gauge: the benchmark's
+    gauge cache (INT8 pages + the 256-token exact ring); affine_group16:
+    every completed page quantised by the bulk affine quantiser, the last
+    16 pages read as FP16 from the dense cache."""
+    import numpy as np
     import torch
 
     from .cache import build_gauge_cache, synthetic_dense_cache
+    from .decode import split_tables
+    from .quantize import quantize_pages
+
+    q, dk, dv = synthetic_dense_cache(lengths, hkv=kv_heads, seed=seed, device="cuda")
+    if representation == "page_gauge":
+        c, t = build_gauge_cache(dk, dv, lengths)
+        del dk, dv
+        args = (c.key_codes, c.value_codes, c.key_scales, c.value_scales, c.exact_key,
+                c.exact_value, c.value_center)
+        return q, args, {}, (t.old_indptr, t.old_indices, t.exact_indptr, t.exact_indices,
+                             t.exact_last_page_len)
+    kc, kb, ks, _ = quantize_pages(dk)
+    vc, vb, vs, _ = quantize_pages(dv)
+    o_ptr, o_idx, e_ptr, e_idx = split_tables([-(-n // PAGE) for n in lengths], 16)
+    last = torch.tensor([(n - 1) % PAGE + 1 for n in lengths], dtype=torch.int32,
+                        device="cuda")
+    tables = (o_ptr, torch.from_numpy(np.ascontiguousarray(o_idx)).cuda(), e_ptr,
+              torch.from_numpy(np.ascontiguousarray(e_idx)).cuda(), last)
+    return q, (kc, vc, ks, vs, dk, dv, None), {"affine_bias": (kb, vb)}, tables
+
+
+def _sweep_steady(batch, context, repeats, seeds, write, path, lengths, layers, kv_heads=8,
+                  representation="page_gauge"):
+    import torch
+
     from .decode import PageGaugeDecode
 
     lengths = list(lengths) if lengths is not None else [context] * batch
@@ -193,30 +242,26 @@ def _sweep_steady(batch, context, repeats, seeds, write, path, lengths, layers, 
     ws = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     stream = torch.cuda.Stream()
     chunk = 8 * layers
-    setups = []  # per seed: (q, layer caches, page tables)
+    setups = []  # per seed: (q, per-layer (run arguments, keywords), plan tables)
     for seed in seeds:
         caches = []
         for layer in range(layers):
-            q, dk, dv = synthetic_dense_cache(lengths, hkv=kv_heads, seed=seed + 7919 * layer,
-                                              device="cuda")
-            cache, tables = build_gauge_cache(dk, dv, lengths)
-            del dk, dv
-            caches.append(cache)
+            q, args, kw, tables = _layer_setup(lengths, seed + 7919 * layer, kv_heads,
+                                               representation)
+            caches.append((args, kw))
         setups.append((q, caches, tables))
     out = torch.empty_like(setups[0][0])
-    old_pages = max(t // PAGE for t in setups[0][2].old_tokens)
+    o_ptr = setups[0][2][0]
+    old_pages = max(int(o_ptr[r + 1] - o_ptr[r]) for r in range(len(lengths)))
 
     def measure(split: int) -> float:
         per_seed = []
         for q, caches, tables in setups:
             dec = PageGaugeDecode(ws)
-            dec.plan(tables.old_indptr, tables.old_indices, tables.exact_indptr,
-                     tables.exact_indices, tables.exact_last_page_len, 4 * kv_heads, kv_heads,
-                     old_split_pages=split)
+            dec.plan(*tables, 4 * kv_heads, kv_heads, old_split_pages=split)
 
             def run(c):
-                dec.run(q, c.key_codes, c.value_codes, c.key_scales, c.value_scales, c.exact_key,
-                        c.exact_value, c.value_center, out=out)
+                dec.run(q, *c[0], out=out, **c[1])
 
             with torch.cuda.stream(stream):
                 for c in caches:
@@ -241,14 +286,16 @@ def _sweep_steady(batch, context, repeats, seeds, write, path, lengths, layers, 
         return statistics.fmean(per_seed)
 
     p50 = {split: measure(split) for split in candidates(old_pages)}
-    for split in refinements(min(p50, key=p50.get), p50):
+    # Refine around the best fixed size even when the heuristic (0) wins.
+    fixed = {k: v for k, v in p50.items() if k > 0}
+    for split in refinements(min(fixed, key=fixed.get), p50) if fixed else []:
         p50[split] = measure(split)
     del setups
     if write:
-        record(batch, context, p50, path=path, kv_heads=kv_heads,
+        record(batch, context, p50, path=path, kv_heads=kv_heads, representation=representation,
                meta={"gpu": torch.cuda.get_device_name(), "repeats": repeats,
                      "seeds": list(seeds), "lengths": lengths, "layers": layers,
-                     "kv_heads": kv_heads,
+                     "kv_heads": kv_heads, "representation": representation,
                      "mode": (f"steady: CUDA graph of {chunk} back-to-back decode steps "
                               f"(split + merge) cycling {layers} caches; coarse num_splits "
                               f"candidates, then +-20 % around the winner")})
@@ -267,6 +314,7 @@ def main() -> None:
     parser.add_argument("--mode", choices=("steady", "burst"), default="steady")
     parser.add_argument("--kv-heads", type=int, nargs="*", default=[8],
                         help="KV heads per GPU (8 / tensor-parallel or head-shard degree)")
+    parser.add_argument("--representation", choices=REPRESENTATIONS, default="page_gauge")
     parser.add_argument("--reset", action="store_true", help="start from an empty table")
     args = parser.parse_args()
     if args.reset and args.sweep:
@@ -278,13 +326,17 @@ def main() -> None:
         for b in args.batch:
             for c in args.context:
                 print(b, c, h, json.dumps(sweep(b, c, args.repeats, path=args.table,
-                                                mode=args.mode, kv_heads=h)), flush=True)
+                                                mode=args.mode, kv_heads=h,
+                                                representation=args.representation)),
+                      flush=True)
         if args.ragged:
             from .shard import ragged_lengths
             lengths = ragged_lengths(args.ragged, 20261001)
             print("ragged", lengths, h, json.dumps(sweep(0, 0, args.repeats, path=args.table,
                                                          lengths=lengths, mode=args.mode,
-                                                         kv_heads=h)), flush=True)
+                                                         kv_heads=h,
+                                                         representation=args.representation)),
+                  flush=True)
 
 
 if __name__ == "__main__":

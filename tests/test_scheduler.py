@@ -40,8 +40,11 @@ def test_record_keeps_the_argmin(tmp_path):
 
 def test_candidates_span_one_to_64_splits():
     c = S.candidates(3056)
-    assert c[0] == 0 and 3056 in c and 48 in c and 64 in c
+    assert c[0] == 0 and 48 in c and 64 in c
     assert all(-(-3056 // s) <= 64 for s in c if s)
+    # sizes above the planner's 128-page cap collapse onto it
+    assert max(c) == S.MAX_SPLIT_PAGES == 128 and 3056 not in c
+    assert S.candidates(100) == sorted({0, 100, 50, 25, 13, 9, 7, 5, 4, 3, 2})
 
 
 def test_refinements_surround_the_coarse_winner():
@@ -64,3 +67,20 @@ def test_kv_head_entries_and_fallback(tmp_path):
     assert S.lookup(1, 16384, path=path, kv_heads=1) == 12
     assert S.lookup(1, 16384, path=path) == 24
     assert S.bucket(1, 16384, 1) == "b1_c16384_h1" and S.bucket(1, 16384) == "b1_c16384"
+
+
+def test_representation_entries_and_fallback(tmp_path):
+    path = tmp_path / "t.json"
+    S.record(1, 49152, {64: 20.0, 70: 19.5}, path=path)
+    # affine_group16 without an entry of its own takes the page_gauge split
+    assert S.lookup(1, 49152, path=path, representation="affine_group16") == 70
+    S.record(1, 49152, {48: 24.0, 56: 23.0}, path=path, representation="affine_group16")
+    assert S.lookup(1, 49152, path=path, representation="affine_group16") == 56
+    assert S.lookup(1, 49152, path=path) == 70
+    assert S.bucket(1, 49152, 8, "affine_group16") == "b1_c49152_affine"
+    assert S.bucket(1, 49152, 2, "affine_group16") == "b1_c49152_h2_affine"
+    # fewer heads: the representation's own 8-head entry, scaled
+    assert S.lookup(1, 49152, path=path, kv_heads=4, representation="affine_group16") == 28
+    import pytest
+    with pytest.raises(ValueError):
+        S.bucket(1, 49152, representation="fp8")
