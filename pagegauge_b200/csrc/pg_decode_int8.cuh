@@ -18,19 +18,21 @@ __device__ __forceinline__ int clamp127(int v) { return v < -127 ? -127 : (v > 1
 
 // Three-part int8 Q for the INT8 segment, computed once per CTA into the
 // shared table (all warps call this after the query is final, then read
-// their fragments).  Warp w splits the row slots g = w, w + W, ... of the
-// eight mma lane groups: GQA <= 4, slots g and g + 4 both split query row
-// g & 3, slot g keeping (hi, lo) and slot g + 4 (lo2, 0); WIDE, slot g
-// splits row g into (hi, lo) and the second-MMA register lo2.  Lane l of
-// the warp owns the 4 dims 4l..4l+3 = (t, ks, half) = (l / 8, (l / 2) % 4,
-// l % 2) of the fragment order described at QInt8.
+// their fragments).  GQA <= 4: warp w splits query rows g = w, w + W, ...
+// (< 4) and writes two of the eight mma lane-group slots, slot g with
+// (hi, lo) and slot g + 4 with (lo2, 0), so each row is loaded and split
+// once (this runs after the dependency wait, on every launch's critical
+// path); WIDE: warp w splits rows g = w, w + W, ... (< 8), slot g holding
+// (hi, lo) and the second-MMA register lo2.  Lane l of the warp owns the
+// 4 dims 4l..4l+3 = (t, ks, half) = (l / 8, (l / 2) % 4, l % 2) of the
+// fragment order described at QInt8.
 template <bool WIDE>
 __device__ __forceinline__ void split_q_cta(const DecodeParams& p, int r, int h, int warp,
                                             int W, int lane, QFragTable* tab) {
   const int t = lane >> 3, ks = (lane >> 1) & 3, half = lane & 1;
-  for (int g = warp; g < 8; g += W) {
-    const int row = WIDE ? g : (g & 3);
-    const bool second = !WIDE && g >= 4;
+  constexpr int kRows = WIDE ? 8 : 4;
+  for (int g = warp; g < kRows; g += W) {
+    const int row = g;
     float x[4] = {0.f, 0.f, 0.f, 0.f};
     if (row < p.group) {
       // Rows are 4-byte aligned (the C ABI's guarantee): half2 loads.
@@ -67,16 +69,19 @@ __device__ __forceinline__ void split_q_cta(const DecodeParams& p, int r, int h,
     const uint32_t pl = pack_s8x4(lv[0], lv[1], lv[2], lv[3]);
     const uint32_t p2 = pack_s8x4(l2[0], l2[1], l2[2], l2[3]);
     uint32_t* a = tab->a[4 * g + t] + 4 * ks + 2 * half;
+    a[0] = ph;
+    a[1] = pl;
     if constexpr (WIDE) {
-      a[0] = ph;
-      a[1] = pl;
       tab->a2[4 * g + t][2 * ks + half] = p2;
     } else {
-      a[0] = second ? p2 : ph;
-      a[1] = second ? 0u : pl;
+      uint32_t* b = tab->a[4 * (g + 4) + t] + 4 * ks + 2 * half;
+      b[0] = p2;
+      b[1] = 0u;
     }
-    if ((lane & 7) == 0)
-      tab->c[4 * g + t] = (second || row >= p.group) ? 0.f : sq * (p.sm_scale_log2 / 64516.f);
+    if ((lane & 7) == 0) {
+      tab->c[4 * g + t] = row >= p.group ? 0.f : sq * (p.sm_scale_log2 / 64516.f);
+      if constexpr (!WIDE) tab->c[4 * (g + 4) + t] = 0.f;
+    }
   }
   __syncthreads();
 }

@@ -591,7 +591,6 @@ __global__ void __launch_bounds__(kTpReduceThreads)
   const int32_t* seq = reinterpret_cast<const int32_t*>(p.exchange + tp_seq_offset(cap));
   const uint2* recv = reinterpret_cast<const uint2*>(p.exchange + tp_recv_offset(cap));
   const int n = p.tiles * kGemmTileRows;
-  const int batch = gridDim.x;
   // Thread-owned 8-column chunks, as the add_rmsnorm kernel.
   constexpr int kMaxChunks = 4;  // n <= 4 * 8 * 512
   uint4 x[kMaxChunks];
