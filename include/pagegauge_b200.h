@@ -87,9 +87,14 @@ int32_t pg_tp_exchange_destroy(void* buffer);
 /* Publish this rank's partial product computed by another GEMM (FP16
  * src [batch, tiles * 64], e.g. cuBLAS's row-parallel o_proj / down_proj
  * output) to every rank's exchange buffer (peers[r] = rank r's buffer as
- * mapped here) in the format a tensor-parallel pg_skinny_gemm publishes,
- * so that pg_tp_reduce replaces the all-reduce (and the residual add +
- * RMSNorm after it).  Every rank must launch the same sequence.           */
+ * mapped here), so that pg_tp_reduce with PG_TP_PAYLOAD_F16 replaces the
+ * all-reduce (and the residual add + RMSNorm after it).  The values travel
+ * as FP16 pairs, half the bytes of the FP32 tiles a tensor-parallel
+ * pg_skinny_gemm publishes.  Every rank must launch the same sequence.    */
+enum {
+  PG_TP_PAYLOAD_F32 = 0, /* tiles published by a tensor-parallel pg_skinny_gemm */
+  PG_TP_PAYLOAD_F16 = 1  /* tiles published by pg_tp_publish */
+};
 int32_t pg_tp_publish(void* const* peers, int32_t world, int32_t rank, int32_t tiles_cap,
                       int32_t tiles, int32_t batch, const void* src, int64_t src_stride,
                       void* stream);
@@ -104,11 +109,14 @@ int32_t pg_tp_publish(void* const* peers, int32_t world, int32_t rank, int32_t t
  *   residual != NULL: residual = f16(residual + f16(sum)), then out =
  *                     RMSNorm(residual) with norm_weight (MistralRMSNorm),
  *                     or out = residual without it
- *   residual == NULL: out = f16(sum)                                       */
+ *   residual == NULL: out = f16(sum)
+ * payload names the publisher of the tiles: PG_TP_PAYLOAD_F32 after a
+ * tensor-parallel pg_skinny_gemm, PG_TP_PAYLOAD_F16 after pg_tp_publish
+ * (every rank of one exchange uses the same publisher).                   */
 int32_t pg_tp_reduce(const void* exchange, int32_t world, int32_t tiles_cap, int32_t tiles,
                      int32_t batch, void* residual, int64_t residual_stride,
                      const void* norm_weight, float eps, void* out, int64_t out_stride,
-                     void* stream);
+                     int32_t payload, void* stream);
 
 /* Device address of a page-locked, mapped host buffer (cudaHostAlloc /
  * pinned memory): kernels may take it wherever an input or output pointer

@@ -80,7 +80,7 @@ _SIGNATURES = {
     "pg_tp_publish": (c_i32, [ctypes.POINTER(c_vp), c_i32, c_i32, c_i32, c_i32, c_i32, c_vp,
                               c_i64, c_vp]),
     "pg_tp_reduce": (c_i32, [c_vp, c_i32, c_i32, c_i32, c_i32, c_vp, c_i64, c_vp, ctypes.c_float,
-                             c_vp, c_i64, c_vp]),
+                             c_vp, c_i64, c_i32, c_vp]),
     "pg_rope_append_fp16": (c_i32, [c_vp] * 8 + [c_i64] * 3 + [c_i32] * 3 + [c_i64, c_i64, c_vp, c_i64, c_i64, c_vp]),
     "pg_rope_append_page_gauge": (
         c_i32,

@@ -240,7 +240,7 @@ extern "C" {
 
 const char* pg_last_error(void) { return g_last_error.c_str(); }
 
-int32_t pg_abi_version(void) { return 107; }
+int32_t pg_abi_version(void) { return 108; }
 
 int64_t pg_tp_exchange_bytes(int32_t tiles_cap) {
   return tiles_cap > 0 ? pg::tp_exchange_bytes(tiles_cap) : -1;
@@ -1344,8 +1344,11 @@ int32_t pg_tp_publish(void* const* peers, int32_t world, int32_t rank, int32_t t
 int32_t pg_tp_reduce(const void* exchange, int32_t world, int32_t tiles_cap, int32_t tiles,
                      int32_t batch, void* residual, int64_t residual_stride,
                      const void* norm_weight, float eps, void* out, int64_t out_stride,
-                     void* stream) {
+                     int32_t payload, void* stream) {
   PG_REQUIRE(exchange != nullptr && aligned(exchange, 256), "the exchange buffer is required");
+  PG_REQUIRE(payload == PG_TP_PAYLOAD_F32 || payload == PG_TP_PAYLOAD_F16,
+             "payload must be PG_TP_PAYLOAD_F32 (a publishing pg_skinny_gemm) or "
+             "PG_TP_PAYLOAD_F16 (pg_tp_publish)");
   PG_REQUIRE(world >= 2 && world <= pg::kGemmMaxTp, "world must be 2..8");
   PG_REQUIRE(tiles >= 1 && tiles <= tiles_cap && tiles * pg::kGemmTileRows <= 16384,
              "tiles must be 1..tiles_cap with at most 16384 columns");
@@ -1371,7 +1374,10 @@ int32_t pg_tp_reduce(const void* exchange, int32_t world, int32_t tiles_cap, int
   p.out = static_cast<__half*>(out);
   p.out_stride = out_stride;
   p.error_flag = device_error_ptr();
-  return launch_pdl(pg::pg_tp_reduce_kernel, dim3(batch), dim3(pg::kTpReduceThreads), 0,
+  if (payload == PG_TP_PAYLOAD_F16)
+    return launch_pdl(pg::pg_tp_reduce_kernel<true>, dim3(batch), dim3(pg::kTpReduceThreads), 0,
+                      static_cast<cudaStream_t>(stream), "tp reduce launch", p);
+  return launch_pdl(pg::pg_tp_reduce_kernel<false>, dim3(batch), dim3(pg::kTpReduceThreads), 0,
                     static_cast<cudaStream_t>(stream), "tp reduce launch", p);
 }
 

@@ -202,6 +202,17 @@ __device__ __forceinline__ void st_pairs2_relaxed_sys(uint2* p, float v0, float 
                : "memory");
 }
 
+// Two 8-byte words {v0, tag}, {v1, tag} in one store (v0 / v1: raw bits,
+// e.g. an FP16 pair).
+__device__ __forceinline__ void st_words2_relaxed_sys(uint2* p, uint32_t v0, uint32_t v1,
+                                                      int32_t tag) {
+  const unsigned long long t = static_cast<unsigned long long>(static_cast<uint32_t>(tag)) << 32;
+  const unsigned long long x = static_cast<unsigned long long>(v0) | t;
+  const unsigned long long y = static_cast<unsigned long long>(v1) | t;
+  asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(x), "l"(y)
+               : "memory");
+}
+
 __device__ __forceinline__ uint2 ld_pair_relaxed_sys(const uint2* p) {
   unsigned long long v;
   asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
@@ -516,11 +527,14 @@ __global__ void __launch_bounds__(kGemmWarps * 32)
 }
 
 // Publication of a partial product computed elsewhere (a library GEMM's
-// FP16 output [batch, tiles * 64]) in the exchange format of
-// gemm_tp_push: one CTA per output tile stores the tile's values, each
-// paired with the tile's exchange count, into every rank's exchange buffer
-// (this rank's own included), then advances the count.  pg_tp_reduce then
-// sums the ranks' tiles exactly as after a publishing skinny GEMM.
+// FP16 output [batch, tiles * 64]): one CTA per output tile stores the
+// tile's values into every rank's exchange buffer (this rank's own
+// included), then advances the count.  The values are already FP16, so
+// each 8-byte word carries an FP16 pair with the tile's exchange count as
+// its tag (row b's pairs at b * 64 + j / 2 of the slot): half the bytes of
+// the FP32 pairs gemm_tp_push sends, which matters when every rank sends
+// every other rank a [32, 4096] partial.  pg_tp_reduce (FP16 payload) then
+// sums the same FP16 values in FP32 in rank order.
 struct TpPublishParams {
   uint8_t* peers[kGemmMaxTp];
   int32_t world, rank, cap, batch;
@@ -542,17 +556,17 @@ __global__ void __launch_bounds__(kTpPublishThreads)
   __syncthreads();
   const int32_t seq = s_seq;
   const int64_t slot = (static_cast<int64_t>(seq & 1) * kGemmMaxTp + p.rank) * cap + tile;
-  // Two values per 16-byte store: 32 pairs of columns per row.
-  const int n2 = kGemmTileRows / 2 * p.batch;
-  for (int i = threadIdx.x; i < n2; i += blockDim.x) {
-    const int b = i / (kGemmTileRows / 2), j = 2 * (i - b * (kGemmTileRows / 2));
-    const __half2 v = *reinterpret_cast<const __half2*>(p.src + b * p.src_stride +
-                                                        tile * kGemmTileRows + j);
-    const float2 f = __half22float2(v);
+  // Four columns (two FP16 pairs) per 16-byte store: 16 stores per row.
+  const int n4 = kGemmTileRows / 4 * p.batch;
+  for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+    const int b = i / (kGemmTileRows / 4), j = 4 * (i - b * (kGemmTileRows / 4));
+    const __half* src = p.src + b * p.src_stride + tile * kGemmTileRows + j;
+    const uint32_t v0 = *reinterpret_cast<const uint32_t*>(src);
+    const uint32_t v1 = *reinterpret_cast<const uint32_t*>(src + 2);
     for (int dst = 0; dst < p.world; ++dst) {
       uint2* out = reinterpret_cast<uint2*>(p.peers[dst] + tp_recv_offset(cap)) +
                    slot * tp_slot_pairs();
-      st_pairs2_relaxed_sys(out + b * kGemmTileRows + j, f.x, f.y, seq);
+      st_words2_relaxed_sys(out + b * kGemmTileRows + j / 2, v0, v1, seq);
     }
   }
   __syncthreads();
@@ -561,7 +575,9 @@ __global__ void __launch_bounds__(kTpPublishThreads)
 
 // Consumer of a tensor-parallel GEMM's published tiles: one CTA of 512
 // threads per batch row b.  It waits (bounded) until every rank's tile of
-// every output tile has arrived, sums them in rank order in FP32 and then
+// every output tile has arrived (F16: the FP16-pair words of
+// pg_tp_publish; else the FP32 pairs of gemm_tp_push), sums them in rank
+// order in FP32 and then
 //   residual != null: r = f16(r + f16(sum)); with norm_w, out = RMSNorm(r)
 //   residual == null: out = f16(sum)
 // (the all-reduce and the decoder's residual add + RMSNorm in one launch).
@@ -580,7 +596,8 @@ struct TpReduceParams {
 constexpr int kTpReduceThreads = 512;
 constexpr uint64_t kTpWaitNs = 1000000000ull;  // a peer's tiles: wait about a second
 
-__global__ void __launch_bounds__(kTpReduceThreads)
+template <bool F16>
+__global__ void __launch_bounds__(kTpReduceThreads, 1)
     pg_tp_reduce_kernel(const __grid_constant__ TpReduceParams p) {
   __shared__ float part[kTpReduceThreads / 32];
   pdl_launch_dependents();
@@ -612,25 +629,26 @@ __global__ void __launch_bounds__(kTpReduceThreads)
     // count (not arrived) are re-read, for about a second at most.  The
     // sum runs in rank order, identical on every rank.
     constexpr int kSrcBatch = 4;
+    constexpr int NP = F16 ? 4 : 8;  // words per 8-column chunk and rank
     for (int s0 = 0; s0 < p.world; s0 += kSrcBatch) {
-      uint2 v[kSrcBatch][8];
+      uint2 v[kSrcBatch][NP];
       const uint2* rows[kSrcBatch];
 #pragma unroll
       for (int k = 0; k < kSrcBatch; ++k) {
         const int src = s0 + k;
         rows[k] = recv + ((static_cast<int64_t>(par) * kGemmMaxTp + src) * cap + t) *
                              tp_slot_pairs() +
-                  b * kGemmTileRows + j0;  // 8 contiguous pairs (64 B)
+                  b * kGemmTileRows + (F16 ? j0 / 2 : j0);  // NP contiguous words
         if (src < p.world) {
 #pragma unroll
-          for (int e = 0; e < 8; e += 2) ld_pairs2_relaxed_sys(rows[k] + e, v[k][e], v[k][e + 1]);
+          for (int e = 0; e < NP; e += 2) ld_pairs2_relaxed_sys(rows[k] + e, v[k][e], v[k][e + 1]);
         }
       }
 #pragma unroll
       for (int k = 0; k < kSrcBatch; ++k) {
         if (s0 + k >= p.world) break;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
+        for (int e = 0; e < NP; ++e) {
           for (uint32_t spin = 0; ok && static_cast<int32_t>(v[k][e].y) != want; ++spin) {
             // About a second from the kernel's start (2^26 polls as a backstop).
             if (spin == (1u << 26) ||
@@ -641,7 +659,14 @@ __global__ void __launch_bounds__(kTpReduceThreads)
             __nanosleep(32);
             v[k][e] = ld_pair_relaxed_sys(rows[k] + e);
           }
-          d[e] += __uint_as_float(v[k][e].x);
+          if constexpr (F16) {
+            const uint32_t bits = v[k][e].x;
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&bits));
+            d[2 * e] += f.x;
+            d[2 * e + 1] += f.y;
+          } else {
+            d[e] += __uint_as_float(v[k][e].x);
+          }
         }
       }
     }

@@ -7,7 +7,9 @@ is involved: the projection GEMM publishes every finished FP32 output tile
 into every rank's exchange buffer as soon as the tile is done (plain peer
 stores over NVLink, every value tagged with the exchange count, so the
 transfer overlaps the rest of the GEMM), or ``publish`` does the same for a
-partial another GEMM (cuBLAS) wrote; the next kernel on each rank waits
+partial another GEMM (cuBLAS) wrote, as FP16 pairs (half the bytes, since
+every rank sends its whole partial to every other rank); the next kernel
+on each rank waits
 (bounded) for all ranks' tiles, sums them in rank order and applies the
 residual add and RMSNorm (``reduce``).  This module allocates one
 exchange buffer per rank (CUDA IPC), shares the handles over the process
@@ -21,6 +23,10 @@ import ctypes
 import torch
 
 from . import _lib
+
+# pg_tp_reduce's payload argument (PG_TP_PAYLOAD_* in the C header).
+PAYLOAD_F32 = 0  # tiles published by a tensor-parallel streaming GEMM
+PAYLOAD_F16 = 1  # tiles published by pg_tp_publish
 
 
 class TpExchange:
@@ -66,12 +72,16 @@ class TpExchange:
             raise
         dist.barrier(group=process_group)
         self.closed = False
+        # Format of the tiles the next reduce sums: FP32 pairs from a
+        # publishing streaming GEMM (``fill``), FP16 pairs from ``publish``.
+        self.payload = PAYLOAD_F32
 
     def fill(self, args) -> None:
         """Set the tensor-parallel fields of a PgGemmArgs."""
         args.tp_world, args.tp_rank, args.tp_tiles_cap = self.world, self.rank, self.tiles_cap
         for r, ptr in enumerate(self.peers):
             args.tp_peers[r] = ptr
+        self.payload = PAYLOAD_F32
 
     def publish(self, src: torch.Tensor) -> None:
         """Publish this rank's partial product computed by another GEMM
@@ -86,6 +96,7 @@ class TpExchange:
         _lib.check(_lib.load().pg_tp_publish(
             peers, self.world, self.rank, self.tiles_cap, src.shape[1] // 64, src.shape[0],
             src.data_ptr(), src.stride(0), torch.cuda.current_stream(src.device).cuda_stream))
+        self.payload = PAYLOAD_F16
 
     def reduce(self, batch: int, residual: torch.Tensor | None, norm_weight: torch.Tensor | None,
                eps: float, out: torch.Tensor, tiles: int | None = None) -> torch.Tensor:
@@ -107,7 +118,8 @@ class TpExchange:
             None if residual is None else residual.data_ptr(),
             0 if residual is None else residual.stride(0),
             None if norm_weight is None else norm_weight.data_ptr(), float(eps),
-            out.data_ptr(), out.stride(0), torch.cuda.current_stream(out.device).cuda_stream))
+            out.data_ptr(), out.stride(0), self.payload,
+            torch.cuda.current_stream(out.device).cuda_stream))
         return out
 
     def _release(self) -> None:

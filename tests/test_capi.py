@@ -48,7 +48,7 @@ def test_struct_sizes_match_header_layout(lib):
     assert tuple(sizes) == (ctypes.sizeof(_lib.PgDecodeArgs), ctypes.sizeof(_lib.PgGemmArgs),
                             ctypes.sizeof(_lib.PgSegment), ctypes.sizeof(_lib.PgPlanInfo),
                             ctypes.sizeof(_lib.PgDecodeItem))
-    assert lib.pg_abi_version() == 107
+    assert lib.pg_abi_version() == 108
 
 
 def test_planner_chunks_and_offsets(lib):
@@ -112,6 +112,13 @@ def test_tp_publish_validation_without_gpu(lib):
     assert b"batch must be 1..32" in lib.pg_last_error()
     assert lib.pg_tp_publish(peers, 2, 0, 64, 64, 1, src, 4000, None) == 1
     assert b"src must be fp16" in lib.pg_last_error()
+
+
+def test_tp_reduce_payload_validation_without_gpu(lib):
+    ex = ctypes.c_void_p(0x10000)
+    assert lib.pg_tp_reduce(ex, 2, 64, 64, 1, None, 0, None, 1e-5, ctypes.c_void_p(0x20000),
+                            4096, 2, None) == 1
+    assert b"payload must be PG_TP_PAYLOAD_F32" in lib.pg_last_error()
 
 
 def _decode_items(items):

@@ -20,6 +20,7 @@ from pagegauge_b200.runtime import read_device_error
 pytestmark = pytest.mark.gpu
 
 PG_DEV_WAIT_TIMEOUT = 1
+PG_TP_PAYLOAD_F16 = 1  # tiles published by pg_tp_publish
 
 
 def test_tp_reduce_gives_up_when_a_rank_never_publishes(cuda_lib):
@@ -41,7 +42,8 @@ def test_tp_reduce_gives_up_when_a_rank_never_publishes(cuda_lib):
         torch.cuda.synchronize()
         t0 = time.perf_counter()
         _lib.check(lib.pg_tp_reduce(own, 2, tiles, tiles, batch, residual.data_ptr(), n,
-                                    norm_w.data_ptr(), 1e-5, out.data_ptr(), n, stream))
+                                    norm_w.data_ptr(), 1e-5, out.data_ptr(), n,
+                                    PG_TP_PAYLOAD_F16, stream))
         torch.cuda.synchronize()
         waited = time.perf_counter() - t0
         assert read_device_error() == PG_DEV_WAIT_TIMEOUT
