@@ -80,12 +80,23 @@ __device__ __forceinline__ uint32_t hadd2_rn(uint32_t a, uint32_t b) {
   return r;
 }
 
+// A 4-byte word of the new token's q / k / v.  These rows may sit in
+// mapped host memory (zero copy, pg_host_device_pointer): ld.cv fetches
+// the word over the host link on every call instead of reusing a line an
+// earlier launch left in the L2, so each step reads its own inputs.  For
+// device memory it is an ordinary L2 load (each word is read once).
+__device__ __forceinline__ uint32_t ld_input(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.global.cv.u32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+
 // HF rotate-half RoPE for the dims (2j, 2j+1) of one 128-wide head.
 __device__ __forceinline__ uint32_t rope_pair(const __half* head, int j,
                                               uint32_t c, uint32_t s) {
   const uint32_t* h32 = reinterpret_cast<const uint32_t*>(head);
-  const uint32_t x = h32[j];
-  uint32_t partner = h32[(j + 32) & 63];
+  const uint32_t x = ld_input(h32 + j);
+  uint32_t partner = ld_input(h32 + ((j + 32) & 63));
   if (j < 32) partner ^= 0x80008000u;  // -x[d + 64] for d < 64
   return hadd2_rn(hmul2_rn(x, c), hmul2_rn(partner, s));
 }
@@ -174,19 +185,19 @@ __device__ __forceinline__ AppendInputs load_append_inputs(const AppendParams& p
   if (in.qh < p.hq) {
     const uint32_t* q32 = reinterpret_cast<const uint32_t*>(
         p.q + r * p.q_stride_b + static_cast<int64_t>(in.qh) * kHeadDim);
-    in.q = q32[j];
-    in.qpartner = q32[(j + 32) & 63];
+    in.q = ld_input(q32 + j);
+    in.qpartner = ld_input(q32 + ((j + 32) & 63));
   } else {
     in.qh = -1;
   }
   if (g == 0) {
     const uint32_t* k32 = reinterpret_cast<const uint32_t*>(
         p.k + r * p.k_stride_b + static_cast<int64_t>(h) * kHeadDim);
-    in.x = k32[j];
-    in.partner = k32[(j + 32) & 63];
+    in.x = ld_input(k32 + j);
+    in.partner = ld_input(k32 + ((j + 32) & 63));
   } else if (g == 1) {
-    in.x = reinterpret_cast<const uint32_t*>(
-        p.v + r * p.v_stride_b + static_cast<int64_t>(h) * kHeadDim)[j];
+    in.x = ld_input(reinterpret_cast<const uint32_t*>(
+                        p.v + r * p.v_stride_b + static_cast<int64_t>(h) * kHeadDim) + j);
   }
   return in;
 }
@@ -314,13 +325,13 @@ __global__ void __launch_bounds__(kAppendThreads)
     const uint32_t* src = reinterpret_cast<const uint32_t*>(
         (role == 0 ? p.k + r * p.k_stride_b : p.v + r * p.v_stride_b) +
         static_cast<int64_t>(h) * kHeadDim);
-    x = src[j];
-    if (role == 0) partner = src[(j + 32) & 63];
+    x = ld_input(src + j);
+    if (role == 0) partner = ld_input(src + ((j + 32) & 63));
   } else if (qh < p.hq) {
     const uint32_t* q32 = reinterpret_cast<const uint32_t*>(
         p.q + r * p.q_stride_b + static_cast<int64_t>(qh) * kHeadDim);
-    qx = q32[j];
-    qpartner = q32[(j + 32) & 63];
+    qx = ld_input(q32 + j);
+    qpartner = ld_input(q32 + ((j + 32) & 63));
   }
   int64_t crow = r;
   if constexpr (SERVED) {
