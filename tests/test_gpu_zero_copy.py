@@ -21,7 +21,8 @@ def test_graph_replays_see_rewritten_host_rows(cuda_lib):
     ext = load_append_extension()
     lengths = [300, 200]  # positions 299 / 199: no page closes
     _, dk, dv = synthetic_dense_cache(lengths, seed=20261001, device="cuda")
-    cache, _ = build_gauge_cache(dk, dv, lengths)
+    # The batched append addresses request r's code pages at r * capacity.
+    cache, _ = build_gauge_cache(dk, dv, lengths, capacity_pages=24)
     cos, sin = rope_tables(1024, device="cuda")
     positions = torch.tensor([n - 1 for n in lengths], dtype=torch.int32, device="cuda")
     B, hq, hkv = len(lengths), 32, 8
@@ -54,6 +55,7 @@ def test_graph_replays_see_rewritten_host_rows(cuda_lib):
             t.copy_(torch.randn(t.shape, generator=g).half())  # host writes
         graph.replay()
         torch.cuda.synchronize()
+        assert read_device_error() == 0
         got_q = rq.clone()
         got_ring = [cache.exact_key[16 * r + ring_pages[r]].clone() for r in range(B)]
         append(hq_rows.cuda(), hk_rows.cuda(), hv_rows.cuda(), rq_ref)
