@@ -1148,7 +1148,12 @@ int32_t gemm_shape(int32_t n, int32_t k, int32_t batch, int32_t mode, int32_t gr
   g.kblocks = k / pg::kGemmBK;
   const int64_t total = static_cast<int64_t>(g.tiles) * g.kblocks;
   const int64_t slots = static_cast<int64_t>(std::max(num_sms, 1)) * gemm_ctas_per_sm(gemm_nt(batch));
-  int64_t grid_n = std::min<int64_t>(total, grid > 0 ? grid : slots);
+  // Default grid: every resident CTA slot, except for narrow shapes (at
+  // most 1024 weight blocks of 64 x 64, e.g. a tensor-parallel rank's
+  // qkv / o projection at TP8), which one CTA per SM streams faster
+  // (TP8 B=1: qkv 7.55 -> 6.75 us, o 7.16 -> 5.96 us).
+  const int64_t fallback = total <= 1024 ? std::max(num_sms, 1) : slots;
+  int64_t grid_n = std::min<int64_t>(total, grid > 0 ? grid : fallback);
   // At most 16 CTAs may share a tile (the finishing CTA's slot table).
   while (grid_n > 1 && (g.kblocks + total / grid_n - 1) / (total / grid_n) + 1 > pg::kGemmMaxContrib)
     --grid_n;

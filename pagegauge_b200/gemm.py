@@ -50,10 +50,11 @@ class SkinnyGemm:
         self.partials = torch.empty(partial_floats, dtype=torch.float32, device=self.device)
         self.counters = torch.zeros(counters, dtype=torch.int32, device=self.device)
 
-    def reserve(self, n: int, k: int, batch: int, mode: int = STORE) -> None:
-        """Grow the scratch for a shape (host-side; outside graph capture)."""
+    def reserve(self, n: int, k: int, batch: int, mode: int = STORE, grid: int = 0) -> None:
+        """Grow the scratch for a shape launched with ``grid`` CTAs (0: the
+        default, one per resident slot) (host-side; outside graph capture)."""
         floats, tiles = ctypes.c_int64(0), ctypes.c_int32(0)
-        _lib.check(_lib.load().pg_skinny_gemm_workspace(n, k, batch, mode, 0, self.sms,
+        _lib.check(_lib.load().pg_skinny_gemm_workspace(n, k, batch, mode, grid, self.sms,
                                                         ctypes.byref(floats), ctypes.byref(tiles)))
         if floats.value > self.partials.numel():
             self.partials = torch.empty(floats.value, dtype=torch.float32, device=self.device)
