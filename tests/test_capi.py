@@ -167,3 +167,27 @@ def test_planner_fixed_split_sizes_items(lib):
     counts = [c for *_, c, _ in _decode_items(items)[:off[1]]]
     assert counts == [30, 30, 30, 10]
     assert info.split_pages[0] == 30
+
+
+def test_gemm_default_grid_without_gpu(lib):
+    """The streaming GEMM's default grid (seen through its scratch size,
+    grid x segments x 64 x 8 floats): one CTA per SM for a narrow shape
+    (<= 1024 weight blocks, e.g. a TP8 rank's qkv), every resident slot
+    (3 per SM at one row) otherwise."""
+    floats, tiles = ctypes.c_int64(0), ctypes.c_int32(0)
+    # TP8 qkv: 12 tiles x 64 k-blocks = 768 blocks -> 148 CTAs, 2 segments each.
+    assert lib.pg_skinny_gemm_workspace(768, 4096, 1, 0, 0, 148, ctypes.byref(floats),
+                                        ctypes.byref(tiles)) == 0
+    assert floats.value == 148 * 2 * 64 * 8
+    # o at TP1: 64 tiles x 64 k-blocks = 4096 blocks -> 444 CTAs.
+    assert lib.pg_skinny_gemm_workspace(4096, 4096, 1, 1, 0, 148, ctypes.byref(floats),
+                                        ctypes.byref(tiles)) == 0
+    assert floats.value == 444 * 2 * 64 * 8
+    # An explicit grid is kept ...
+    assert lib.pg_skinny_gemm_workspace(768, 4096, 1, 0, 100, 148, ctypes.byref(floats),
+                                        ctypes.byref(tiles)) == 0
+    assert floats.value == 100 * 2 * 64 * 8
+    # ... unless more than 16 CTAs would share a tile (296 -> 153 here).
+    assert lib.pg_skinny_gemm_workspace(768, 4096, 1, 0, 296, 148, ctypes.byref(floats),
+                                        ctypes.byref(tiles)) == 0
+    assert floats.value == 153 * 2 * 64 * 8
