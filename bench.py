@@ -19,10 +19,16 @@ under ``workloads``, measured in the same run (``--only`` skips them):
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload b1_49k|b8_ragged|b1_4k|decoder|gemm] [--split PAGES] [--only]
 
+``e2e`` is the same step through the public API with host buffers: the
+append reads each step's q/k/v from page-locked host memory and the decode
+writes the output there, every step, in CUDA graphs of 32 steps (plus the
+remainder), exactly K steps timed.
+
 Multi-GPU (torchrun, one process per GPU): B1/49K and B1/4K run one replica
-per rank (weak scaling, no data-path collective); B8 ragged shards its 8
-requests over the ranks by longest-first bin packing on decode bytes (strong
-scaling, no data-path collective); the decoder is tensor-parallel by KV head.
+per rank (weak scaling, no data-path collective); B8 ragged splits its 8
+requests over the ranks by request (longest-first bin packing on decode
+bytes) or by KV head, whichever balances the bytes (strong scaling, no
+data-path collective); the decoder is tensor-parallel by KV head.
 ``value`` is the whole-job bytes/s: all ranks' bytes over the max-over-ranks
 device time.
 """
