@@ -637,11 +637,14 @@ class AttentionBench:
         hv = hqkv[:, (HQ + HKV) * DIM:].view(B, HKV, DIM)
 
         def one_zero_copy(layer: int):
+            # The host rows are written before the graph and by no kernel:
+            # the append may request them before waiting for the previous
+            # step's kernels (each step still reads them over the host link).
             c = self.caches[layer]
             ext.rope_append_page_gauge_batched(hq, hk, hv, cos, sin, positions, c.key_center,
                                                c.value_center, rq, c.exact_key, c.exact_value,
                                                c.key_codes, c.value_codes, c.key_scales,
-                                               c.value_scales, 0)
+                                               c.value_scales, 0, inputs_ready=True)
             self.step(layer, q=rq, out=hout)
 
         def timed(fn, n):

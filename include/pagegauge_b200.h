@@ -180,6 +180,11 @@ int32_t pg_rope_append_fp16_batched(const void* query, const void* key,
                                     int64_t rope_row_stride, int64_t rope_rows,
                                     void* stream);
 
+/* inputs_ready != 0 declares that no kernel earlier in the stream writes
+ * query / key / value (e.g. rows the host wrote into page-locked memory
+ * before the call): the kernel then requests them before waiting for the
+ * previous kernel, so a trip over the host link overlaps that kernel's
+ * tail.  0 (the reference's behaviour): everything after the wait.        */
 int32_t pg_rope_append_page_gauge_batched(
     const void* query, const void* key, const void* value,
     const void* cosine, const void* sine, const void* key_center,
@@ -190,7 +195,7 @@ int32_t pg_rope_append_page_gauge_batched(
     int64_t center_batch_stride, int32_t batch, int32_t query_heads,
     int32_t kv_heads, int64_t exact_pages, int64_t code_pages,
     int64_t exact_sink_pages, const int32_t* positions,
-    int64_t rope_row_stride, int64_t rope_rows, void* stream);
+    int64_t rope_row_stride, int64_t rope_rows, int32_t inputs_ready, void* stream);
 
 /* The fused append on the served pool layout (the device side of the
  * serving decode metadata, experiments/mlsys2027/serving_v1/pagegauge_vllm/

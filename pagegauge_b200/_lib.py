@@ -89,7 +89,7 @@ _SIGNATURES = {
     "pg_rope_append_fp16_batched": (c_i32, [c_vp] * 8 + [c_i64] * 3 + [c_i32] * 3 + [c_i64, c_vp, c_i64, c_i64, c_vp]),
     "pg_rope_append_page_gauge_batched": (
         c_i32,
-        [c_vp] * 14 + [c_i64] * 4 + [c_i32] * 3 + [c_i64] * 3 + [c_vp, c_i64, c_i64, c_vp],
+        [c_vp] * 14 + [c_i64] * 4 + [c_i32] * 3 + [c_i64] * 3 + [c_vp, c_i64, c_i64, c_i32, c_vp],
     ),
     "pg_rope_append_page_gauge_served": (
         c_i32, [c_vp] * 15 + [c_i64] * 3 + [c_i32] * 3 + [c_i64] * 3 + [c_vp] * 4 + [c_i64, c_i64, c_vp],

@@ -57,6 +57,10 @@ struct AppendParams {
   int64_t exact_sink_pages;
   int64_t code_pages_per_request;
   int* error_flag;
+  // Nonzero: q / k / v are not written by any kernel earlier in the stream
+  // (e.g. rows the host wrote before the launch), so the page-gauge append
+  // requests them before waiting for the previous kernel.
+  int32_t inputs_ready;
   // Served pool layout (the served kernel instantiation only): per batch
   // row the physical token slot in the code pool (page * 16 + token), the
   // token slot in the exact sidecar and the centre row (the request's
@@ -309,9 +313,11 @@ __global__ void __launch_bounds__(kAppendThreads)
   // decode was told to request its INT8 tiles only after this grid), and
   // the decode waits for this grid before reading q or the ring.  This grid
   // waits for its own predecessor (which produced q, k, v) before reading
-  // anything.
+  // anything, unless the caller declared q / k / v ready: then their loads
+  // (for host rows, a trip over the host link) overlap the predecessor's
+  // tail, and everything else still waits.
   pdl_launch_dependents();
-  pdl_wait_primary();
+  if (!p.inputs_ready) pdl_wait_primary();
   __shared__ __align__(16) uint32_t newest[kHeadDim / 2];
   const int per_request = 2 * p.hkv;
   const int r = blockIdx.x / per_request;
@@ -333,6 +339,7 @@ __global__ void __launch_bounds__(kAppendThreads)
     qx = ld_input(q32 + j);
     qpartner = ld_input(q32 + ((j + 32) & 63));
   }
+  if (p.inputs_ready) pdl_wait_primary();
   int64_t crow = r;
   if constexpr (SERVED) {
     crow = __ldg(p.center_rows + r);

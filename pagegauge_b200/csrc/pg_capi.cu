@@ -240,7 +240,7 @@ extern "C" {
 
 const char* pg_last_error(void) { return g_last_error.c_str(); }
 
-int32_t pg_abi_version(void) { return 108; }
+int32_t pg_abi_version(void) { return 109; }
 
 int64_t pg_tp_exchange_bytes(int32_t tiles_cap) {
   return tiles_cap > 0 ? pg::tp_exchange_bytes(tiles_cap) : -1;
@@ -432,7 +432,7 @@ static int32_t append_page_gauge_impl(
     int32_t kv_heads, int64_t exact_pages, int64_t code_pages,
     int64_t exact_sink_pages, int64_t position,
     const int32_t* device_position, int64_t position_stride,
-    int64_t rope_row_stride, int64_t rope_rows, void* stream) {
+    int64_t rope_row_stride, int64_t rope_rows, void* stream, int32_t inputs_ready = 0) {
   PG_REQUIRE(batch > 0, "Q/K/V batch sizes must match and be positive");
   PG_REQUIRE(query_heads > 0 && kv_heads > 0, "head counts must be positive");
   if (device_position == nullptr) {
@@ -498,6 +498,7 @@ static int32_t append_page_gauge_impl(
   p.exact_sink_pages = exact_sink_pages;
   p.code_pages_per_request = code_ppr;
   p.error_flag = device_error_ptr();
+  p.inputs_ready = inputs_ready != 0;
   return launch_pdl(pg::pg_rope_append_page_gauge_kernel<false>, dim3(batch * kv_heads * 2),
                     dim3(pg::kAppendThreads), 0, static_cast<cudaStream_t>(stream),
                     "rope_append_page_gauge launch", p);
@@ -624,14 +625,14 @@ int32_t pg_rope_append_page_gauge_batched(
     int64_t center_batch_stride, int32_t batch, int32_t query_heads,
     int32_t kv_heads, int64_t exact_pages, int64_t code_pages,
     int64_t exact_sink_pages, const int32_t* positions,
-    int64_t rope_row_stride, int64_t rope_rows, void* stream) {
+    int64_t rope_row_stride, int64_t rope_rows, int32_t inputs_ready, void* stream) {
   PG_REQUIRE(positions != nullptr, "per-request positions must be a device int32 [B] tensor");
   return append_page_gauge_impl(
       query, key, value, cosine, sine, key_center, value_center, rotated_query,
       exact_key_pages, exact_value_pages, key_codes, value_codes, key_scales, value_scales,
       query_batch_stride, key_batch_stride, value_batch_stride, center_batch_stride, batch,
       query_heads, kv_heads, exact_pages, code_pages, exact_sink_pages, 0, positions, 1,
-      rope_row_stride, rope_rows, stream);
+      rope_row_stride, rope_rows, stream, inputs_ready);
 }
 
 // -------------------------------------------------------------- tail merge

@@ -238,12 +238,16 @@ class AppendExtension:
     def rope_append_page_gauge_batched(self, query, key, value, cosine, sine, positions,
                                        key_center, value_center, rotated_query, exact_key_pages,
                                        exact_value_pages, key_codes, value_codes, key_scales,
-                                       value_scales, exact_sink_pages: int) -> None:
+                                       value_scales, exact_sink_pages: int,
+                                       inputs_ready: bool = False) -> None:
         """rope_append_page_gauge_dynamic with one position per request
         (``positions`` int32 [B] on the device): request r appends at
         positions[r] and closes its page when positions[r] % 16 == 15.
         ``query``/``key``/``value`` may be page-locked host tensors: the
-        kernel then reads them over the host link (no separate copy)."""
+        kernel then reads them over the host link (no separate copy).
+        ``inputs_ready=True`` declares that no kernel earlier in the stream
+        writes query/key/value (host rows written before the call): the
+        kernel requests them before waiting for the previous kernel."""
         host_in = not query.is_cuda
         if host_in:
             for name, t in (("query", query), ("key", key), ("value", value)):
@@ -271,7 +275,8 @@ class AppendExtension:
             key_scales.data_ptr(), value_scales.data_ptr(), query.stride(0), key.stride(0),
             value.stride(0), cstride, query.size(0), query.size(1), key.size(1),
             exact_key_pages.size(0), key_codes.size(0), int(exact_sink_pages),
-            positions.data_ptr(), cosine.stride(0), cosine.size(0), _stream(rotated_query))
+            positions.data_ptr(), cosine.stride(0), cosine.size(0), int(bool(inputs_ready)),
+            _stream(rotated_query))
 
     def _gauge_call(self, query, key, value, cosine, sine, key_center, value_center,
                     rotated_query, exact_k, exact_v, codes_k, codes_v, scales_k, scales_v,

@@ -48,7 +48,7 @@ def test_struct_sizes_match_header_layout(lib):
     assert tuple(sizes) == (ctypes.sizeof(_lib.PgDecodeArgs), ctypes.sizeof(_lib.PgGemmArgs),
                             ctypes.sizeof(_lib.PgSegment), ctypes.sizeof(_lib.PgPlanInfo),
                             ctypes.sizeof(_lib.PgDecodeItem))
-    assert lib.pg_abi_version() == 108
+    assert lib.pg_abi_version() == 109
 
 
 def test_planner_chunks_and_offsets(lib):

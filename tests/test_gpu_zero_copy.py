@@ -4,7 +4,9 @@ after the host rewrote the rows, must see the new rows every time (the
 kernel fetches them over the host link on every load, never a line an
 earlier launch left in the L2).  Each replay's outputs (the rotated query
 and the token written into the exact ring) must equal those of an eager
-call on device copies of the same rows."""
+call on device copies of the same rows, with the loads after the
+dependency wait (the default) or before it (``inputs_ready``, rows no
+kernel writes)."""
 
 from __future__ import annotations
 
@@ -14,7 +16,8 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
-def test_graph_replays_see_rewritten_host_rows(cuda_lib):
+@pytest.mark.parametrize("inputs_ready", [False, True])
+def test_graph_replays_see_rewritten_host_rows(cuda_lib, inputs_ready):
     from pagegauge_b200.cache import build_gauge_cache, rope_tables, synthetic_dense_cache
     from pagegauge_b200.runtime import load_append_extension, read_device_error
 
@@ -32,22 +35,23 @@ def test_graph_replays_see_rewritten_host_rows(cuda_lib):
     rq = torch.empty(B, hq, 128, dtype=torch.float16, device="cuda")
     rq_ref = torch.empty_like(rq)
 
-    def append(q, k, v, out):
+    def append(q, k, v, out, ready=False):
         ext.rope_append_page_gauge_batched(q, k, v, cos, sin, positions, cache.key_center,
                                            cache.value_center, out, cache.exact_key,
                                            cache.exact_value, cache.key_codes, cache.value_codes,
-                                           cache.key_scales, cache.value_scales, 0)
+                                           cache.key_scales, cache.value_scales, 0,
+                                           inputs_ready=ready)
 
     g = torch.Generator().manual_seed(7)
     for t in (hq_rows, hk_rows, hv_rows):
         t.copy_(torch.randn(t.shape, generator=g).half())
     stream = torch.cuda.Stream()
     with torch.cuda.stream(stream):
-        append(hq_rows, hk_rows, hv_rows, rq)  # warm-up outside capture
+        append(hq_rows, hk_rows, hv_rows, rq, inputs_ready)  # warm-up outside capture
         torch.cuda.synchronize()
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=stream):
-            append(hq_rows, hk_rows, hv_rows, rq)
+            append(hq_rows, hk_rows, hv_rows, rq, inputs_ready)
     torch.cuda.synchronize()
     ring_pages = [(n - 1) // 16 % 16 for n in lengths]
     for it in range(4):
