@@ -46,11 +46,13 @@ constexpr int kGemmMaxXR = 32;     // activation rows of the widest instantiatio
 
 // Exchange buffer of one rank (identical layout on every rank):
 //   seq  [cap] int32   exchanges of each output tile completed on this rank
-//   recv [2][kGemmMaxTp][cap][64 * kGemmMaxXR] (value, tag) pairs: the
-//        tiles by source rank, double-buffered by exchange parity; every
-//        FP32 value travels with the exchange count as its tag in one
-//        8-byte store, so a reader knows a value has arrived from the value
-//        itself (no separate flag, no fence).
+//   recv [2][kGemmMaxTp][cap][64 * kGemmMaxXR] 8-byte (value, tag) words:
+//        the tiles by source rank, double-buffered by exchange parity; each
+//        word carries one FP32 value (a publishing GEMM: row b, column j at
+//        b * 64 + j) or one FP16 pair (pg_tp_publish: columns j, j + 1 at
+//        b * 64 + j / 2) with the exchange count as its tag in one store, so
+//        a reader knows a value has arrived from the word itself (no
+//        separate flag, no fence).
 __host__ __device__ constexpr int64_t tp_seq_offset(int) { return 0; }
 __host__ __device__ constexpr int64_t tp_recv_offset(int cap) {
   return (static_cast<int64_t>(cap) * 4 + 255) / 256 * 256;
